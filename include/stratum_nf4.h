@@ -1,0 +1,103 @@
+/*
+ * stratum_nf4.h -- C ABI of libstratum_nf4.so, the B200 (sm_100a) kernels behind
+ * Stratum's NF4 frozen-weight path.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, element counts and a cudaStream_t (passed
+ *     as void*; NULL means the legacy default stream);
+ *   - enqueues work on that stream and returns without synchronising;
+ *   - allocates no device memory (callers pass outputs and workspaces);
+ *   - returns STRATUM_OK (0) or a nonzero status; stratum_last_error() then
+ *     holds a message for the calling thread.
+ *
+ * Layouts follow bitsandbytes' NF4 format, which the reference stores in its
+ * NF4Payload (stratum/upload.py:70-95):
+ *   packed  : uint8[ceil(n/2)], element 2i in the high nibble of byte i;
+ *   absmax  : float32[ceil(n/blocksize)], one per block of the flattened tensor;
+ *   code16  : float32[16], the NF4 levels (NF4Payload.code).
+ * Double quantization (compress_statistics=True) replaces absmax by
+ *   absmax_q: uint8[nb], absmax2: float32[ceil(nb/blocksize2)],
+ *   code2: float32[256] (signed dynamic code), offset: float32[1] (device),
+ * with absmax[b] = fp32(fp32(code2[absmax_q[b]] * absmax2[b/blocksize2]) + offset).
+ */
+#ifndef STRATUM_NF4_H
+#define STRATUM_NF4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum stratum_status {
+    STRATUM_OK = 0,
+    STRATUM_ERR_INVALID = 1,     /* bad argument: null pointer, size, alignment */
+    STRATUM_ERR_UNSUPPORTED = 2, /* valid but not implemented (dtype, blocksize, shape) */
+    STRATUM_ERR_CUDA = 3,        /* a CUDA runtime call or kernel launch failed */
+    STRATUM_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up */
+    STRATUM_ERR_NCCL = 5         /* an NCCL call failed */
+};
+
+enum stratum_dtype { STRATUM_F32 = 0, STRATUM_F16 = 1, STRATUM_BF16 = 2 };
+
+/* ABI version; bumped on any signature change. */
+int stratum_abi_version(void);
+
+/* Message for the last nonzero status returned on the calling thread. */
+const char *stratum_last_error(void);
+
+/* Number of this library's kernel launches issued so far by this process
+ * (all threads).  Used by benchmarks to count launches in a timed region. */
+uint64_t stratum_launch_count(void);
+
+/* ---------------------------------------------------------------- codec -- */
+
+/* K1: blockwise NF4 quantization.
+ * Replaces bitsandbytes.functional.quantize_4bit(A, blocksize=64,
+ * compress_statistics=False, quant_type="nf4") called at
+ * stratum/upload.py:367-369 and :725-727.
+ *   src        : n elements of src_dtype (F32/F16/BF16), contiguous
+ *   thresholds : device float32[15], sorted decision thresholds between the 16
+ *                levels (q = number of thresholds strictly below x * (1/absmax))
+ *   blocksize  : 32, 64, 128 or 256
+ *   packed     : out uint8[ceil(n/2)]      absmax : out float32[ceil(n/blocksize)] */
+int stratum_nf4_quantize(const void *src, int src_dtype, int64_t n, int blocksize,
+                         const float *thresholds, uint8_t *packed, float *absmax,
+                         void *stream);
+
+/* Workspace bytes stratum_nf4_quantize_absmax_dq needs for nb blocks. */
+size_t stratum_nf4_dq_workspace_bytes(int64_t nb);
+
+/* Double quantization of a float32 absmax vector (the compress_statistics=True
+ * branch of bitsandbytes' quantize_4bit; the reference always passes False at
+ * stratum/upload.py:368, so this is an extension it can opt into).
+ *   thresholds2 : device float32[255], midpoints of the sorted 256-entry code2
+ *   blocksize2  : 256
+ *   absmax_q : out uint8[nb]   absmax2 : out float32[ceil(nb/256)]
+ *   offset   : out float32[1] (device) = deterministic mean of absmax
+ *   workspace: >= stratum_nf4_dq_workspace_bytes(nb) bytes of device memory */
+int stratum_nf4_quantize_absmax_dq(const float *absmax, int64_t nb, int blocksize2,
+                                   const float *thresholds2, uint8_t *absmax_q,
+                                   float *absmax2, float *offset, void *workspace,
+                                   size_t workspace_bytes, void *stream);
+
+/* K2: blockwise NF4 dequantization to F16/BF16/F32.
+ * Replaces bitsandbytes.functional.dequantize_4bit(q, QuantState(...)) called at
+ * stratum/upload.py:221, :946, :1038 and stratum/nf4_linear.py:44-46.
+ *   out[i] = out_dtype(fp32(code16[q_i] * absmax[i / blocksize]))
+ *   blocksize: power of two, 32..4096 */
+int stratum_nf4_dequantize(const uint8_t *packed, const float *absmax, const float *code16,
+                           int64_t n, int blocksize, void *out, int out_dtype, void *stream);
+
+/* K2 with a double-quantized absmax (see the layout note at the top). */
+int stratum_nf4_dequantize_dq(const uint8_t *packed, const uint8_t *absmax_q,
+                              const float *absmax2, const float *code2, const float *offset,
+                              int blocksize2, const float *code16, int64_t n, int blocksize,
+                              void *out, int out_dtype, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STRATUM_NF4_H */

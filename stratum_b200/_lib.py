@@ -1,0 +1,109 @@
+"""ctypes binding of libstratum_nf4.so (the C ABI in include/stratum_nf4.h).
+
+There is no CPU fallback: every product entry point goes through this library,
+and a missing library or a missing CUDA device raises instead of degrading.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libstratum_nf4.so"
+
+STRATUM_OK = 0
+STRATUM_ERR_INVALID = 1
+STRATUM_ERR_UNSUPPORTED = 2
+STRATUM_ERR_CUDA = 3
+STRATUM_ERR_TIMEOUT = 4
+STRATUM_ERR_NCCL = 5
+
+DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_f32 = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); must match include/stratum_nf4.h
+SIGNATURES: dict[str, tuple] = {
+    "stratum_abi_version": (_int, []),
+    "stratum_last_error": (ctypes.c_char_p, []),
+    "stratum_launch_count": (ctypes.c_uint64, []),
+    "stratum_nf4_quantize": (_int, [_vp, _int, _i64, _int, _vp, _vp, _vp, _vp]),
+    "stratum_nf4_dq_workspace_bytes": (_sz, [_i64]),
+    "stratum_nf4_quantize_absmax_dq": (_int, [_vp, _i64, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "stratum_nf4_dequantize": (_int, [_vp, _vp, _vp, _i64, _int, _vp, _int, _vp]),
+    "stratum_nf4_dequantize_dq": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _int, _vp, _int, _vp]),
+}
+
+ABI_VERSION = 1
+
+_lib = None
+_lock = threading.Lock()
+
+
+class StratumError(RuntimeError):
+    """A CUDA, NCCL or timeout failure reported by the native library."""
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        from . import _build
+
+        try:
+            _build.build()
+        except Exception as exc:  # no nvcc: fail loudly, never fall back
+            raise RuntimeError(
+                f"{LIB_PATH.name} is not built and could not be built ({exc}); "
+                "run `python -m stratum_b200._build` on a machine with nvcc"
+            ) from exc
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    ver = lib.stratum_abi_version()
+    if ver != ABI_VERSION:
+        raise RuntimeError(f"{LIB_PATH.name} ABI version {ver} != expected {ABI_VERSION}; rebuild it")
+    return lib
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                _lib = _load()
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc == STRATUM_OK:
+        return
+    msg = lib().stratum_last_error().decode(errors="replace")
+    if rc in (STRATUM_ERR_INVALID, STRATUM_ERR_UNSUPPORTED):
+        raise ValueError(f"{what}: {msg}")
+    raise StratumError(f"{what}: {msg} (status {rc})")
+
+
+def ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def stream_of(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda(t: torch.Tensor, what: str) -> None:
+    if t.device.type != "cuda":
+        raise RuntimeError(f"{what}: tensor on {t.device}; the NF4 kernels run on CUDA only (no CPU fallback)")
+
+
+def launch_count() -> int:
+    return int(lib().stratum_launch_count())

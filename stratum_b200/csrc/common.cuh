@@ -1,0 +1,70 @@
+// Shared helpers for the libstratum_nf4 C ABI: status/error reporting,
+// launch accounting and small device utilities.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+#include <atomic>
+
+#include "../../include/stratum_nf4.h"
+
+namespace stratum {
+
+// Per-thread message of the last failing call (read by stratum_last_error()).
+extern thread_local char g_last_error[512];
+extern std::atomic<uint64_t> g_launches;
+
+inline int fail(int status, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+// Checks the launch that was just enqueued; counts it on success.
+inline int check_launch(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(STRATUM_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return STRATUM_OK;
+}
+
+inline int sm_count() {
+    static int cached = 0;
+    if (cached == 0) {
+        int dev = 0, n = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached = n > 0 ? n : 148;
+    }
+    return cached;
+}
+
+inline bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
+inline int ilog2(int64_t v) { int l = 0; while ((int64_t(1) << l) < v) ++l; return l; }
+
+#define STRATUM_REQUIRE(cond, ...) \
+    do { if (!(cond)) return ::stratum::fail(STRATUM_ERR_INVALID, __VA_ARGS__); } while (0)
+
+// ----------------------------------------------------------------- device --
+
+__device__ __forceinline__ float load_as_f32(const float *p, int64_t i) { return p[i]; }
+__device__ __forceinline__ float load_as_f32(const __half *p, int64_t i) { return __half2float(p[i]); }
+__device__ __forceinline__ float load_as_f32(const __nv_bfloat16 *p, int64_t i) { return __bfloat162float(p[i]); }
+
+// Index of the level for a scaled value: number of thresholds strictly below x.
+// thr[0..14] sorted, thr[15] = +inf padding; NaN fails every test -> 0.
+__device__ __forceinline__ uint32_t nf4_code(float x, const float *thr, float t7) {
+    uint32_t i = (x > t7) ? 8u : 0u;
+    i += (x > thr[i + 3]) ? 4u : 0u;
+    i += (x > thr[i + 1]) ? 2u : 0u;
+    i += (x > thr[i]) ? 1u : 0u;
+    return i;
+}
+
+}  // namespace stratum
