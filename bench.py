@@ -62,57 +62,73 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and throttle reasons sampled every 5 ms (NVML, in a thread) during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, period_s: float = 0.005):
         self.gpu_index = gpu_index
-        self.proc = None
-        self.out = None
+        self.period = period_s
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._nvml = None
 
     def __enter__(self):
+        import threading
+
         try:
-            self.out = open(f"/tmp/stratum_clocks_{os.getpid()}.csv", "w+")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            # NVML enumerates all GPUs; map the CUDA index through the PCI address
+            h = None
+            try:
+                pr = torch.cuda.get_device_properties(self.gpu_index)
+                addr = f"{int(pr.pci_domain_id):08X}:{int(pr.pci_bus_id):02X}:{int(pr.pci_device_id):02X}.0"
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(addr.encode())
+            except Exception:
+                h = None
+            if h is None:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[self.gpu_index]) if vis and vis.split(",")[0].isdigit() else self.gpu_index
+                h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self._h = h
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            nv = self._nvml
+            while not self._stop.is_set():
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                    self.samples.append((mhz, rs))
+                except Exception:
+                    pass
+                self._stop.wait(self.period)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if self.proc is None or self.out is None:
+        if not self.samples:
             return None
-        self.out.seek(0)
-        rows = [r.split(",") for r in self.out.read().strip().splitlines() if r.strip()]
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            r = [c.strip() for c in r]
-            if len(r) < 9:
-                continue
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, r[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        mhz = [m for m, _ in self.samples]
+        reasons = sorted({name for _, rs in self.samples for name, bit in self.REASONS.items() if rs & bit})
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(mhz), "source": "nvml"}
 
 
 def dist_setup(args):
@@ -179,24 +195,19 @@ class CodecWorkload:
         self.quant_bytes = sum(it["n"] * Q_BYTES_PER_ELEM[False] for it in self.items)
 
     def dequant_step(self, events=None):
-        """All dequant launches of one step; per-kernel event pairs when ``events`` is a list."""
+        """All dequant launches of one step.  ``events``: list collecting (kind, n, e0, e1) external-event
+        pairs around every launch (recorded as graph nodes when captured)."""
         F = self.F
         for it in self.items:
-            if events is not None:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e0.record()
-            F.dequantize_4bit(it["packed"], it["st"], out=it["out"], out_dtype=torch.bfloat16)
-            if events is not None:
-                e1 = torch.cuda.Event(enable_timing=True)
-                e1.record()
-                events.append(("plain", it["n"], e0, e1))
-                e0 = torch.cuda.Event(enable_timing=True)
-                e0.record()
-            F.dequantize_4bit(it["packed_dq"], it["st_dq"], out=it["out"], out_dtype=torch.bfloat16)
-            if events is not None:
-                e1 = torch.cuda.Event(enable_timing=True)
-                e1.record()
-                events.append(("dq", it["n"], e0, e1))
+            for kind, packed, st in (("plain", it["packed"], it["st"]), ("dq", it["packed_dq"], it["st_dq"])):
+                if events is not None:
+                    e0 = torch.cuda.Event(enable_timing=True, external=True)
+                    e1 = torch.cuda.Event(enable_timing=True, external=True)
+                    e0.record()
+                F.dequantize_4bit(packed, st, out=it["out"], out_dtype=torch.bfloat16)
+                if events is not None:
+                    e1.record()
+                    events.append((kind, it["n"], e0, e1))
 
     def quant_step(self):
         from stratum_b200 import _lib, codebook
@@ -209,77 +220,98 @@ class CodecWorkload:
                                               _lib.ptr(it["qabsmax"]), st), "quantize")
 
 
-def run_codec(args, world, rank, local):
+def capture(fn):
+    """Capture ``fn()`` into a CUDA graph (after one eager warm-up call); returns (graph, result, launches)."""
     from stratum_b200 import _lib
 
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    n0 = _lib.launch_count()
+    with torch.cuda.graph(g):
+        res = fn()
+    return g, res, _lib.launch_count() - n0
+
+
+def run_codec(args, world, rank, local):
     dev = torch.device("cuda", torch.cuda.current_device())
     wl = CodecWorkload(dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
 
+    # one step = one replay of a CUDA graph holding the step's launches (the
+    # kernels are a few microseconds each; eager Python dispatch would starve the GPU)
+    ev = []
+    g_dq, _, dq_launches = capture(lambda: (ev.clear(), wl.dequant_step(ev)))
+    g_q, _, q_launches = capture(wl.quant_step)
+
     for _ in range(args.warmup):
-        wl.dequant_step()
-        wl.quant_step()
+        g_dq.replay()
+        g_q.replay()
     torch.cuda.synchronize()
 
-    # --- timed region: K dequant steps (value) -------------------------------
-    step_ms, kern = [], []
+    step_ms, plain = [], []
     barrier(world)
     torch.cuda.synchronize()
-    launches0 = _lib.launch_count()
     t_wall = time.perf_counter()
     with ClockSampler(dev.index) as clocks:
         for _ in range(args.steps):
             flush.fill_(1)  # L2 flush between timed steps (outside the event brackets)
-            ev = []
-            wl.dequant_step(ev)
-            kern.append(ev)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g_dq.replay()
+            e1.record()
+            e1.synchronize()
+            step_ms.append(e0.elapsed_time(e1))
+            plain += [(n, a.elapsed_time(b)) for kind, n, a, b in ev if kind == "plain"]
         torch.cuda.synchronize()
         t_wall = time.perf_counter() - t_wall
-        launches = _lib.launch_count() - launches0
         barrier(world)
-        for ev in kern:
-            step_ms.append(sum(e0.elapsed_time(e1) for _, _, e0, e1 in ev))
-        # quantize, timed the same way
         q_ms = []
         for _ in range(args.steps):
             flush.fill_(1)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            wl.quant_step()
+            g_q.replay()
             e1.record()
-            q_ms.append((e0, e1))
-        torch.cuda.synchronize()
-    q_ms = [a.elapsed_time(b) for a, b in q_ms]
+            e1.synchronize()
+            q_ms.append(e0.elapsed_time(e1))
     ms = max_over_ranks(statistics.mean(step_ms), world)
     qms = max_over_ranks(statistics.mean(q_ms), world)
     value = wl.dequant_bytes * world / (ms * 1e-3) / 1e9
     qvalue = wl.quant_bytes * world / (qms * 1e-3) / 1e9
 
-    # dominant kernel: plain dequant to bf16 (k_dequant<bf16,false>)
-    plain = [(n, e0.elapsed_time(e1)) for ev in kern for kind, n, e0, e1 in ev if kind == "plain"]
+    # dominant kernel: plain dequant to bf16 (k_dequant_seg<bf16, plain absmax>)
     plain_bytes = sum(n * DQ_BYTES_PER_ELEM[False] for n, _ in plain)
     plain_ms = sum(t for _, t in plain)
     achieved = plain_bytes / (plain_ms * 1e-3) / 1e9
+    big = [(n, t) for n, t in plain if n == max(nn for nn, _ in plain)]
+    big_gbs = sum(n * DQ_BYTES_PER_ELEM[False] for n, _ in big) / (sum(t for _, t in big) * 1e-3) / 1e9
     peaks = load_peaks()
-    traffic_tab = load_traffic().get("k_dequant_bf16", {})
+    traffic_tab = load_traffic().get("k_dequant_seg_bf16", {})
     per_launch_elems = plain_bytes / DQ_BYTES_PER_ELEM[False] / len(plain)
     traffic = traffic_tab.get("bytes_per_elem")
     roofline = {
         "bound": "hbm",
-        "kernel": "k_dequant<bf16,plain>",
+        "kernel": "k_dequant_seg<bf16, plain absmax>",
         "achieved": round(achieved, 1),
         "peak": peaks["hbm_gbs"],
         "unit": "GB/s",
         "frac": round(achieved / peaks["hbm_gbs"], 4),
         "frac_of": peaks["source"],
         "frac_nominal_8000": round(achieved / NOMINAL_HBM_GBS, 4),
+        "largest_launch_GBps": round(big_gbs, 1),
         "algorithmic_bytes_per_launch": round(plain_bytes / len(plain)),
         "traffic": None if traffic is None else round(traffic * per_launch_elems),
         "traffic_source": traffic_tab.get("source"),
     }
 
-    e2e = run_codec_e2e(args, wl, world) if rank == 0 or world > 1 else None
+    e2e = run_codec_e2e(args, wl, world)
     cpu = run_cpu_baseline_codec() if (world == 1 and rank == 0 and not args.no_cpu_baseline) else None
     clk = clocks.summary()
     return {
@@ -296,14 +328,15 @@ def run_codec(args, world, rank, local):
         "dtype": "u8->bf16",
         "data": "synthetic: seeded fp16 ~N(0,0.02) with 0.1% x20 outliers, NF4 blocksize 64 (BASELINE config 2)",
         "config": {"workload": "codec: dequant of 2048^2, 4096^2, 14336x4096, 4096x14336 to bf16, plain and "
-                               "double-quant absmax", "elements_per_step": wl.n_total, "blocksize": 64,
-                   "parallelism": f"replicas x{world}", "l2": "256 MiB fill between timed steps (outside events)"},
+                               "double-quant absmax (one CUDA-graph replay per step)", "elements_per_step": wl.n_total,
+                   "blocksize": 64, "parallelism": f"replicas x{world}",
+                   "l2": "256 MiB fill between timed steps (outside events)"},
         "quantize": {"value": round(qvalue, 1), "unit": "GB/s", "ms_per_step": round(qms, 4),
                      "frac": round(qvalue / peaks["hbm_gbs"], 4)},
         "roofline": roofline,
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "gpu_launches": int(launches),
+        "gpu_launches": int(dq_launches) * args.steps,
         "wall_s_timed": round(t_wall, 4),
         "clocks": clk,
     }
@@ -448,7 +481,7 @@ def run_reference(args, world, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("codec",), default="codec")

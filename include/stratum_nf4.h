@@ -96,6 +96,35 @@ int stratum_nf4_dequantize_dq(const uint8_t *packed, const uint8_t *absmax_q,
                               int blocksize2, const float *code16, int64_t n, int blocksize,
                               void *out, int out_dtype, void *stream);
 
+/* -------------------------------------------------------------- GEMMs -- */
+
+/* Status word written by the GEMM kernels when a bounded device-side wait gives
+ * up (0 = ok).  Copies it to *out (host), synchronising `stream`; clears it
+ * when `reset` is nonzero. */
+int stratum_device_status(int *out, int reset, void *stream);
+
+/* K3+K4: fused NF4 linear forward with the LoRA update in the same accumulator.
+ * Replaces NF4Linear.forward (dequantize_4bit then F.linear,
+ * stratum/nf4_linear.py:43-47) and PEFT lora.Linear's
+ * y += scaling * lora_B(lora_A(x)) (scripts/train.py:568-573):
+ *   y[T,N] = x[T,K] . W[N,K]^T + bias[N] + lora_xa[T,r] . lora_b[N,r]^T
+ *   x        : T x K, x_dtype BF16 or F16, row-major, 16-byte aligned
+ *   W        : NF4, blocksize 64 along K (K % 64 == 0): packed uint8[N*K/2] and
+ *              either absmax float32[N*K/64] (absmax != NULL) or the
+ *              double-quant set (absmax == NULL; absmax_q, absmax2, code2, offset)
+ *   bias     : N values of bias_dtype, or NULL
+ *   lora_xa  : T x ceil(r/64)*64 in x_dtype = scaling * x . lora_A^T, zero-padded
+ *              columns (NULL when r == 0)
+ *   lora_b   : N x r in x_dtype (r even), NULL when r == 0
+ *   y        : T x N in x_dtype */
+int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K,
+                         const uint8_t *packed, const float *absmax,
+                         const uint8_t *absmax_q, const float *absmax2,
+                         const float *code2, const float *offset, const float *code16,
+                         int64_t N, const void *bias, int bias_dtype,
+                         const void *lora_xa, const void *lora_b, int r,
+                         void *y, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

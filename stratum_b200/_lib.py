@@ -40,6 +40,9 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_nf4_quantize_absmax_dq": (_int, [_vp, _i64, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "stratum_nf4_dequantize": (_int, [_vp, _vp, _vp, _i64, _int, _vp, _int, _vp]),
     "stratum_nf4_dequantize_dq": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _int, _vp, _int, _vp]),
+    "stratum_device_status": (_int, [ctypes.POINTER(ctypes.c_int), _int, _vp]),
+    "stratum_nf4_gemm_fwd": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _int, _vp,
+                                    _vp, _int, _vp, _vp]),
 }
 
 ABI_VERSION = 1
@@ -103,6 +106,21 @@ def stream_of(device: torch.device) -> ctypes.c_void_p:
 def require_cuda(t: torch.Tensor, what: str) -> None:
     if t.device.type != "cuda":
         raise RuntimeError(f"{what}: tensor on {t.device}; the NF4 kernels run on CUDA only (no CPU fallback)")
+
+
+def device_status(device=None, reset: bool = True) -> int:
+    """Status word of the GEMM kernels on ``device`` (0 = no bounded wait gave up)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    out = ctypes.c_int(0)
+    with torch.cuda.device(dev):
+        check(lib().stratum_device_status(ctypes.byref(out), int(reset), stream_of(dev)), "device_status")
+    return out.value
+
+
+def check_device_status(what: str, device=None) -> None:
+    st = device_status(device)
+    if st != 0:
+        raise StratumError(f"{what}: a device-side wait timed out (status 0x{st:x}); the kernel unwound")
 
 
 def launch_count() -> int:

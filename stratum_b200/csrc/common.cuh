@@ -45,6 +45,19 @@ inline int sm_count() {
     return cached;
 }
 
+// Resident CTAs of `kernel` on the whole GPU (SM count x occupancy), cached per kernel.
+template <auto Kernel>
+inline int64_t resident_grid(int threads, size_t smem = 0) {
+    static int64_t cached = 0;
+    if (cached == 0) {
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, Kernel, threads, smem) != cudaSuccess || per_sm < 1)
+            per_sm = 1;
+        cached = int64_t(per_sm) * sm_count();
+    }
+    return cached;
+}
+
 inline bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
 inline int ilog2(int64_t v) { int l = 0; while ((int64_t(1) << l) < v) ++l; return l; }
 

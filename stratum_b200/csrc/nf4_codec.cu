@@ -14,6 +14,9 @@
 // op that the CPU restatement performs is written with an explicit _rn
 // intrinsic so that the compiler cannot contract it into an FMA.
 #include "common.cuh"
+#include "nf4_decode.cuh"
+
+#include <type_traits>
 
 namespace stratum {
 
@@ -136,6 +139,67 @@ __global__ void __launch_bounds__(kThreads) k_dequant(DequantArgs a, OutT *__res
     }
 }
 
+// 16-bit outputs, blocksize >= 64: one thread per 64-element segment (32
+// packed bytes, one absmax), decoded in registers with the scaled 16-entry
+// table (nf4_decode.cuh): two 16-byte loads in, eight 16-byte stores out.
+template <bool BF16, bool DQ>
+__global__ void __launch_bounds__(kThreads) k_dequant_seg(DequantArgs a, uint4 *__restrict__ out) {
+    __shared__ float lv_s[16];
+    __shared__ float c2[DQ ? 256 : 1];
+    if (threadIdx.x < 16) lv_s[threadIdx.x] = a.code16[threadIdx.x];
+    if constexpr (DQ) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) c2[i] = a.code2[i];
+    }
+    const float offset = DQ ? *a.offset : 0.f;
+    __syncthreads();
+    float lv[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
+
+    const uint4 *pk = reinterpret_cast<const uint4 *>(a.packed);
+    const int64_t nseg = a.n >> 6;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    // two segments per iteration, all loads issued before any decode (more bytes in flight)
+    for (int64_t g0 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g0 < nseg; g0 += 2 * stride) {
+        uint4 p[4];
+        float am[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int64_t g = g0 + u * stride;
+            if (g < nseg) {
+                p[2 * u] = __ldcs(pk + 2 * g);
+                p[2 * u + 1] = __ldcs(pk + 2 * g + 1);
+                am[u] = block_absmax<DQ>(a, c2, offset, (g << 6) >> a.log2bs);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int64_t g = g0 + u * stride;
+            if (g >= nseg) break;
+            const Nf4Tables t = nf4_build_tables<BF16>(lv, am[u]);
+            const uint32_t w[8] = {p[2 * u].x, p[2 * u].y, p[2 * u].z, p[2 * u].w,
+                                   p[2 * u + 1].x, p[2 * u + 1].y, p[2 * u + 1].z, p[2 * u + 1].w};
+            uint4 *o = out + 8 * g;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                uint32_t r[4];
+                nf4_decode_word(t, w[i], r);
+                o[i] = make_uint4(r[0], r[1], r[2], r[3]);
+            }
+        }
+    }
+    // ragged tail: the last n % 64 elements
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+        OutT *o = reinterpret_cast<OutT *>(out);
+        for (int64_t e = nseg << 6; e < a.n; ++e) {
+            const uint8_t byte = a.packed[e >> 1];
+            const uint32_t q = (e & 1) ? (byte & 0xFu) : (byte >> 4);
+            Out8<OutT>::store1(o, e, __fmul_rn(lv_s[q], block_absmax<DQ>(a, c2, offset, e >> a.log2bs)));
+        }
+    }
+}
+
 // Fallback for buffers that are not 16-byte aligned: one element per thread.
 template <typename OutT, bool DQ>
 __global__ void __launch_bounds__(kThreads) k_dequant_unaligned(DequantArgs a, OutT *__restrict__ out) {
@@ -158,6 +222,23 @@ template <bool DQ>
 int launch_dequant(const DequantArgs &a, void *out, int out_dtype, cudaStream_t st) {
     const bool aligned = (reinterpret_cast<uintptr_t>(a.packed) % 4 == 0) &&
                          (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+    const bool seg_path = (reinterpret_cast<uintptr_t>(a.packed) % 16 == 0) &&
+                          (reinterpret_cast<uintptr_t>(out) % 16 == 0) && a.log2bs >= 6 &&
+                          (out_dtype == STRATUM_F16 || out_dtype == STRATUM_BF16);
+    if (seg_path) {
+        const int64_t nseg = a.n >> 6;
+        int64_t want = (nseg + 2 * kThreads - 1) / (2 * kThreads);
+        if (out_dtype == STRATUM_BF16) {
+            const int64_t cap = resident_grid<k_dequant_seg<true, DQ>>(kThreads);
+            const int grid = int(want < 1 ? 1 : (want > cap ? cap : want));
+            k_dequant_seg<true, DQ><<<grid, kThreads, 0, st>>>(a, reinterpret_cast<uint4 *>(out));
+        } else {
+            const int64_t cap = resident_grid<k_dequant_seg<false, DQ>>(kThreads);
+            const int grid = int(want < 1 ? 1 : (want > cap ? cap : want));
+            k_dequant_seg<false, DQ><<<grid, kThreads, 0, st>>>(a, reinterpret_cast<uint4 *>(out));
+        }
+        return check_launch(DQ ? "nf4_dequantize_dq" : "nf4_dequantize");
+    }
     const int64_t nwords = a.n >> 3;
     const int64_t ntiles = (nwords + 255) >> 8;
     const int warps_per_cta = kThreads / 32;

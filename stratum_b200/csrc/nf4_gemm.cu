@@ -1,0 +1,465 @@
+// Fused NF4 GEMM for B200 (sm_100a): dequant-in-mainloop, tcgen05 tensor
+// cores, TMEM accumulators, LoRA folded into the same accumulator.
+//
+// Forward (the reference's NF4Linear.forward + PEFT lora.Linear,
+// stratum/nf4_linear.py:43-47, scripts/train.py:568-573):
+//     y[T, N] = x[T, K] . W[N, K]^T + bias[N] + xa[T, r] . lora_B[N, r]^T
+// with W stored NF4 (packed nibbles + per-64 absmax, optionally double
+// quantized) and xa = scaling * x . lora_A^T computed beforehand.
+//
+// Layout of the work (swap-AB): the MMA computes D[n, t] = sum_k W[n, k] x[t, k]
+// for a 128 (weight rows, TMEM lanes) x 256 (tokens) tile, 64 K per stage.
+//   * the weight tile is the A operand and lives in TMEM: dequant warps turn
+//     TMA-staged packed bytes into bf16/fp16 pairs in registers and
+//     tcgen05.st them straight into TMEM, so the dequantized weight never
+//     touches shared memory (shared-memory bandwidth is the scarce resource
+//     once the tensor core runs at full rate);
+//   * the token tile is the B operand, TMA-staged into 128B-swizzled shared
+//     memory (K-major canonical layout);
+//   * LoRA is one more K-chunk per 64 of rank: A = lora_B rows (staged into
+//     TMEM by the same warps), B = the xa tile;
+//   * the fp32 accumulator (256 TMEM columns) is drained by an epilogue
+//     warpgroup that adds the bias, rounds and stores y.
+// Warp roles (384 threads): w0 TMA producer, w1 TMEM owner + MMA issuer,
+// w4-7 dequant (w%4 selects the TMEM lane quarter), w8-11 epilogue.
+// Every wait is bounded; a timeout records a status word and unwinds.
+#include "common.cuh"
+#include "nf4_decode.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace stratum {
+
+// Status word of the GEMM kernels (0 = ok), one per device.
+__device__ int g_gemm_status;
+
+namespace gemm {
+
+using namespace sm100;
+
+constexpr int BM = 128;       // weight rows per tile (TMEM lanes, MMA M)
+constexpr int BN = 256;       // tokens per tile (MMA N)
+constexpr int BK = 64;        // K per stage: one NF4 block per weight row
+constexpr int STAGES = 5;     // shared-memory ring: token tile + packed weight tile
+constexpr int ASTAGES = 4;    // TMEM ring of dequantized weight tiles
+constexpr int X_BYTES = BN * BK * 2;  // 32 KiB
+constexpr int W_BYTES = BM * BK / 2;  // 4 KiB
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_COL = 0;    // accumulator: columns [0, 256)
+constexpr int A_COL0 = 256;   // A ring: 32 columns (64 x 16-bit) per stage
+constexpr int NUM_THREADS = 384;
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (X_BYTES + W_BYTES) + 1024 /*barriers*/ + 1088 /*tables*/;
+
+struct FwdParams {
+    const float *absmax;      // [N, K/64] (plain)
+    const uint8_t *absmax_q;  // [N, K/64] (double quant)
+    const float *absmax2;     // [ceil(N*K/64 / 256)]
+    const float *code2;       // [256]
+    const float *offset;      // [1]
+    const float *code16;      // [16]
+    const void *bias;         // [N] or null
+    int bias_dtype;
+    const uint16_t *lora_b;   // [N, r] (bf16/fp16 bits) or null
+    int r;
+    int lora_chunks;
+    uint16_t *y;              // [T, N]
+    int64_t T, N, K;
+    int n_tiles, t_tiles;
+    int *status;
+};
+
+struct Smem {
+    uint8_t *x0;  // stage i token tile at x0 + i * X_BYTES (1024-byte aligned)
+    uint8_t *w0;  // stage i packed weight tile at w0 + i * W_BYTES
+    uint64_t *full, *xempty, *wempty, *afull, *aempty, *accfull, *accempty, *drain;
+    uint32_t *tmem_slot;
+    float *lv, *c2;
+};
+
+__device__ __forceinline__ Smem carve(uint8_t *raw) {
+    Smem s;
+    uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023);
+    uint8_t *p = reinterpret_cast<uint8_t *>(base);
+    s.x0 = p;
+    p += STAGES * X_BYTES;
+    s.w0 = p;
+    p += STAGES * W_BYTES;
+    uint64_t *b = reinterpret_cast<uint64_t *>(p);
+    s.full = b; b += STAGES;
+    s.xempty = b; b += STAGES;
+    s.wempty = b; b += STAGES;
+    s.afull = b; b += ASTAGES;
+    s.aempty = b; b += ASTAGES;
+    s.accfull = b; b += 1;
+    s.accempty = b; b += 1;
+    s.drain = b; b += 1;
+    s.tmem_slot = reinterpret_cast<uint32_t *>(b);
+    s.lv = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(b) + 64);
+    s.c2 = s.lv + 16;
+    return s;
+}
+
+__device__ __forceinline__ float load_bias(const void *bias, int dt, int64_t n) {
+    if (dt == STRATUM_F32) return static_cast<const float *>(bias)[n];
+    if (dt == STRATUM_BF16) return __bfloat162float(static_cast<const __nv_bfloat16 *>(bias)[n]);
+    return __half2float(static_cast<const __half *>(bias)[n]);
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint16_t to16(float v) {
+    if constexpr (BF16) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    else return __half_as_ushort(__float2half_rn(v));
+}
+
+template <bool BF16, bool DQ>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+               const __grid_constant__ CUtensorMap tm_xa, const FwdParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem sm = carve(smem_raw);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nkw = int(p.K / BK);
+    const int nk = nkw + p.lora_chunks;
+    const int ntiles = p.n_tiles * p.t_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&sm.full[i], 1);
+            mbar_init(&sm.xempty[i], 1);
+            mbar_init(&sm.wempty[i], 128);
+        }
+        for (int i = 0; i < ASTAGES; ++i) {
+            mbar_init(&sm.afull[i], 128);
+            mbar_init(&sm.aempty[i], 1);
+        }
+        mbar_init(sm.accfull, 1);
+        mbar_init(sm.accempty, 128);
+        mbar_init(sm.drain, 1);
+        fence_barrier_init();
+    }
+    if (threadIdx.x < 16) sm.lv[threadIdx.x] = p.code16[threadIdx.x];
+    if (DQ) {
+        for (int i = threadIdx.x; i < 256; i += NUM_THREADS) sm.c2[i] = p.code2[i];
+    }
+    if (warp == 1) tmem_alloc(sm.tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *sm.tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            prefetch_tensormap(&tm_x);
+            prefetch_tensormap(&tm_w);
+            if (p.lora_chunks) prefetch_tensormap(&tm_xa);
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                const int n0 = (tile % p.n_tiles) * BM;
+                const int t0 = (tile / p.n_tiles) * BN;
+                for (int ks = 0; ks < nk; ++ks, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait(&sm.xempty[s], ph ^ 1, p.status, kErrTimeoutProducer) ||
+                        !mbar_wait(&sm.wempty[s], ph ^ 1, p.status, kErrTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    if (ks < nkw) {
+                        mbar_arrive_expect_tx(&sm.full[s], X_BYTES + W_BYTES);
+                        tma_load_2d((sm.x0 + s * X_BYTES), &tm_x, ks * BK, t0, &sm.full[s]);
+                        tma_load_2d((sm.w0 + s * W_BYTES), &tm_w, ks * (BK / 2), n0, &sm.full[s]);
+                    } else {
+                        mbar_arrive_expect_tx(&sm.full[s], X_BYTES);
+                        tma_load_2d((sm.x0 + s * X_BYTES), &tm_xa, (ks - nkw) * BK, t0, &sm.full[s]);
+                    }
+                }
+            }
+            // drain: every copy issued lands before the CTA can exit
+            for (uint32_t j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+                mbar_wait(&sm.full[j % STAGES], (j / STAGES) & 1, p.status, kErrTimeoutTeardown);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(BF16, BM, BN);
+            uint32_t it = 0, tc = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tc) {
+                if (!mbar_wait(sm.accempty, (tc & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                tc_fence_after();
+                for (int ks = 0; ks < nk; ++ks, ++it) {
+                    const int s = it % STAGES;
+                    const int sa = it % ASTAGES;
+                    if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, p.status, kErrTimeoutMma) ||
+                        !mbar_wait(&sm.afull[sa], (it / ASTAGES) & 1, p.status, kErrTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t bdesc = smem_desc_k_sw128((sm.x0 + s * X_BYTES));
+                    const uint32_t a0 = tmem + A_COL0 + sa * 32;
+#pragma unroll
+                    for (int j = 0; j < BK / 16; ++j)
+                        mma_ts_f16(tmem + ACC_COL, a0 + j * 8, bdesc + uint64_t(j * 2), idesc, (ks | j) != 0);
+                    mma_commit(&sm.xempty[s]);
+                    mma_commit(&sm.aempty[sa]);
+                }
+                if (ok) mma_commit(sm.accfull);
+            }
+            // drain: all issued MMAs complete before TMEM is released
+            mma_commit(sm.drain);
+            mbar_wait(sm.drain, 0, p.status, kErrTimeoutTeardown);
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------------------------------------------- dequant warps
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const uint32_t lane_addr = uint32_t(q * 32) << 16;
+        float lv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) lv[i] = sm.lv[i];
+        const int64_t kb = p.K / BK;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+            const int64_t n = int64_t(tile % p.n_tiles) * BM + row;
+            const bool valid = n < p.N;
+            for (int ks = 0; ks < nk; ++ks, ++it) {
+                const int s = it % STAGES;
+                const int sa = it % ASTAGES;
+                // absmax of this row's block (issued before the barrier wait to overlap its latency)
+                float am = 0.f;
+                if (valid && ks < nkw) {
+                    const int64_t b = n * kb + ks;
+                    if constexpr (DQ) {
+                        am = __fadd_rn(__fmul_rn(sm.c2[__ldg(p.absmax_q + b)], __ldg(p.absmax2 + (b >> 8))), *p.offset);
+                    } else {
+                        am = __ldg(p.absmax + b);
+                    }
+                }
+                // warp-uniform outcome: the tcgen05.st below is a warp collective
+                if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[s], (it / STAGES) & 1, p.status, kErrTimeoutDequant))) {
+                    ok = false;
+                    break;
+                }
+                uint32_t vals[32];
+                if (ks < nkw) {
+                    const uint4 *src = reinterpret_cast<const uint4 *>((sm.w0 + s * W_BYTES) + row * 32);
+                    const uint4 p0 = src[0], p1 = src[1];
+                    mbar_arrive(&sm.wempty[s]);
+                    const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+                    const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
+                    nf4_decode_block(t, w, vals);
+                } else {
+                    mbar_arrive(&sm.wempty[s]);
+                    const int j0 = (ks - nkw) * BK;
+#pragma unroll
+                    for (int m = 0; m < 32; ++m) {
+                        const int j = j0 + 2 * m;
+                        vals[m] = (valid && j < p.r)
+                                      ? __ldg(reinterpret_cast<const uint32_t *>(p.lora_b + n * p.r + j))
+                                      : 0u;
+                    }
+                }
+                if (!__all_sync(0xffffffffu,
+                                mbar_wait(&sm.aempty[sa], ((it / ASTAGES) & 1) ^ 1, p.status, kErrTimeoutDequant))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                tmem_st_32x32b_x32(tmem + lane_addr + A_COL0 + sa * 32, vals);
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&sm.afull[sa]);
+            }
+        }
+    } else if (warp >= 8) {
+        // --------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const uint32_t lane_addr = uint32_t(q * 32) << 16;
+        uint32_t tc = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
+            if (!__all_sync(0xffffffffu, mbar_wait(sm.accfull, tc & 1, p.status, kErrTimeoutEpilogue))) break;
+            tc_fence_after();
+            const int64_t n = int64_t(tile % p.n_tiles) * BM + row;
+            const int64_t t0 = int64_t(tile / p.n_tiles) * BN;
+            const bool valid = n < p.N;
+            const float bias = (valid && p.bias) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem + lane_addr + ACC_COL + c * 32, v);
+                tmem_ld_wait();
+                if (valid) {
+                    uint16_t *yp = p.y + (t0 + c * 32) * p.N + n;
+                    const int64_t lim = p.T - (t0 + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (i < lim) yp[int64_t(i) * p.N] = to16<BF16>(__uint_as_float(v[i]) + bias);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(sm.accempty);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------- host --
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+int make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw, const char *what) {
+    auto enc = encode_fn();
+    if (!enc) return fail(STRATUM_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", what);
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(STRATUM_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, int(r));
+    return STRATUM_OK;
+}
+
+int *status_ptr() {
+    static int *ptrs[64] = {nullptr};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return nullptr;
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_gemm_status) != cudaSuccess) return nullptr;
+        ptrs[dev] = static_cast<int *>(p);
+    }
+    return ptrs[dev];
+}
+
+template <bool BF16, bool DQ>
+int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mxa, const FwdParams &p,
+               cudaStream_t st) {
+    auto kern = k_nf4_gemm_fwd<BF16, DQ>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+            return fail(STRATUM_ERR_CUDA, "nf4_gemm_fwd: cannot set %d bytes of shared memory", SMEM_BYTES);
+        attr_set[dev] = true;
+    }
+    const int ntiles = p.n_tiles * p.t_tiles;
+    const int grid = ntiles < sm_count() ? ntiles : sm_count();
+    kern<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(mx, mw, mxa, p);
+    return check_launch("nf4_gemm_fwd");
+}
+
+}  // namespace gemm
+}  // namespace stratum
+
+using namespace stratum;
+
+extern "C" {
+
+int stratum_device_status(int *out, int reset, void *stream) {
+    STRATUM_REQUIRE(out != nullptr, "device_status: null out");
+    int *dp = gemm::status_ptr();
+    if (!dp) return fail(STRATUM_ERR_CUDA, "device_status: cannot resolve the status word");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(out, dp, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(STRATUM_ERR_CUDA, "device_status: copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+    if (reset && *out != 0) {
+        if (cudaMemsetAsync(dp, 0, sizeof(int), st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+            return fail(STRATUM_ERR_CUDA, "device_status: reset failed");
+    }
+    return STRATUM_OK;
+}
+
+int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const uint8_t *packed, const float *absmax,
+                         const uint8_t *absmax_q, const float *absmax2, const float *code2, const float *offset,
+                         const float *code16, int64_t N, const void *bias, int bias_dtype, const void *lora_xa,
+                         const void *lora_b, int r, void *y, void *stream) {
+    STRATUM_REQUIRE(T >= 0 && N >= 0 && K >= 0, "nf4_gemm_fwd: negative size");
+    if (T == 0 || N == 0) return STRATUM_OK;
+    STRATUM_REQUIRE(x && packed && code16 && y, "nf4_gemm_fwd: null pointer");
+    if (x_dtype != STRATUM_BF16 && x_dtype != STRATUM_F16)
+        return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_fwd: x must be bf16 or fp16");
+    if (K % gemm::BK != 0 || K == 0)
+        return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_fwd: K=%lld must be a positive multiple of 64", (long long)K);
+    const bool dq = absmax == nullptr;
+    STRATUM_REQUIRE(!dq || (absmax_q && absmax2 && code2 && offset), "nf4_gemm_fwd: need absmax or the double-quant set");
+    STRATUM_REQUIRE(r >= 0 && r <= 256, "nf4_gemm_fwd: lora rank %d out of range", r);
+    STRATUM_REQUIRE(r == 0 || (lora_xa && lora_b && r % 2 == 0), "nf4_gemm_fwd: lora needs xa, B and an even rank");
+    STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(packed) % 16 == 0,
+                    "nf4_gemm_fwd: x and packed must be 16-byte aligned");
+    STRATUM_REQUIRE(T <= (int64_t(1) << 31) && N <= (int64_t(1) << 31), "nf4_gemm_fwd: size too large");
+    int *status = gemm::status_ptr();
+    if (!status) return fail(STRATUM_ERR_CUDA, "nf4_gemm_fwd: no status word");
+
+    const bool bf16 = x_dtype == STRATUM_BF16;
+    const CUtensorMapDataType xdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap mx, mw, mxa;
+    int rc = gemm::make_map_2d(&mx, xdt, x, uint64_t(K), uint64_t(T), uint64_t(K) * 2, gemm::BK, gemm::BN,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_fwd x");
+    if (rc) return rc;
+    rc = gemm::make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(K / 2), uint64_t(N), uint64_t(K / 2),
+                           gemm::BK / 2, gemm::BM, CU_TENSOR_MAP_SWIZZLE_NONE, "nf4_gemm_fwd packed");
+    if (rc) return rc;
+    const int lora_chunks = (r + gemm::BK - 1) / gemm::BK;
+    if (r > 0) {
+        STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(lora_xa) % 16 == 0, "nf4_gemm_fwd: xa must be 16-byte aligned");
+        rc = gemm::make_map_2d(&mxa, xdt, lora_xa, uint64_t(lora_chunks * gemm::BK), uint64_t(T),
+                               uint64_t(lora_chunks * gemm::BK) * 2, gemm::BK, gemm::BN, CU_TENSOR_MAP_SWIZZLE_128B,
+                               "nf4_gemm_fwd xa");
+        if (rc) return rc;
+    } else {
+        mxa = mx;
+    }
+    gemm::FwdParams p{};
+    p.absmax = absmax;
+    p.absmax_q = absmax_q;
+    p.absmax2 = absmax2;
+    p.code2 = code2;
+    p.offset = offset;
+    p.code16 = code16;
+    p.bias = bias;
+    p.bias_dtype = bias_dtype;
+    p.lora_b = static_cast<const uint16_t *>(lora_b);
+    p.r = r;
+    p.lora_chunks = lora_chunks;
+    p.y = static_cast<uint16_t *>(y);
+    p.T = T;
+    p.N = N;
+    p.K = K;
+    p.n_tiles = int((N + gemm::BM - 1) / gemm::BM);
+    p.t_tiles = int((T + gemm::BN - 1) / gemm::BN);
+    p.status = status;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (bf16) return dq ? gemm::launch_fwd<true, true>(mx, mw, mxa, p, st) : gemm::launch_fwd<true, false>(mx, mw, mxa, p, st);
+    return dq ? gemm::launch_fwd<false, true>(mx, mw, mxa, p, st) : gemm::launch_fwd<false, false>(mx, mw, mxa, p, st);
+}
+
+}  // extern "C"
