@@ -342,6 +342,133 @@ def run_codec(args, world, rank, local):
     }
 
 
+# ---------------------------------------------------------- linear workload --
+
+LINEAR_SHAPES = ((14336, 4096), (4096, 14336))  # [N, K]: up/gate-proj and down-proj of Llama-3-8B
+LINEAR_T = 8192
+LINEAR_RANK = 64
+LINEAR_ALPHA = 128
+
+
+class LinearWorkload:
+    """Fused NF4 linear forward (+ LoRA r=64) at the config-5 micro-benchmark shapes."""
+
+    def __init__(self, device, T=LINEAR_T):
+        from stratum_b200 import functional as F
+        from stratum_b200 import ops
+
+        self.F, self.ops, self.device, self.T = F, ops, device, T
+        g = torch.Generator(device=device).manual_seed(0)
+        self.items = []
+        for N, K in LINEAR_SHAPES:
+            w = (torch.randn(N, K, generator=g, device=device) * 0.02).to(torch.float16)
+            packed, qs = F.quantize_4bit(w)
+            x = torch.randn(T, K, generator=g, device=device).to(torch.bfloat16)
+            A = ((torch.rand(LINEAR_RANK, K, generator=g, device=device) * 2 - 1) / K**0.5).to(torch.bfloat16)
+            B = (torch.randn(N, LINEAR_RANK, generator=g, device=device) * 0.01).to(torch.bfloat16)
+            xa = ops.lora_down(x, A, LINEAR_ALPHA / LINEAR_RANK)
+            self.items.append(dict(N=N, K=K, packed=packed, qs=qs, x=x, A=A, B=B, xa=xa,
+                                   wbuf=torch.empty(N, K, dtype=torch.bfloat16, device=device)))
+        self.flops_main = sum(2.0 * T * it["N"] * it["K"] for it in self.items)
+        self.flops_lora = sum(2.0 * T * LINEAR_RANK * it["N"] for it in self.items)
+
+    def fused_step(self, events=None):
+        for it in self.items:
+            if events is not None:
+                e0 = torch.cuda.Event(enable_timing=True, external=True)
+                e1 = torch.cuda.Event(enable_timing=True, external=True)
+            # the LoRA down-projection (cuBLAS) runs inside the step; only the fused kernel is bracketed
+            xa = self.ops.lora_down(it["x"], it["A"], LINEAR_ALPHA / LINEAR_RANK)
+            if events is not None:
+                e0.record()
+            self.ops.nf4_gemm_fwd(it["x"], it["packed"], it["qs"], lora_A=it["A"], lora_B=it["B"],
+                                  scaling=LINEAR_ALPHA / LINEAR_RANK, xa=xa)
+            if events is not None:
+                e1.record()
+                events.append((it["N"], it["K"], e0, e1))
+
+    def unfused_step(self):
+        """Reference GPU path: dequantize to bf16, then cuBLAS (the reference's K2 + K3)."""
+        for it in self.items:
+            self.F.dequantize_4bit(it["packed"], it["qs"], out=it["wbuf"], out_dtype=torch.bfloat16)
+            torch.matmul(it["x"], it["wbuf"].t())
+
+
+def run_linear(args, world, rank, local):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    wl = LinearWorkload(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    ev = []
+    g_f, _, launches = capture(lambda: (ev.clear(), wl.fused_step(ev)))
+    g_u, _, _ = capture(wl.unfused_step)
+    for _ in range(args.warmup):
+        g_f.replay()
+        g_u.replay()
+    torch.cuda.synchronize()
+
+    def timed(graph, n):
+        out = []
+        for _ in range(n):
+            flush.fill_(1)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            e1.synchronize()
+            out.append(e0.elapsed_time(e1))
+        return out
+
+    barrier(world)
+    torch.cuda.synchronize()
+    kern = []
+    with ClockSampler(dev.index) as clocks:
+        step_ms = []
+        for _ in range(args.steps):
+            step_ms += timed(g_f, 1)
+            kern += [(n, k, a.elapsed_time(b)) for n, k, a, b in ev]
+        torch.cuda.synchronize()
+        barrier(world)
+        base_ms = timed(g_u, max(3, args.steps // 4))
+    ms = max_over_ranks(statistics.mean(step_ms), world)
+    flops = wl.flops_main + wl.flops_lora
+    value = flops * world / (ms * 1e-3) / 1e12
+    peaks = load_peaks()
+    # dominant kernel: the fused GEMM launches (both shapes)
+    kflops = sum(2.0 * LINEAR_T * n * k for n, k, _ in kern)
+    kms = sum(t for _, _, t in kern)
+    achieved = kflops / (kms * 1e-3) / 1e12
+    per_shape = {}
+    for N, K in LINEAR_SHAPES:
+        ts = [t for n, k, t in kern if n == N and k == K]
+        per_shape[f"{N}x{K}"] = round(2.0 * LINEAR_T * N * K / (statistics.mean(ts) * 1e-3) / 1e12, 1)
+    base = statistics.mean(base_ms)
+    return {
+        "metric": "nf4_linear_fwd_TFLOPs",
+        "value": round(value, 1),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 (NF4 weights)",
+        "data": "synthetic: W ~N(0,0.02) fp16 -> NF4 bs64, x ~N(0,1) bf16, LoRA r=64 alpha=128",
+        "config": {"workload": f"fused NF4 linear forward + LoRA, T={LINEAR_T}, weights 14336x4096 and 4096x14336",
+                   "parallelism": f"replicas x{world}", "l2": "256 MiB fill between timed steps"},
+        "roofline": {"bound": "tensor", "kernel": "k_nf4_gemm_fwd<bf16>", "achieved": round(achieved, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "frac_of": peaks["source"], "frac_nominal_2250": round(achieved / 2250.0, 4),
+                     "per_shape_TFLOPs": per_shape, "traffic": None},
+        "gpu_reference_path": {"what": "dequantize_4bit -> bf16 + cuBLAS matmul (no LoRA)",
+                               "TFLOPs": round(wl.flops_main / (base * 1e-3) / 1e12, 1), "ms_per_step": round(base, 4)},
+        "gpu_launches": int(launches) * args.steps,
+        "clocks": clocks.summary(),
+    }
+
+
 def run_codec_e2e(args, wl, world):
     """Same metric through the reference-facing call with host buffers.
 
@@ -484,7 +611,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("codec",), default="codec")
+    ap.add_argument("--workload", choices=("codec", "linear"), default="codec")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -496,7 +623,7 @@ def main():
         else:
             if not torch.cuda.is_available():
                 raise SystemExit("bench.py: no CUDA device (the product path has no CPU fallback)")
-            out = run_codec(args, world, rank, local)
+            out = (run_linear if args.workload == "linear" else run_codec)(args, world, rank, local)
         if rank == 0 and out is not None:
             print(json.dumps(out), flush=True)
     finally:

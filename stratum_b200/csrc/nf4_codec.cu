@@ -141,11 +141,15 @@ __global__ void __launch_bounds__(kThreads) k_dequant(DequantArgs a, OutT *__res
 
 // 16-bit outputs, blocksize >= 64: one thread per 64-element segment (32
 // packed bytes, one absmax), decoded in registers with the scaled 16-entry
-// table (nf4_decode.cuh): two 16-byte loads in, eight 16-byte stores out.
+// table (nf4_decode.cuh).  Each warp owns 32 consecutive segments (4 KiB of
+// output): lanes write their decoded 128-byte rows into shared memory with a
+// 16-byte-chunk XOR swizzle (conflict-free), then the warp stores the 4 KiB as
+// eight fully coalesced 512-byte rows.
 template <bool BF16, bool DQ>
 __global__ void __launch_bounds__(kThreads) k_dequant_seg(DequantArgs a, uint4 *__restrict__ out) {
     __shared__ float lv_s[16];
     __shared__ float c2[DQ ? 256 : 1];
+    __shared__ uint4 stage[kThreads / 32][32 * 8];  // per warp: 32 rows x 8 chunks of 16 B
     if (threadIdx.x < 16) lv_s[threadIdx.x] = a.code16[threadIdx.x];
     if constexpr (DQ) {
         for (int i = threadIdx.x; i < 256; i += blockDim.x) c2[i] = a.code2[i];
@@ -156,37 +160,41 @@ __global__ void __launch_bounds__(kThreads) k_dequant_seg(DequantArgs a, uint4 *
 #pragma unroll
     for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
 
+    const int lane = threadIdx.x & 31;
+    uint4 *buf = stage[threadIdx.x >> 5];
     const uint4 *pk = reinterpret_cast<const uint4 *>(a.packed);
     const int64_t nseg = a.n >> 6;
-    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-    // two segments per iteration, all loads issued before any decode (more bytes in flight)
-    for (int64_t g0 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g0 < nseg; g0 += 2 * stride) {
-        uint4 p[4];
-        float am[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int64_t g = g0 + u * stride;
-            if (g < nseg) {
-                p[2 * u] = __ldcs(pk + 2 * g);
-                p[2 * u + 1] = __ldcs(pk + 2 * g + 1);
-                am[u] = block_absmax<DQ>(a, c2, offset, (g << 6) >> a.log2bs);
-            }
+    const int64_t nwarp_tiles = (nseg + 31) >> 5;
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t wt = warp; wt < nwarp_tiles; wt += nwarps) {
+        const int64_t g = (wt << 5) + lane;
+        const bool valid = g < nseg;
+        uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
+        float am = 0.f;
+        if (valid) {
+            p0 = __ldcs(pk + 2 * g);
+            p1 = __ldcs(pk + 2 * g + 1);
+            am = block_absmax<DQ>(a, c2, offset, (g << 6) >> a.log2bs);
         }
+        const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
+        const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int64_t g = g0 + u * stride;
-            if (g >= nseg) break;
-            const Nf4Tables t = nf4_build_tables<BF16>(lv, am[u]);
-            const uint32_t w[8] = {p[2 * u].x, p[2 * u].y, p[2 * u].z, p[2 * u].w,
-                                   p[2 * u + 1].x, p[2 * u + 1].y, p[2 * u + 1].z, p[2 * u + 1].w};
-            uint4 *o = out + 8 * g;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                uint32_t r[4];
-                nf4_decode_word(t, w[i], r);
-                o[i] = make_uint4(r[0], r[1], r[2], r[3]);
-            }
+        for (int i = 0; i < 8; ++i) {
+            uint32_t r[4];
+            nf4_decode_word(t, w[i], r);
+            buf[lane * 8 + (i ^ (lane & 7))] = make_uint4(r[0], r[1], r[2], r[3]);
         }
+        __syncwarp();
+        // chunk c of the warp's 4 KiB = chunk (c & 7) of row (c >> 3)
+        const int64_t rows_valid = nseg - (wt << 5);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int c = k * 32 + lane;
+            const int row = c >> 3;
+            if (row < rows_valid) out[(wt << 8) + c] = buf[row * 8 + ((c & 7) ^ (row & 7))];
+        }
+        __syncwarp();
     }
     // ragged tail: the last n % 64 elements
     if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -227,7 +235,7 @@ int launch_dequant(const DequantArgs &a, void *out, int out_dtype, cudaStream_t 
                           (out_dtype == STRATUM_F16 || out_dtype == STRATUM_BF16);
     if (seg_path) {
         const int64_t nseg = a.n >> 6;
-        int64_t want = (nseg + 2 * kThreads - 1) / (2 * kThreads);
+        int64_t want = (nseg + kThreads - 1) / kThreads;
         if (out_dtype == STRATUM_BF16) {
             const int64_t cap = resident_grid<k_dequant_seg<true, DQ>>(kThreads);
             const int grid = int(want < 1 ? 1 : (want > cap ? cap : want));
