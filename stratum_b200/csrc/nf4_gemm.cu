@@ -20,8 +20,9 @@
 //     TMEM by the same warps), B = the xa tile;
 //   * the fp32 accumulator (256 TMEM columns) is drained by an epilogue
 //     warpgroup that adds the bias, rounds and stores y.
-// Warp roles (384 threads): w0 TMA producer, w1 TMEM owner + MMA issuer,
-// w4-7 dequant (w%4 selects the TMEM lane quarter), w8-11 epilogue.
+// Warp roles (512 threads): w0 TMA producer, w1 TMEM owner + MMA issuer,
+// w4-7 and w8-11 dequant (two warpgroups taking alternate K-steps; w%4
+// selects the TMEM lane quarter), w12-15 epilogue.
 // Every wait is bounded; a timeout records a status word and unwinds.
 #include "common.cuh"
 #include "nf4_decode.cuh"
@@ -48,7 +49,8 @@ constexpr int W_BYTES = BM * BK / 2;  // 4 KiB
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;    // accumulator: columns [0, 256)
 constexpr int A_COL0 = 256;   // A ring: 32 columns (64 x 16-bit) per stage
-constexpr int NUM_THREADS = 384;
+constexpr int NUM_THREADS = 512;
+constexpr int DQ_GROUPS = 2;  // dequant warpgroups, alternating K-steps
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (X_BYTES + W_BYTES) + 1024 /*barriers*/ + 1088 /*tables*/;
 
 struct FwdParams {
@@ -128,7 +130,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&sm.full[i], 1);
             mbar_init(&sm.xempty[i], 1);
-            mbar_init(&sm.wempty[i], 128);
+            mbar_init(&sm.wempty[i], 128);  // the one dequant warpgroup that owns the step
         }
         for (int i = 0; i < ASTAGES; ++i) {
             mbar_init(&sm.afull[i], 128);
@@ -214,8 +216,9 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             mma_commit(sm.drain);
             mbar_wait(sm.drain, 0, p.status, kErrTimeoutTeardown);
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 4 && warp < 4 + 4 * DQ_GROUPS) {
         // ---------------------------------------------------- dequant warps
+        const int grp = (warp - 4) >> 2;  // owns the K-steps with it % DQ_GROUPS == grp
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
@@ -223,61 +226,71 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 #pragma unroll
         for (int i = 0; i < 16; ++i) lv[i] = sm.lv[i];
         const int64_t kb = p.K / BK;
-        uint32_t it = 0;
+        // absmax of this row's block for step (tile, ks); zero for padding rows and LoRA steps
+        auto absmax_of = [&](int tile, int ks) -> float {
+            const int64_t n = int64_t(tile % p.n_tiles) * BM + row;
+            if (tile >= ntiles || n >= p.N || ks >= nkw) return 0.f;
+            const int64_t b = n * kb + ks;
+            if constexpr (DQ) {
+                return __fadd_rn(__fmul_rn(sm.c2[__ldg(p.absmax_q + b)], __ldg(p.absmax2 + (b >> 8))), *p.offset);
+            } else {
+                return __ldg(p.absmax + b);
+            }
+        };
+        // first owned step, and its absmax loaded one owned step ahead of use
+        int tile = blockIdx.x, ks = grp;
+        while (ks >= nk && tile < ntiles) { ks -= nk; tile += gridDim.x; }
+        uint32_t it = uint32_t(grp);
+        float am_next = absmax_of(tile, ks);
         bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        while (ok && tile < ntiles) {
+            const float am = am_next;
+            int ntile = tile, nks = ks + DQ_GROUPS;
+            while (nks >= nk && ntile < ntiles) { nks -= nk; ntile += gridDim.x; }
+            am_next = absmax_of(ntile, nks);
             const int64_t n = int64_t(tile % p.n_tiles) * BM + row;
             const bool valid = n < p.N;
-            for (int ks = 0; ks < nk; ++ks, ++it) {
-                const int s = it % STAGES;
-                const int sa = it % ASTAGES;
-                // absmax of this row's block (issued before the barrier wait to overlap its latency)
-                float am = 0.f;
-                if (valid && ks < nkw) {
-                    const int64_t b = n * kb + ks;
-                    if constexpr (DQ) {
-                        am = __fadd_rn(__fmul_rn(sm.c2[__ldg(p.absmax_q + b)], __ldg(p.absmax2 + (b >> 8))), *p.offset);
-                    } else {
-                        am = __ldg(p.absmax + b);
-                    }
-                }
-                // warp-uniform outcome: the tcgen05.st below is a warp collective
-                if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[s], (it / STAGES) & 1, p.status, kErrTimeoutDequant))) {
-                    ok = false;
-                    break;
-                }
-                uint32_t vals[32];
-                if (ks < nkw) {
-                    const uint4 *src = reinterpret_cast<const uint4 *>((sm.w0 + s * W_BYTES) + row * 32);
-                    const uint4 p0 = src[0], p1 = src[1];
-                    mbar_arrive(&sm.wempty[s]);
-                    const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-                    const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
-                    nf4_decode_block(t, w, vals);
-                } else {
-                    mbar_arrive(&sm.wempty[s]);
-                    const int j0 = (ks - nkw) * BK;
-#pragma unroll
-                    for (int m = 0; m < 32; ++m) {
-                        const int j = j0 + 2 * m;
-                        vals[m] = (valid && j < p.r)
-                                      ? __ldg(reinterpret_cast<const uint32_t *>(p.lora_b + n * p.r + j))
-                                      : 0u;
-                    }
-                }
-                if (!__all_sync(0xffffffffu,
-                                mbar_wait(&sm.aempty[sa], ((it / ASTAGES) & 1) ^ 1, p.status, kErrTimeoutDequant))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                tmem_st_32x32b_x32(tmem + lane_addr + A_COL0 + sa * 32, vals);
-                tmem_st_wait();
-                tc_fence_before();
-                mbar_arrive(&sm.afull[sa]);
+            const int s = it % STAGES;
+            const int sa = it % ASTAGES;
+            // warp-uniform outcome: the tcgen05.st below is a warp collective
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[s], (it / STAGES) & 1, p.status, kErrTimeoutDequant))) {
+                ok = false;
+                break;
             }
+            uint32_t vals[32];
+            if (ks < nkw) {
+                // 32-byte swizzled tile: row r's 16-byte halves are swapped when bit 2 of r is set
+                const uint4 *src = reinterpret_cast<const uint4 *>(sm.w0 + s * W_BYTES + row * 32);
+                const int sw = (row >> 2) & 1;
+                const uint4 p0 = src[sw], p1 = src[sw ^ 1];
+                mbar_arrive(&sm.wempty[s]);
+                const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+                const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
+                nf4_decode_block(t, w, vals);
+            } else {
+                mbar_arrive(&sm.wempty[s]);
+                const int j0 = (ks - nkw) * BK;
+#pragma unroll
+                for (int m = 0; m < 32; ++m) {
+                    const int j = j0 + 2 * m;
+                    vals[m] = (valid && j < p.r) ? __ldg(reinterpret_cast<const uint32_t *>(p.lora_b + n * p.r + j)) : 0u;
+                }
+            }
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(&sm.aempty[sa], ((it / ASTAGES) & 1) ^ 1, p.status, kErrTimeoutDequant))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            tmem_st_32x32b_x32(tmem + lane_addr + A_COL0 + sa * 32, vals);
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(&sm.afull[sa]);
+            tile = ntile;
+            ks = nks;
+            it += DQ_GROUPS;
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 4 + 4 * DQ_GROUPS) {
         // --------------------------------------------------------- epilogue
         const int q = warp & 3;
         const int row = q * 32 + lane;
@@ -425,8 +438,10 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
     int rc = gemm::make_map_2d(&mx, xdt, x, uint64_t(K), uint64_t(T), uint64_t(K) * 2, gemm::BK, gemm::BN,
                                CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_fwd x");
     if (rc) return rc;
+    // 32-byte swizzle: rows r and r+4 trade 16-byte halves, so the dequant
+    // warps' row-per-lane 16-byte reads are bank-conflict free
     rc = gemm::make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(K / 2), uint64_t(N), uint64_t(K / 2),
-                           gemm::BK / 2, gemm::BM, CU_TENSOR_MAP_SWIZZLE_NONE, "nf4_gemm_fwd packed");
+                           gemm::BK / 2, gemm::BM, CU_TENSOR_MAP_SWIZZLE_32B, "nf4_gemm_fwd packed");
     if (rc) return rc;
     const int lora_chunks = (r + gemm::BK - 1) / gemm::BK;
     if (r > 0) {
