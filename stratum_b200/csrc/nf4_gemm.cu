@@ -20,9 +20,10 @@
 //     TMEM by the same warps), B = the xa tile;
 //   * the fp32 accumulator (256 TMEM columns) is drained by an epilogue
 //     warpgroup that adds the bias, rounds and stores y.
-// Warp roles (512 threads): w0 TMA producer, w1 TMEM owner + MMA issuer,
-// w4-7 and w8-11 dequant (two warpgroups taking alternate K-steps; w%4
-// selects the TMEM lane quarter), w12-15 epilogue.
+// Warp roles (640 threads): w0 TMA producer of token tiles, w2 TMA producer
+// of packed weight tiles (its own deep ring, so weights stream ahead of the
+// MMA), w1 TMEM owner + MMA issuer, w4-15 dequant (three warpgroups taking
+// turns by K-step; w%4 selects the TMEM lane quarter), w16-19 epilogue.
 // Every wait is bounded; a timeout records a status word and unwinds.
 #include "common.cuh"
 #include "nf4_decode.cuh"
@@ -41,17 +42,23 @@ using namespace sm100;
 
 constexpr int BM = 128;       // weight rows per tile (TMEM lanes, MMA M)
 constexpr int BN = 256;       // tokens per tile (MMA N)
-constexpr int BK = 64;        // K per stage: one NF4 block per weight row
-constexpr int STAGES = 5;     // shared-memory ring: token tile + packed weight tile
-constexpr int ASTAGES = 4;    // TMEM ring of dequantized weight tiles
+constexpr int BK = 64;        // K per step: one NF4 block per weight row
+constexpr int XS = 4;         // ring of token tiles (32 KiB each), released by MMA completion
+constexpr int WS = 16;        // ring of packed weight tiles (4 KiB each), released by the dequant warps
+constexpr int AS = 8;         // TMEM ring of dequantized weight tiles (32 columns each)
+constexpr int DQG = 3;        // dequant warpgroups; group g owns the steps with it % DQG == g
 constexpr int X_BYTES = BN * BK * 2;  // 32 KiB
 constexpr int W_BYTES = BM * BK / 2;  // 4 KiB
+constexpr int EPI_STAGE_BYTES = 32 * 32 * 2;  // per epilogue warp: 32 tokens x 32 rows of 16-bit
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;    // accumulator: columns [0, 256)
-constexpr int A_COL0 = 256;   // A ring: 32 columns (64 x 16-bit) per stage
-constexpr int NUM_THREADS = 512;
-constexpr int DQ_GROUPS = 2;  // dequant warpgroups, alternating K-steps
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (X_BYTES + W_BYTES) + 1024 /*barriers*/ + 1088 /*tables*/;
+constexpr int A_COL0 = 256;   // A ring: columns [256, 512)
+constexpr int EPI_WARP0 = 4 + 4 * DQG;
+constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_BYTES + WS * W_BYTES + 4 * EPI_STAGE_BYTES +
+                           1024 /*barriers*/ + 1088 /*tables*/;
+static_assert(A_COL0 + AS * 32 <= TMEM_COLS, "TMEM budget");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 struct FwdParams {
     const float *absmax;      // [N, K/64] (plain)
@@ -68,13 +75,15 @@ struct FwdParams {
     uint16_t *y;              // [T, N]
     int64_t T, N, K;
     int n_tiles, t_tiles;
+    int vec_store;            // y 16-byte aligned and N % 8 == 0
     int *status;
 };
 
 struct Smem {
-    uint8_t *x0;  // stage i token tile at x0 + i * X_BYTES (1024-byte aligned)
-    uint8_t *w0;  // stage i packed weight tile at w0 + i * W_BYTES
-    uint64_t *full, *xempty, *wempty, *afull, *aempty, *accfull, *accempty, *drain;
+    uint8_t *x0;    // token tile i at x0 + i * X_BYTES (1024-byte aligned)
+    uint8_t *w0;    // packed weight tile i at w0 + i * W_BYTES
+    uint8_t *epi0;  // epilogue staging, EPI_STAGE_BYTES per epilogue warp
+    uint64_t *xfull, *xempty, *wfull, *wempty, *afull, *aempty, *accfull, *accempty, *drain;
     uint32_t *tmem_slot;
     float *lv, *c2;
 };
@@ -84,15 +93,18 @@ __device__ __forceinline__ Smem carve(uint8_t *raw) {
     uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023);
     uint8_t *p = reinterpret_cast<uint8_t *>(base);
     s.x0 = p;
-    p += STAGES * X_BYTES;
+    p += XS * X_BYTES;
     s.w0 = p;
-    p += STAGES * W_BYTES;
+    p += WS * W_BYTES;
+    s.epi0 = p;
+    p += 4 * EPI_STAGE_BYTES;
     uint64_t *b = reinterpret_cast<uint64_t *>(p);
-    s.full = b; b += STAGES;
-    s.xempty = b; b += STAGES;
-    s.wempty = b; b += STAGES;
-    s.afull = b; b += ASTAGES;
-    s.aempty = b; b += ASTAGES;
+    s.xfull = b; b += XS;
+    s.xempty = b; b += XS;
+    s.wfull = b; b += WS;
+    s.wempty = b; b += WS;
+    s.afull = b; b += AS;
+    s.aempty = b; b += AS;
     s.accfull = b; b += 1;
     s.accempty = b; b += 1;
     s.drain = b; b += 1;
@@ -125,14 +137,19 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     const int nkw = int(p.K / BK);
     const int nk = nkw + p.lora_chunks;
     const int ntiles = p.n_tiles * p.t_tiles;
+    // tiles of this CTA: blockIdx.x + tl * gridDim.x, tl = 0 .. my_tiles - 1
+    const int my_tiles = ntiles > int(blockIdx.x) ? (ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < STAGES; ++i) {
-            mbar_init(&sm.full[i], 1);
+        for (int i = 0; i < XS; ++i) {
+            mbar_init(&sm.xfull[i], 1);
             mbar_init(&sm.xempty[i], 1);
-            mbar_init(&sm.wempty[i], 128);  // the one dequant warpgroup that owns the step
         }
-        for (int i = 0; i < ASTAGES; ++i) {
+        for (int i = 0; i < WS; ++i) {
+            mbar_init(&sm.wfull[i], 1);
+            mbar_init(&sm.wempty[i], 128);  // the dequant warpgroup that owns the step
+        }
+        for (int i = 0; i < AS; ++i) {
             mbar_init(&sm.afull[i], 128);
             mbar_init(&sm.aempty[i], 1);
         }
@@ -152,57 +169,68 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     const uint32_t tmem = *sm.tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------------------------------ TMA producer
+        // ------------------------------------------- producer: token tiles
         if (lane == 0) {
             prefetch_tensormap(&tm_x);
-            prefetch_tensormap(&tm_w);
             if (p.lora_chunks) prefetch_tensormap(&tm_xa);
             uint32_t it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-                const int n0 = (tile % p.n_tiles) * BM;
-                const int t0 = (tile / p.n_tiles) * BN;
+            for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                const int t0 = ((int(blockIdx.x) + tl * int(gridDim.x)) / p.n_tiles) * BN;
                 for (int ks = 0; ks < nk; ++ks, ++it) {
-                    const int s = it % STAGES;
-                    const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(&sm.xempty[s], ph ^ 1, p.status, kErrTimeoutProducer) ||
-                        !mbar_wait(&sm.wempty[s], ph ^ 1, p.status, kErrTimeoutProducer)) {
+                    const int s = it % XS;
+                    if (!mbar_wait(&sm.xempty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
                         ok = false;
                         break;
                     }
-                    if (ks < nkw) {
-                        mbar_arrive_expect_tx(&sm.full[s], X_BYTES + W_BYTES);
-                        tma_load_2d((sm.x0 + s * X_BYTES), &tm_x, ks * BK, t0, &sm.full[s]);
-                        tma_load_2d((sm.w0 + s * W_BYTES), &tm_w, ks * (BK / 2), n0, &sm.full[s]);
-                    } else {
-                        mbar_arrive_expect_tx(&sm.full[s], X_BYTES);
-                        tma_load_2d((sm.x0 + s * X_BYTES), &tm_xa, (ks - nkw) * BK, t0, &sm.full[s]);
-                    }
+                    mbar_arrive_expect_tx(&sm.xfull[s], X_BYTES);
+                    if (ks < nkw) tma_load_2d(sm.x0 + s * X_BYTES, &tm_x, ks * BK, t0, &sm.xfull[s]);
+                    else tma_load_2d(sm.x0 + s * X_BYTES, &tm_xa, (ks - nkw) * BK, t0, &sm.xfull[s]);
                 }
             }
-            // drain: every copy issued lands before the CTA can exit
-            for (uint32_t j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
-                mbar_wait(&sm.full[j % STAGES], (j / STAGES) & 1, p.status, kErrTimeoutTeardown);
+            for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)  // every copy lands before exit
+                mbar_wait(&sm.xfull[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+        }
+    } else if (warp == 2) {
+        // ---------------------------------- producer: packed weight tiles
+        if (lane == 0) {
+            prefetch_tensormap(&tm_w);
+            uint32_t wt = 0;
+            bool ok = true;
+            for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                const int n0 = ((int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles) * BM;
+                for (int ks = 0; ks < nkw; ++ks, ++wt) {
+                    const int s = wt % WS;
+                    if (!mbar_wait(&sm.wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&sm.wfull[s], W_BYTES);
+                    tma_load_2d(sm.w0 + s * W_BYTES, &tm_w, ks * (BK / 2), n0, &sm.wfull[s]);
+                }
+            }
+            for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
+                mbar_wait(&sm.wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(BF16, BM, BN);
-            uint32_t it = 0, tc = 0;
+            uint32_t it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tc) {
-                if (!mbar_wait(sm.accempty, (tc & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+            for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                if (!mbar_wait(sm.accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
-                    const int s = it % STAGES;
-                    const int sa = it % ASTAGES;
-                    if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, p.status, kErrTimeoutMma) ||
-                        !mbar_wait(&sm.afull[sa], (it / ASTAGES) & 1, p.status, kErrTimeoutMma)) {
+                    const int s = it % XS;
+                    const int sa = it % AS;
+                    if (!mbar_wait(&sm.afull[sa], (it / AS) & 1, p.status, kErrTimeoutMma) ||
+                        !mbar_wait(&sm.xfull[s], (it / XS) & 1, p.status, kErrTimeoutMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bdesc = smem_desc_k_sw128((sm.x0 + s * X_BYTES));
+                    const uint64_t bdesc = smem_desc_k_sw128(sm.x0 + s * X_BYTES);
                     const uint32_t a0 = tmem + A_COL0 + sa * 32;
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j)
@@ -212,13 +240,12 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 }
                 if (ok) mma_commit(sm.accfull);
             }
-            // drain: all issued MMAs complete before TMEM is released
-            mma_commit(sm.drain);
+            mma_commit(sm.drain);  // all issued MMAs complete before TMEM is released
             mbar_wait(sm.drain, 0, p.status, kErrTimeoutTeardown);
         }
-    } else if (warp >= 4 && warp < 4 + 4 * DQ_GROUPS) {
+    } else if (warp >= 4 && warp < EPI_WARP0) {
         // ---------------------------------------------------- dequant warps
-        const int grp = (warp - 4) >> 2;  // owns the K-steps with it % DQ_GROUPS == grp
+        const int grp = (warp - 4) >> 2;
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
@@ -226,10 +253,11 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 #pragma unroll
         for (int i = 0; i < 16; ++i) lv[i] = sm.lv[i];
         const int64_t kb = p.K / BK;
-        // absmax of this row's block for step (tile, ks); zero for padding rows and LoRA steps
-        auto absmax_of = [&](int tile, int ks) -> float {
-            const int64_t n = int64_t(tile % p.n_tiles) * BM + row;
-            if (tile >= ntiles || n >= p.N || ks >= nkw) return 0.f;
+        auto absmax_of = [&](uint32_t it) -> float {
+            const int tl = int(it / nk), ks = int(it % nk);
+            if (tl >= my_tiles || ks >= nkw) return 0.f;
+            const int64_t n = int64_t((int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles) * BM + row;
+            if (n >= p.N) return 0.f;
             const int64_t b = n * kb + ks;
             if constexpr (DQ) {
                 return __fadd_rn(__fmul_rn(sm.c2[__ldg(p.absmax_q + b)], __ldg(p.absmax2 + (b >> 8))), *p.offset);
@@ -237,28 +265,20 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 return __ldg(p.absmax + b);
             }
         };
-        // first owned step, and its absmax loaded one owned step ahead of use
-        int tile = blockIdx.x, ks = grp;
-        while (ks >= nk && tile < ntiles) { ks -= nk; tile += gridDim.x; }
-        uint32_t it = uint32_t(grp);
-        float am_next = absmax_of(tile, ks);
-        bool ok = true;
-        while (ok && tile < ntiles) {
+        const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
+        float am_next = absmax_of(uint32_t(grp));
+        for (uint32_t it = uint32_t(grp); it < total; it += DQG) {
             const float am = am_next;
-            int ntile = tile, nks = ks + DQ_GROUPS;
-            while (nks >= nk && ntile < ntiles) { nks -= nk; ntile += gridDim.x; }
-            am_next = absmax_of(ntile, nks);
-            const int64_t n = int64_t(tile % p.n_tiles) * BM + row;
-            const bool valid = n < p.N;
-            const int s = it % STAGES;
-            const int sa = it % ASTAGES;
-            // warp-uniform outcome: the tcgen05.st below is a warp collective
-            if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[s], (it / STAGES) & 1, p.status, kErrTimeoutDequant))) {
-                ok = false;
-                break;
-            }
+            am_next = absmax_of(it + DQG);  // one owned step ahead
+            const int tl = int(it / nk), ks = int(it % nk);
+            const int64_t n = int64_t((int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles) * BM + row;
             uint32_t vals[32];
             if (ks < nkw) {
+                const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
+                const int s = wt % WS;
+                // warp-uniform outcome: the tcgen05.st below is a warp collective
+                if (!__all_sync(0xffffffffu, mbar_wait(&sm.wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant)))
+                    break;
                 // 32-byte swizzled tile: row r's 16-byte halves are swapped when bit 2 of r is set
                 const uint4 *src = reinterpret_cast<const uint4 *>(sm.w0 + s * W_BYTES + row * 32);
                 const int sw = (row >> 2) & 1;
@@ -268,56 +288,68 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
                 nf4_decode_block(t, w, vals);
             } else {
-                mbar_arrive(&sm.wempty[s]);
                 const int j0 = (ks - nkw) * BK;
+                const bool valid = n < p.N;
 #pragma unroll
                 for (int m = 0; m < 32; ++m) {
                     const int j = j0 + 2 * m;
                     vals[m] = (valid && j < p.r) ? __ldg(reinterpret_cast<const uint32_t *>(p.lora_b + n * p.r + j)) : 0u;
                 }
             }
-            if (!__all_sync(0xffffffffu,
-                            mbar_wait(&sm.aempty[sa], ((it / ASTAGES) & 1) ^ 1, p.status, kErrTimeoutDequant))) {
-                ok = false;
+            const int sa = it % AS;
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.aempty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
                 break;
-            }
             tc_fence_after();
             tmem_st_32x32b_x32(tmem + lane_addr + A_COL0 + sa * 32, vals);
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&sm.afull[sa]);
-            tile = ntile;
-            ks = nks;
-            it += DQ_GROUPS;
         }
-    } else if (warp >= 4 + 4 * DQ_GROUPS) {
+    } else if (warp >= EPI_WARP0) {
         // --------------------------------------------------------- epilogue
+        // TMEM lane = weight row: each thread holds one output feature for 32
+        // tokens per load; the warp transposes its 32 x 32 block through shared
+        // memory and stores 16-byte row segments of y.
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
-        uint32_t tc = 0;
-        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
-            if (!__all_sync(0xffffffffu, mbar_wait(sm.accfull, tc & 1, p.status, kErrTimeoutEpilogue))) break;
+        uint16_t *stage = reinterpret_cast<uint16_t *>(sm.epi0 + q * EPI_STAGE_BYTES);  // [32 tokens][32 rows]
+        for (int tl = 0; tl < my_tiles; ++tl) {
+            if (!__all_sync(0xffffffffu, mbar_wait(sm.accfull, tl & 1, p.status, kErrTimeoutEpilogue))) break;
             tc_fence_after();
-            const int64_t n = int64_t(tile % p.n_tiles) * BM + row;
+            const int tile = int(blockIdx.x) + tl * int(gridDim.x);
+            const int64_t nq = int64_t(tile % p.n_tiles) * BM + q * 32;  // first row of this warp
+            const int64_t n = nq + lane;
             const int64_t t0 = int64_t(tile / p.n_tiles) * BN;
-            const bool valid = n < p.N;
-            const float bias = (valid && p.bias) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+            const float bias = (n < p.N && p.bias) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + lane_addr + ACC_COL + c * 32, v);
                 tmem_ld_wait();
-                if (valid) {
-                    uint16_t *yp = p.y + (t0 + c * 32) * p.N + n;
-                    const int64_t lim = p.T - (t0 + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (i < lim) yp[int64_t(i) * p.N] = to16<BF16>(__uint_as_float(v[i]) + bias);
+                if (c == BN / 32 - 1) {  // accumulator fully read: the next tile's MMAs may start
+                    tc_fence_before();
+                    mbar_arrive(sm.accempty);
                 }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) stage[i * 32 + lane] = to16<BF16>(__uint_as_float(v[i]) + bias);
+                __syncwarp();
+                const int64_t tc0 = t0 + c * 32;
+                if (p.vec_store && nq + 32 <= p.N) {
+                    // lane -> (token row lane/4 + 8j, 16-byte chunk lane%4): 8 rows x 64 B per instruction
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int rr = (lane >> 2) + 8 * j;
+                        if (tc0 + rr < p.T) {
+                            const uint4 val = reinterpret_cast<const uint4 *>(stage + rr * 32)[lane & 3];
+                            *reinterpret_cast<uint4 *>(p.y + (tc0 + rr) * p.N + nq + (lane & 3) * 8) = val;
+                        }
+                    }
+                } else if (n < p.N) {
+                    for (int i = 0; i < 32 && tc0 + i < p.T; ++i) p.y[(tc0 + i) * p.N + n] = stage[i * 32 + lane];
+                }
+                __syncwarp();
             }
-            tc_fence_before();
-            mbar_arrive(sm.accempty);
         }
     }
 
@@ -472,6 +504,7 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
     p.n_tiles = int((N + gemm::BM - 1) / gemm::BM);
     p.t_tiles = int((T + gemm::BN - 1) / gemm::BN);
     p.status = status;
+    p.vec_store = (reinterpret_cast<uintptr_t>(y) % 16 == 0) && (N % 8 == 0);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bf16) return dq ? gemm::launch_fwd<true, true>(mx, mw, mxa, p, st) : gemm::launch_fwd<true, false>(mx, mw, mxa, p, st);
     return dq ? gemm::launch_fwd<false, true>(mx, mw, mxa, p, st) : gemm::launch_fwd<false, false>(mx, mw, mxa, p, st);

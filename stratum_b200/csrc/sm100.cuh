@@ -25,6 +25,8 @@ enum DeviceError : int {
 // A wait that takes longer than this is a hang, never a slow pipeline stage
 // (one stage is microseconds); the kernel then records an error and unwinds.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+// Suspend-time hint for a blocked mbarrier wait (the thread wakes when the phase completes).
+constexpr uint32_t kSuspendHintNs = 1000000u;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -64,6 +66,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread (up to `hint_ns`) until
+// the phase completes, instead of spinning on the issue slots that the
+// working warps of the same sub-partition need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity.  Returns false (after
 // recording `code` in *err) on timeout, or when another thread of the grid
 // already recorded an error, so every role unwinds instead of spinning.
@@ -71,9 +88,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true) {
-#pragma unroll 1
-        for (int i = 0; i < 128; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
         if (*reinterpret_cast<volatile int *>(err) != 0) return false;
         if (globaltimer() - t0 > kWaitTimeoutNs) {
             atomicCAS(err, 0, code);
