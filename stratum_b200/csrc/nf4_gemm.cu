@@ -44,18 +44,18 @@ constexpr int BM = 128;       // weight rows per tile (TMEM lanes, MMA M)
 constexpr int BN = 256;       // tokens per tile (MMA N)
 constexpr int BK = 64;        // K per step: one NF4 block per weight row
 constexpr int XS = 4;         // ring of token tiles (32 KiB each), released by MMA completion
-constexpr int WS = 16;        // ring of packed weight tiles (4 KiB each), released by the dequant warps
+constexpr int WS = 6;         // ring of packed weight tiles (4 KiB each), released by the dequant warps
 constexpr int AS = 8;         // TMEM ring of dequantized weight tiles (32 columns each)
 constexpr int DQG = 3;        // dequant warpgroups; group g owns the steps with it % DQG == g
 constexpr int X_BYTES = BN * BK * 2;  // 32 KiB
 constexpr int W_BYTES = BM * BK / 2;  // 4 KiB
-constexpr int EPI_STAGE_BYTES = 32 * 32 * 2;  // per epilogue warp: 32 tokens x 32 rows of 16-bit
+constexpr int Y_HALF_BYTES = BN * 64 * 2;  // staging of y: two [256 tokens][64 rows] halves, 128B-swizzled
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;    // accumulator: columns [0, 256)
 constexpr int A_COL0 = 256;   // A ring: columns [256, 512)
 constexpr int EPI_WARP0 = 4 + 4 * DQG;
 constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_BYTES + WS * W_BYTES + 4 * EPI_STAGE_BYTES +
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_BYTES + WS * W_BYTES + 2 * Y_HALF_BYTES +
                            1024 /*barriers*/ + 1088 /*tables*/;
 static_assert(A_COL0 + AS * 32 <= TMEM_COLS, "TMEM budget");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -75,14 +75,14 @@ struct FwdParams {
     uint16_t *y;              // [T, N]
     int64_t T, N, K;
     int n_tiles, t_tiles;
-    int vec_store;            // y 16-byte aligned and N % 8 == 0
+    int tma_store;            // y stored through the staging tile + TMA (N % 8 == 0, 16-byte aligned)
     int *status;
 };
 
 struct Smem {
     uint8_t *x0;    // token tile i at x0 + i * X_BYTES (1024-byte aligned)
     uint8_t *w0;    // packed weight tile i at w0 + i * W_BYTES
-    uint8_t *epi0;  // epilogue staging, EPI_STAGE_BYTES per epilogue warp
+    uint8_t *y0;    // y staging: two halves of Y_HALF_BYTES (1024-byte aligned)
     uint64_t *xfull, *xempty, *wfull, *wempty, *afull, *aempty, *accfull, *accempty, *drain;
     uint32_t *tmem_slot;
     float *lv, *c2;
@@ -94,10 +94,10 @@ __device__ __forceinline__ Smem carve(uint8_t *raw) {
     uint8_t *p = reinterpret_cast<uint8_t *>(base);
     s.x0 = p;
     p += XS * X_BYTES;
+    s.y0 = p;
+    p += 2 * Y_HALF_BYTES;
     s.w0 = p;
     p += WS * W_BYTES;
-    s.epi0 = p;
-    p += 4 * EPI_STAGE_BYTES;
     uint64_t *b = reinterpret_cast<uint64_t *>(p);
     s.xfull = b; b += XS;
     s.xempty = b; b += XS;
@@ -129,7 +129,7 @@ __device__ __forceinline__ uint16_t to16(float v) {
 template <bool BF16, bool DQ>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-               const __grid_constant__ CUtensorMap tm_xa, const FwdParams p) {
+               const __grid_constant__ CUtensorMap tm_xa, const __grid_constant__ CUtensorMap tm_y, const FwdParams p) {
     extern __shared__ uint8_t smem_raw[];
     Smem sm = carve(smem_raw);
     const int warp = threadIdx.x >> 5;
@@ -307,50 +307,91 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
     } else if (warp >= EPI_WARP0) {
         // --------------------------------------------------------- epilogue
-        // TMEM lane = weight row: each thread holds one output feature for 32
-        // tokens per load; the warp transposes its 32 x 32 block through shared
-        // memory and stores 16-byte row segments of y.
         const int q = warp & 3;
-        const int row = q * 32 + lane;
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
-        uint16_t *stage = reinterpret_cast<uint16_t *>(sm.epi0 + q * EPI_STAGE_BYTES);  // [32 tokens][32 rows]
+        const bool leader = warp == EPI_WARP0 && lane == 0;
         for (int tl = 0; tl < my_tiles; ++tl) {
             if (!__all_sync(0xffffffffu, mbar_wait(sm.accfull, tl & 1, p.status, kErrTimeoutEpilogue))) break;
             tc_fence_after();
             const int tile = int(blockIdx.x) + tl * int(gridDim.x);
-            const int64_t nq = int64_t(tile % p.n_tiles) * BM + q * 32;  // first row of this warp
-            const int64_t n = nq + lane;
+            const int64_t n0 = int64_t(tile % p.n_tiles) * BM;
             const int64_t t0 = int64_t(tile / p.n_tiles) * BN;
-            const float bias = (n < p.N && p.bias) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(tmem + lane_addr + ACC_COL + c * 32, v);
-                tmem_ld_wait();
-                if (c == BN / 32 - 1) {  // accumulator fully read: the next tile's MMAs may start
-                    tc_fence_before();
-                    mbar_arrive(sm.accempty);
-                }
+            if (p.tma_store) {
+                // TMEM -> registers as 16x256b fragments (row = weight row, pairs of
+                // tokens), + bias, -> 16-bit -> stmatrix.trans into the [token][row]
+                // staging tile, then one TMA store per 64-row half.
+                if (leader) bulk_wait_read0();  // previous tile's store has read the staging tile
+                named_bar_sync(1, 128);
+                float bias[2][2];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) stage[i * 32 + lane] = to16<BF16>(__uint_as_float(v[i]) + bias);
-                __syncwarp();
-                const int64_t tc0 = t0 + c * 32;
-                if (p.vec_store && nq + 32 <= p.N) {
-                    // lane -> (token row lane/4 + 8j, 16-byte chunk lane%4): 8 rows x 64 B per instruction
+                for (int h = 0; h < 2; ++h)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int rr = (lane >> 2) + 8 * j;
-                        if (tc0 + rr < p.T) {
-                            const uint4 val = reinterpret_cast<const uint4 *>(stage + rr * 32)[lane & 3];
-                            *reinterpret_cast<uint4 *>(p.y + (tc0 + rr) * p.N + nq + (lane & 3) * 8) = val;
-                        }
+                    for (int e = 0; e < 2; ++e) {
+                        const int64_t n = n0 + q * 32 + h * 16 + (lane >> 2) + 8 * e;
+                        bias[h][e] = (p.bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
                     }
-                } else if (n < p.N) {
-                    for (int i = 0; i < 32 && tc0 + i < p.T; ++i) p.y[(tc0 + i) * p.N + n] = stage[i * 32 + lane];
+                // this thread's stmatrix row: matrix k = lane/8, row j = lane%8
+                const int k = lane >> 3, j = lane & 7;
+                const int tok_in = j + 8 * (k >> 1);         // token offset within a 16-column block
+                const int nrow = q * 32 + 8 * (k & 1);        // + 16h: first weight row of the 8x8 matrix
+#pragma unroll 1
+                for (int cb = 0; cb < BN / 16; ++cb) {
+                    uint32_t v[2][8];
+                    tmem_ld_16x256b_x2(tmem + lane_addr + ACC_COL + cb * 16, v[0]);
+                    tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + ACC_COL + cb * 16, v[1]);
+                    tmem_ld_wait();
+                    if (cb == BN / 16 - 1) {  // accumulator fully read: the next tile's MMAs may start
+                        tc_fence_before();
+                        mbar_arrive(sm.accempty);
+                    }
+                    const int tok = cb * 16 + tok_in;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t x4[4];
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) {
+                            const float b = bias[h][m & 1];
+                            const float lo = __uint_as_float(v[h][2 * m]) + b;
+                            const float hi = __uint_as_float(v[h][2 * m + 1]) + b;
+                            x4[m] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+                        }
+                        // registers {0,1}: rows +0, tokens +0..7; {2,3}: rows +8; {4,5}/{6,7}: tokens +8
+                        const int nr = nrow + 16 * h;
+                        const int half = nr >> 6, chunk = (nr & 63) >> 3;
+                        const uint8_t *dst = sm.y0 + half * Y_HALF_BYTES + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+                        stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
+                    }
                 }
-                __syncwarp();
+                fence_proxy_async_smem();
+                named_bar_sync(1, 128);
+                if (leader) {
+                    tma_store_2d(&tm_y, int32_t(n0), int32_t(t0), sm.y0);
+                    if (n0 + 64 < p.N) tma_store_2d(&tm_y, int32_t(n0 + 64), int32_t(t0), sm.y0 + Y_HALF_BYTES);
+                    bulk_commit();
+                }
+            } else {
+                // generic path (N % 8 != 0 or unaligned y): element stores
+                const int row = q * 32 + lane;
+                const int64_t n = n0 + row;
+                const float bias = (n < p.N && p.bias) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem + lane_addr + ACC_COL + c * 32, v);
+                    tmem_ld_wait();
+                    if (c == BN / 32 - 1) {
+                        tc_fence_before();
+                        mbar_arrive(sm.accempty);
+                    }
+                    if (n < p.N) {
+                        const int64_t tc0 = t0 + c * 32;
+                        for (int i = 0; i < 32 && tc0 + i < p.T; ++i)
+                            p.y[(tc0 + i) * p.N + n] = to16<BF16>(__uint_as_float(v[i]) + bias);
+                    }
+                }
             }
         }
+        if (leader) bulk_wait0();  // stores complete before the CTA exits
     }
 
     tc_fence_before();
@@ -404,8 +445,8 @@ int *status_ptr() {
 }
 
 template <bool BF16, bool DQ>
-int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mxa, const FwdParams &p,
-               cudaStream_t st) {
+int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mxa, const CUtensorMap &my,
+               const FwdParams &p, cudaStream_t st) {
     auto kern = k_nf4_gemm_fwd<BF16, DQ>;
     static bool attr_set[64] = {false};
     int dev = 0;
@@ -417,7 +458,7 @@ int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &
     }
     const int ntiles = p.n_tiles * p.t_tiles;
     const int grid = ntiles < sm_count() ? ntiles : sm_count();
-    kern<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(mx, mw, mxa, p);
+    kern<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(mx, mw, mxa, my, p);
     return check_launch("nf4_gemm_fwd");
 }
 
@@ -504,10 +545,16 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
     p.n_tiles = int((N + gemm::BM - 1) / gemm::BM);
     p.t_tiles = int((T + gemm::BN - 1) / gemm::BN);
     p.status = status;
-    p.vec_store = (reinterpret_cast<uintptr_t>(y) % 16 == 0) && (N % 8 == 0);
+    p.tma_store = (reinterpret_cast<uintptr_t>(y) % 16 == 0) && (N % 8 == 0);
+    CUtensorMap my = mx;
+    if (p.tma_store) {
+        rc = gemm::make_map_2d(&my, xdt, y, uint64_t(N), uint64_t(T), uint64_t(N) * 2, 64, gemm::BN,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_fwd y");
+        if (rc) return rc;
+    }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (bf16) return dq ? gemm::launch_fwd<true, true>(mx, mw, mxa, p, st) : gemm::launch_fwd<true, false>(mx, mw, mxa, p, st);
-    return dq ? gemm::launch_fwd<false, true>(mx, mw, mxa, p, st) : gemm::launch_fwd<false, false>(mx, mw, mxa, p, st);
+    if (bf16) return dq ? gemm::launch_fwd<true, true>(mx, mw, mxa, my, p, st) : gemm::launch_fwd<true, false>(mx, mw, mxa, my, p, st);
+    return dq ? gemm::launch_fwd<false, true>(mx, mw, mxa, my, p, st) : gemm::launch_fwd<false, false>(mx, mw, mxa, my, p, st);
 }
 
 }  // extern "C"
