@@ -125,6 +125,22 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K,
                          const void *lora_xa, const void *lora_b, int r,
                          void *y, void *stream);
 
+/* K3+K4 backward: fused NF4 input gradient with the LoRA term.
+ * Replaces the autograd backward of NF4Linear.forward's F.linear
+ * (stratum/nf4_linear.py:47) and of PEFT lora.Linear (scripts/train.py:568-573):
+ *   dx[T,K] = dy[T,N] . W[N,K] + lora_dyb[T,r] . lora_a[r,K]
+ *   dy       : T x N (N % 8 == 0), dtype BF16 or F16, 16-byte aligned
+ *   W        : as in stratum_nf4_gemm_fwd, K % 64 == 0
+ *   lora_dyb : T x ceil(r/64)*64 = scaling * dy . lora_B, zero-padded (NULL when r == 0)
+ *   lora_a   : r x K, 16-byte aligned (NULL when r == 0)
+ *   dx       : T x K */
+int stratum_nf4_gemm_dx(const void *dy, int dtype, int64_t T, int64_t N,
+                        const uint8_t *packed, const float *absmax,
+                        const uint8_t *absmax_q, const float *absmax2,
+                        const float *code2, const float *offset, const float *code16,
+                        int64_t K, const void *lora_dyb, const void *lora_a, int r,
+                        void *dx, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

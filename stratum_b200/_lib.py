@@ -43,6 +43,8 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_device_status": (_int, [ctypes.POINTER(ctypes.c_int), _int, _vp]),
     "stratum_nf4_gemm_fwd": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _int, _vp,
                                     _vp, _int, _vp, _vp]),
+    "stratum_nf4_gemm_dx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _int,
+                                   _vp, _vp]),
 }
 
 ABI_VERSION = 1

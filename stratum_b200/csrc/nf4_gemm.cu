@@ -402,6 +402,319 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     }
 }
 
+// =================================================================== dX ===
+//
+// Input gradient (autograd of NF4Linear.forward / PEFT lora.Linear):
+//     dX[T, K] = dY[T, N] . W[N, K] + dyb[T, r] . lora_A[r, K]
+// with dyb = scaling * dY . lora_B computed beforehand.  Swap-AB again: the
+// MMA computes D[k, t] = sum_n W[n, k] dY[t, n] for 128 columns of W (TMEM
+// lanes) x 256 tokens, 64 rows of W per step.  The contraction now runs over
+// W's rows, so the A operand is W^T: the dequant warps decode each (row,
+// 64-column block) of W -- one NF4 block, exactly as in the forward -- and
+// write the 64 values as one 128-byte row of an MN-major, 128B-swizzled
+// shared-memory tile (conflict-free), which tcgen05.mma reads transposed.
+// The kernel keeps no weight tile in TMEM, so the accumulator is double
+// buffered (2 x 256 columns) and the epilogue of tile i overlaps the
+// mainloop of tile i+1.
+namespace dx {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int XS = 3;               // dY tiles (32 KiB)
+constexpr int WS = 4;               // packed weight tiles: 64 rows x 64 bytes (4 KiB)
+constexpr int AS = 3;               // dequantized W^T tiles in shared memory (16 KiB)
+constexpr int DQG = 3;
+constexpr int X_BYTES = BN * BK * 2;
+constexpr int W_BYTES = BK * BM / 2;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int A_ATOM = BK * 128;    // one 64-column MN atom: 64 K-rows x 128 B
+constexpr int Y_HALF_BYTES = BN * 64 * 2;
+constexpr int EPI_WARP0 = 4 + 4 * DQG;
+constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
+constexpr int SMEM_BYTES = 1024 + XS * X_BYTES + AS * A_BYTES + 2 * Y_HALF_BYTES + WS * W_BYTES + 512 + 1088;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+struct Params {
+    const float *absmax;
+    const uint8_t *absmax_q;
+    const float *absmax2;
+    const float *code2;
+    const float *offset;
+    const float *code16;
+    const uint16_t *lora_a;  // [r, K] or null
+    int r;
+    int lora_chunks;
+    uint16_t *dx;            // [T, K]
+    int64_t T, N, K;
+    int k_tiles, t_tiles;
+    int tma_store;
+    int *status;
+};
+
+template <bool BF16, bool DQ>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_w,
+              const __grid_constant__ CUtensorMap tm_dyb, const __grid_constant__ CUtensorMap tm_dx, const Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *x0 = base;                              // XS x 32 KiB (1024-aligned)
+    uint8_t *a0 = x0 + XS * X_BYTES;                 // AS x 16 KiB (1024-aligned)
+    uint8_t *y0 = a0 + AS * A_BYTES;                 // 2 x 32 KiB (1024-aligned)
+    uint8_t *w0 = y0 + 2 * Y_HALF_BYTES;             // WS x 4 KiB
+    uint64_t *bars = reinterpret_cast<uint64_t *>(w0 + WS * W_BYTES);
+    uint64_t *xfull = bars, *xempty = xfull + XS, *wfull = xempty + XS, *wempty = wfull + WS;
+    uint64_t *afull = wempty + WS, *aempty = afull + AS, *accfull = aempty + AS, *accempty = accfull + 2;
+    uint64_t *drain = accempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    float *lv_s = reinterpret_cast<float *>(bars + 64);
+    float *c2 = lv_s + 16;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nkw = int((p.N + BK - 1) / BK);  // weight-row steps (ragged last step zero-filled)
+    const int nk = nkw + p.lora_chunks;
+    const int ntiles = p.k_tiles * p.t_tiles;
+    const int my_tiles = ntiles > int(blockIdx.x) ? (ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < XS; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xempty[i], 1); }
+        for (int i = 0; i < WS; ++i) { mbar_init(&wfull[i], 1); mbar_init(&wempty[i], 128); }
+        for (int i = 0; i < AS; ++i) { mbar_init(&afull[i], 128); mbar_init(&aempty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&accfull[i], 1); mbar_init(&accempty[i], 128); }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (threadIdx.x < 16) lv_s[threadIdx.x] = p.code16[threadIdx.x];
+    if (DQ) {
+        for (int i = threadIdx.x; i < 256; i += NUM_THREADS) c2[i] = p.code2[i];
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------- producer: dY (and dyb) tiles
+        if (lane == 0) {
+            prefetch_tensormap(&tm_dy);
+            if (p.lora_chunks) prefetch_tensormap(&tm_dyb);
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                const int t0 = ((int(blockIdx.x) + tl * int(gridDim.x)) / p.k_tiles) * BN;
+                for (int ks = 0; ks < nk; ++ks, ++it) {
+                    const int s = it % XS;
+                    if (!mbar_wait(&xempty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&xfull[s], X_BYTES);
+                    if (ks < nkw) tma_load_2d(x0 + s * X_BYTES, &tm_dy, ks * BK, t0, &xfull[s]);
+                    else tma_load_2d(x0 + s * X_BYTES, &tm_dyb, (ks - nkw) * BK, t0, &xfull[s]);
+                }
+            }
+            for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
+                mbar_wait(&xfull[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+        }
+    } else if (warp == 2) {
+        // ------------------------------- producer: packed weight tiles (64 x 128)
+        if (lane == 0) {
+            prefetch_tensormap(&tm_w);
+            uint32_t wt = 0;
+            bool ok = true;
+            for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                const int k0 = ((int(blockIdx.x) + tl * int(gridDim.x)) % p.k_tiles) * BM;
+                for (int ks = 0; ks < nkw; ++ks, ++wt) {
+                    const int s = wt % WS;
+                    if (!mbar_wait(&wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&wfull[s], W_BYTES);
+                    tma_load_2d(w0 + s * W_BYTES, &tm_w, k0 / 2, ks * BK, &wfull[s]);
+                }
+            }
+            for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
+                mbar_wait(&wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_amn(BF16, BM, BN);
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                const int ab = tl & 1;
+                if (!mbar_wait(&accempty[ab], ((tl >> 1) & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t acc = tmem + uint32_t(ab * 256);
+                for (int ks = 0; ks < nk; ++ks, ++it) {
+                    const int s = it % XS, sa = it % AS;
+                    if (!mbar_wait(&afull[sa], (it / AS) & 1, p.status, kErrTimeoutMma) ||
+                        !mbar_wait(&xfull[s], (it / XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t bdesc = smem_desc_k_sw128(x0 + s * X_BYTES);
+                    const uint64_t adesc = smem_desc_mn_sw128(a0 + sa * A_BYTES, A_ATOM, 1024);
+#pragma unroll
+                    for (int j = 0; j < BK / 16; ++j)  // 16 K-rows = two 8-row groups = 2 KiB further
+                        mma_ss_f16(acc, adesc + uint64_t(j * (2048 >> 4)), bdesc + uint64_t(j * 2), idesc, (ks | j) != 0);
+                    mma_commit(&xempty[s]);
+                    mma_commit(&aempty[sa]);
+                }
+                if (ok) mma_commit(&accfull[ab]);
+            }
+            mma_commit(drain);
+            mbar_wait(drain, 0, p.status, kErrTimeoutTeardown);
+        }
+    } else if (warp >= 4 && warp < EPI_WARP0) {
+        // ---------------------------------------------------- dequant warps
+        // thread -> (weight row rl = tid % 64 of the step, 64-column block kb = tid / 64)
+        const int grp = (warp - 4) >> 2;
+        const int tid = (warp & 3) * 32 + lane;
+        const int rl = tid & 63, kb = tid >> 6;
+        float lv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
+        const int64_t kbl = p.K / 64;  // NF4 blocks per weight row
+        auto block_of = [&](uint32_t it, int64_t &wrow, int64_t &kblk) {
+            const int tl = int(it / nk), ks = int(it % nk);
+            const int tile = int(blockIdx.x) + tl * int(gridDim.x);
+            wrow = int64_t(ks) * BK + rl;
+            kblk = int64_t(tile % p.k_tiles) * 2 + kb;
+            return ks;
+        };
+        auto absmax_of = [&](uint32_t it) -> float {
+            if (it / nk >= uint32_t(my_tiles)) return 0.f;
+            int64_t wrow, kblk;
+            const int ks = block_of(it, wrow, kblk);
+            if (ks >= nkw || wrow >= p.N || kblk >= kbl) return 0.f;
+            const int64_t b = wrow * kbl + kblk;
+            if constexpr (DQ) {
+                return __fadd_rn(__fmul_rn(c2[__ldg(p.absmax_q + b)], __ldg(p.absmax2 + (b >> 8))), *p.offset);
+            } else {
+                return __ldg(p.absmax + b);
+            }
+        };
+        const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
+        float am_next = absmax_of(uint32_t(grp));
+        for (uint32_t it = uint32_t(grp); it < total; it += DQG) {
+            const float am = am_next;
+            am_next = absmax_of(it + DQG);
+            int64_t wrow, kblk;
+            const int ks = block_of(it, wrow, kblk);
+            const int tl = int(it / nk);
+            uint32_t vals[32];
+            if (ks < nkw) {
+                const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
+                const int s = wt % WS;
+                if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant))) break;
+                // 64-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3)
+                const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * W_BYTES + rl * 64);
+                const int sw = (rl >> 1) & 3;
+                const uint4 p0 = src[(2 * kb) ^ sw], p1 = src[(2 * kb + 1) ^ sw];
+                mbar_arrive(&wempty[s]);
+                const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+                const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
+                nf4_decode_block(t, w, vals);
+            } else {
+                // LoRA chunk: rank row j of lora_A, 64 columns (zero beyond r / K)
+                const int j = (ks - nkw) * BK + rl;
+                const bool ok_row = j < p.r && kblk < kbl;
+                const uint4 *src = reinterpret_cast<const uint4 *>(p.lora_a + int64_t(j) * p.K + kblk * 64);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint4 v = ok_row ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+                    vals[4 * c] = v.x; vals[4 * c + 1] = v.y; vals[4 * c + 2] = v.z; vals[4 * c + 3] = v.w;
+                }
+            }
+            const int sa = it % AS;
+            if (!__all_sync(0xffffffffu, mbar_wait(&aempty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant))) break;
+            // MN-major atom kb, K-row rl: 8 chunks of 16 B, XOR-swizzled by rl % 8
+            uint8_t *dst = a0 + sa * A_BYTES + kb * A_ATOM + (rl >> 3) * 1024 + (rl & 7) * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<uint4 *>(dst + ((c ^ (rl & 7)) << 4)) =
+                    make_uint4(vals[4 * c], vals[4 * c + 1], vals[4 * c + 2], vals[4 * c + 3]);
+            fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
+            mbar_arrive(&afull[sa]);
+        }
+    } else if (warp >= EPI_WARP0) {
+        // --------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const uint32_t lane_addr = uint32_t(q * 32) << 16;
+        const bool leader = warp == EPI_WARP0 && lane == 0;
+        const int kq = lane >> 3, jr = lane & 7;
+        const int tok_in = jr + 8 * (kq >> 1);
+        const int nrow = q * 32 + 8 * (kq & 1);
+        for (int tl = 0; tl < my_tiles; ++tl) {
+            const int ab = tl & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&accfull[ab], (tl >> 1) & 1, p.status, kErrTimeoutEpilogue))) break;
+            tc_fence_after();
+            const int tile = int(blockIdx.x) + tl * int(gridDim.x);
+            const int64_t k0 = int64_t(tile % p.k_tiles) * BM;
+            const int64_t t0 = int64_t(tile / p.k_tiles) * BN;
+            const uint32_t acc = tmem + lane_addr + uint32_t(ab * 256);
+            if (p.tma_store) {
+                if (leader) bulk_wait_read0();
+                named_bar_sync(1, 128);
+#pragma unroll 1
+                for (int cb = 0; cb < BN / 16; ++cb) {
+                    uint32_t v[2][8];
+                    tmem_ld_16x256b_x2(acc + cb * 16, v[0]);
+                    tmem_ld_16x256b_x2(acc + (16u << 16) + cb * 16, v[1]);
+                    tmem_ld_wait();
+                    if (cb == BN / 16 - 1) {
+                        tc_fence_before();
+                        mbar_arrive(&accempty[ab]);
+                    }
+                    const int tok = cb * 16 + tok_in;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t x4[4];
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) {
+                            const float lo = __uint_as_float(v[h][2 * m]), hi = __uint_as_float(v[h][2 * m + 1]);
+                            x4[m] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+                        }
+                        const int nr = nrow + 16 * h;
+                        const int half = nr >> 6, chunk = (nr & 63) >> 3;
+                        const uint8_t *dst = y0 + half * Y_HALF_BYTES + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+                        stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
+                    }
+                }
+                fence_proxy_async_smem();
+                named_bar_sync(1, 128);
+                if (leader) {
+                    tma_store_2d(&tm_dx, int32_t(k0), int32_t(t0), y0);
+                    if (k0 + 64 < p.K) tma_store_2d(&tm_dx, int32_t(k0 + 64), int32_t(t0), y0 + Y_HALF_BYTES);
+                    bulk_commit();
+                }
+            } else {
+                const int64_t k = k0 + q * 32 + lane;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(acc + c * 32, v);
+                    tmem_ld_wait();
+                    if (c == BN / 32 - 1) {
+                        tc_fence_before();
+                        mbar_arrive(&accempty[ab]);
+                    }
+                    if (k < p.K) {
+                        const int64_t tc0 = t0 + c * 32;
+                        for (int i = 0; i < 32 && tc0 + i < p.T; ++i)
+                            p.dx[(tc0 + i) * p.K + k] = to16<BF16>(__uint_as_float(v[i]));
+                    }
+                }
+            }
+        }
+        if (leader) bulk_wait0();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace dx
+
 // ------------------------------------------------------------------- host --
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -460,6 +773,24 @@ int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &
     const int grid = ntiles < sm_count() ? ntiles : sm_count();
     kern<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(mx, mw, mxa, my, p);
     return check_launch("nf4_gemm_fwd");
+}
+
+template <bool BF16, bool DQ>
+int launch_dx(const CUtensorMap &mdy, const CUtensorMap &mw, const CUtensorMap &mdyb, const CUtensorMap &mdx,
+              const dx::Params &p, cudaStream_t st) {
+    auto kern = dx::k_nf4_gemm_dx<BF16, DQ>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dx::SMEM_BYTES) != cudaSuccess)
+            return fail(STRATUM_ERR_CUDA, "nf4_gemm_dx: cannot set %d bytes of shared memory", dx::SMEM_BYTES);
+        attr_set[dev] = true;
+    }
+    const int ntiles = p.k_tiles * p.t_tiles;
+    const int grid = ntiles < sm_count() ? ntiles : sm_count();
+    kern<<<grid, dx::NUM_THREADS, dx::SMEM_BYTES, st>>>(mdy, mw, mdyb, mdx, p);
+    return check_launch("nf4_gemm_dx");
 }
 
 }  // namespace gemm
@@ -555,6 +886,70 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bf16) return dq ? gemm::launch_fwd<true, true>(mx, mw, mxa, my, p, st) : gemm::launch_fwd<true, false>(mx, mw, mxa, my, p, st);
     return dq ? gemm::launch_fwd<false, true>(mx, mw, mxa, my, p, st) : gemm::launch_fwd<false, false>(mx, mw, mxa, my, p, st);
+}
+
+int stratum_nf4_gemm_dx(const void *dy, int dtype, int64_t T, int64_t N, const uint8_t *packed, const float *absmax,
+                        const uint8_t *absmax_q, const float *absmax2, const float *code2, const float *offset,
+                        const float *code16, int64_t K, const void *lora_dyb, const void *lora_a, int r, void *dx_out,
+                        void *stream) {
+    STRATUM_REQUIRE(T >= 0 && N >= 0 && K >= 0, "nf4_gemm_dx: negative size");
+    if (T == 0 || K == 0) return STRATUM_OK;
+    STRATUM_REQUIRE(dy && packed && code16 && dx_out, "nf4_gemm_dx: null pointer");
+    if (dtype != STRATUM_BF16 && dtype != STRATUM_F16)
+        return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_dx: dy must be bf16 or fp16");
+    if (K % 64 != 0) return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_dx: K=%lld must be a multiple of 64", (long long)K);
+    if (N % 8 != 0 || N == 0)
+        return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_dx: N=%lld must be a positive multiple of 8", (long long)N);
+    const bool dq = absmax == nullptr;
+    STRATUM_REQUIRE(!dq || (absmax_q && absmax2 && code2 && offset), "nf4_gemm_dx: need absmax or the double-quant set");
+    STRATUM_REQUIRE(r >= 0 && r <= 256, "nf4_gemm_dx: lora rank %d out of range", r);
+    STRATUM_REQUIRE(r == 0 || (lora_dyb && lora_a), "nf4_gemm_dx: lora needs dyb and A");
+    STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(dy) % 16 == 0 && reinterpret_cast<uintptr_t>(packed) % 16 == 0 &&
+                        (r == 0 || reinterpret_cast<uintptr_t>(lora_a) % 16 == 0),
+                    "nf4_gemm_dx: dy, packed and lora_A must be 16-byte aligned");
+    int *status = gemm::status_ptr();
+    if (!status) return fail(STRATUM_ERR_CUDA, "nf4_gemm_dx: no status word");
+    const bool bf16 = dtype == STRATUM_BF16;
+    const CUtensorMapDataType xdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap mdy, mw, mdyb, mdx;
+    int rc = gemm::make_map_2d(&mdy, xdt, dy, uint64_t(N), uint64_t(T), uint64_t(N) * 2, gemm::dx::BK, gemm::dx::BN,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_dx dy");
+    if (rc) return rc;
+    // packed W viewed as [N rows][K/2 bytes]; box 64 bytes (128 columns) x 64 rows, 64-byte swizzle
+    rc = gemm::make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(K / 2), uint64_t(N), uint64_t(K / 2), 64,
+                           gemm::dx::BK, CU_TENSOR_MAP_SWIZZLE_64B, "nf4_gemm_dx packed");
+    if (rc) return rc;
+    const int lora_chunks = (r + 63) / 64;
+    if (r > 0) {
+        STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(lora_dyb) % 16 == 0, "nf4_gemm_dx: dyb must be 16-byte aligned");
+        rc = gemm::make_map_2d(&mdyb, xdt, lora_dyb, uint64_t(lora_chunks * 64), uint64_t(T),
+                               uint64_t(lora_chunks * 64) * 2, 64, gemm::dx::BN, CU_TENSOR_MAP_SWIZZLE_128B,
+                               "nf4_gemm_dx dyb");
+        if (rc) return rc;
+    } else {
+        mdyb = mdy;
+    }
+    gemm::dx::Params p{};
+    p.absmax = absmax; p.absmax_q = absmax_q; p.absmax2 = absmax2; p.code2 = code2; p.offset = offset;
+    p.code16 = code16;
+    p.lora_a = static_cast<const uint16_t *>(lora_a);
+    p.r = r;
+    p.lora_chunks = lora_chunks;
+    p.dx = static_cast<uint16_t *>(dx_out);
+    p.T = T; p.N = N; p.K = K;
+    p.k_tiles = int((K + gemm::dx::BM - 1) / gemm::dx::BM);
+    p.t_tiles = int((T + gemm::dx::BN - 1) / gemm::dx::BN);
+    p.status = status;
+    p.tma_store = reinterpret_cast<uintptr_t>(dx_out) % 16 == 0;
+    mdx = mdy;
+    if (p.tma_store) {
+        rc = gemm::make_map_2d(&mdx, xdt, dx_out, uint64_t(K), uint64_t(T), uint64_t(K) * 2, 64, gemm::dx::BN,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_dx dx");
+        if (rc) return rc;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (bf16) return dq ? gemm::launch_dx<true, true>(mdy, mw, mdyb, mdx, p, st) : gemm::launch_dx<true, false>(mdy, mw, mdyb, mdx, p, st);
+    return dq ? gemm::launch_dx<false, true>(mdy, mw, mdyb, mdx, p, st) : gemm::launch_dx<false, false>(mdy, mw, mdyb, mdx, p, st);
 }
 
 }  // extern "C"

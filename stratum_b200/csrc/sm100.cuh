@@ -181,6 +181,25 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(const void *tile) {
     return d;
 }
 
+// Shared-memory matrix descriptor: MN-major, 128-byte swizzle.  Atoms of 8
+// K-rows x 128 bytes (64 16-bit MN elements); `lbo` = byte stride between
+// 64-element MN atoms, `sbo` = byte stride between 8-row K groups.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(const void *tile, uint32_t lbo, uint32_t sbo) {
+    const uint64_t addr = smem_u32(tile);
+    uint64_t d = 0;
+    d |= (addr & 0x3FFFFull) >> 4;
+    d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+    d |= uint64_t((sbo >> 4) & 0x3FFF) << 32;
+    d |= uint64_t(1) << 46;
+    d |= uint64_t(2) << 61;
+    return d;
+}
+
+// Instruction descriptor for kind::f16 with A MN-major (transposed), B K-major.
+__host__ __device__ constexpr uint32_t idesc_f16_amn(bool bf16, int M, int N) {
+    return idesc_f16(bf16, M, N) | (1u << 15);
+}
+
 // 32 lanes x 32 columns of 32-bit: thread t <-> lane (base + t), 32 registers.
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(

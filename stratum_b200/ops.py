@@ -99,3 +99,52 @@ def nf4_gemm_fwd(
             "nf4_gemm_fwd",
         )
     return y.reshape(*x.shape[:-1], N)
+
+
+def nf4_gemm_dx(
+    dy: torch.Tensor,
+    packed: torch.Tensor,
+    qs: QuantState,
+    lora_A: Optional[torch.Tensor] = None,
+    lora_B: Optional[torch.Tensor] = None,
+    scaling: float = 1.0,
+    dyb: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """dx = dy . W + scaling * (dy . lora_B) . lora_A with W in NF4 (fused kernel).
+
+    ``dyb`` may be passed precomputed (= scaling * dy . lora_B, padded to a
+    multiple of 64 columns), e.g. when dA needs it too.
+    """
+    _lib.require_cuda(dy, "nf4_gemm_dx")
+    if dy.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"nf4_gemm_dx: dy must be bf16 or fp16, got {dy.dtype}")
+    if qs.blocksize != 64 or len(qs.shape) != 2:
+        raise ValueError("nf4_gemm_dx: needs a 2-D NF4 weight with blocksize 64")
+    N, K = int(qs.shape[0]), int(qs.shape[1])
+    if dy.shape[-1] != N:
+        raise ValueError(f"nf4_gemm_dx: dy has {dy.shape[-1]} features, weight has {N} rows")
+    dev = dy.device
+    dy2 = dy.reshape(-1, N)
+    if not dy2.is_contiguous() or dy2.data_ptr() % 16:
+        dy2 = dy2.contiguous()
+    T = dy2.shape[0]
+    dx = torch.empty((T, K), dtype=dy.dtype, device=dev)
+    r = 0
+    la = None
+    if lora_A is not None:
+        r = int(lora_A.shape[0])
+        if dyb is None:
+            dyb = lora_down(dy2, lora_B.t(), scaling)
+        la = lora_A if (lora_A.dtype == dy.dtype and lora_A.is_contiguous()) else lora_A.to(dy.dtype).contiguous()
+    absmax, absmax_q, absmax2, code2, offset, code16 = _weight_args(qs, dev)
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(
+            L.stratum_nf4_gemm_dx(
+                _lib.ptr(dy2), _lib.DTYPE_CODE[dy.dtype], T, N, _lib.ptr(packed), _lib.ptr(absmax), _lib.ptr(absmax_q),
+                _lib.ptr(absmax2), _lib.ptr(code2), _lib.ptr(offset), _lib.ptr(code16), K, _lib.ptr(dyb), _lib.ptr(la), r,
+                _lib.ptr(dx), _lib.stream_of(dev),
+            ),
+            "nf4_gemm_dx",
+        )
+    return dx.reshape(*dy.shape[:-1], K)
