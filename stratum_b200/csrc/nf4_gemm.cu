@@ -283,10 +283,13 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const uint4 *src = reinterpret_cast<const uint4 *>(sm.w0 + s * W_BYTES + row * 32);
                 const int sw = (row >> 2) & 1;
                 const uint4 p0 = src[sw], p1 = src[sw ^ 1];
-                mbar_arrive(&sm.wempty[s]);
                 const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
                 const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
                 nf4_decode_block(t, w, vals);
+                // release the stage only once the words are consumed, and order these
+                // generic-proxy reads before the TMA (async proxy) refill of the stage
+                fence_proxy_async_smem();
+                mbar_arrive(&sm.wempty[s]);
             } else {
                 const int j0 = (ks - nkw) * BK;
                 const bool valid = n < p.N;
@@ -606,10 +609,13 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * W_BYTES + rl * 64);
                 const int sw = (rl >> 1) & 3;
                 const uint4 p0 = src[(2 * kb) ^ sw], p1 = src[(2 * kb + 1) ^ sw];
-                mbar_arrive(&wempty[s]);
                 const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
                 const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
                 nf4_decode_block(t, w, vals);
+                // release the stage only once the words are consumed, and order these
+                // generic-proxy reads before the TMA (async proxy) refill of the stage
+                fence_proxy_async_smem();
+                mbar_arrive(&wempty[s]);
             } else {
                 // LoRA chunk: rank row j of lora_A, 64 columns (zero beyond r / K)
                 const int j = (ks - nkw) * BK + rl;

@@ -95,3 +95,14 @@ def test_fwd_config5_shape_smoke():
     rows = torch.randint(0, T, (64,), device=DEV)
     ref = x[rows].float() @ w_deq.to(torch.bfloat16).float().t()
     assert relative_error(y[rows].float(), ref) < 4e-3
+
+
+def test_fwd_many_tiles_per_cta_every_tile():
+    T, N, K = 8192, 4096, 2048
+    _, packed, qs, w_deq, x, _, _, _ = _make(N, K, T, seed=13)
+    ref = x.float() @ w_deq.to(torch.bfloat16).float().t()
+    for _ in range(2):
+        y = ops.nf4_gemm_fwd(x, packed, qs).float()
+        err = (y - ref).reshape(T // 256, 256, N // 128, 128)
+        den = ref.reshape(T // 256, 256, N // 128, 128).pow(2).sum(dim=(1, 3)).sqrt()
+        assert (err.pow(2).sum(dim=(1, 3)).sqrt() / den).max().item() < 4e-3

@@ -106,3 +106,19 @@ def test_nf4linear_matches_reference_semantics():
     y = mod(x)
     y_ref = torch.nn.functional.linear(x, mod.weight_dequantized.to(torch.bfloat16))
     assert relative_error(y.float(), y_ref.float()) < 4e-3
+
+
+@pytest.mark.parametrize("T,N,K", [(4096, 1024, 8192), (2048, 4096, 4096)])
+def test_dx_many_tiles_per_cta_every_tile(T, N, K):
+    """Every 256x128 output tile checked, over repeated launches: several tiles per CTA
+    exercise the rings' reuse and the double-buffered accumulator."""
+    packed, qs, w = _weight(N, K, seed=11)
+    g = torch.Generator(device=DEV).manual_seed(12)
+    dy = torch.randn(T, N, generator=g, device=DEV).to(torch.bfloat16)
+    ref = dy.float() @ w.to(torch.bfloat16).float()
+    for _ in range(3):
+        dx = ops.nf4_gemm_dx(dy, packed, qs).float()
+        err = (dx - ref).reshape(T // 256, 256, K // 128, 128)
+        den = ref.reshape(T // 256, 256, K // 128, 128).pow(2).sum(dim=(1, 3)).sqrt()
+        per_tile = err.pow(2).sum(dim=(1, 3)).sqrt() / den
+        assert per_tile.max().item() < 4e-3, f"worst tile {per_tile.max().item()}"
