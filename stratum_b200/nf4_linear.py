@@ -73,7 +73,8 @@ class NF4Linear(nn.Module):
     ``.shape == (out_features, in_features)``), optional frozen ``bias``.
     """
 
-    def __init__(self, quantized: torch.Tensor, quant_state: QuantState, bias: Optional[torch.Tensor] = None):
+    def __init__(self, quantized: Optional[torch.Tensor], quant_state: Optional[QuantState],
+                 bias: Optional[torch.Tensor] = None):
         super().__init__()
         self.quantized = quantized
         self.quant_state = quant_state
@@ -81,15 +82,50 @@ class NF4Linear(nn.Module):
             self.bias = nn.Parameter(bias.contiguous(), requires_grad=False)
         else:
             self.bias = None
-        self.in_features = quant_state.shape[1]
-        self.out_features = quant_state.shape[0]
+        if quant_state is not None:
+            self.in_features = quant_state.shape[1]
+            self.out_features = quant_state.shape[0]
         self.lora_A: Optional[nn.Parameter] = None
         self.lora_B: Optional[nn.Parameter] = None
         self.scaling = 1.0
+        self.streamed = False
 
-    def attach_lora(self, r: int, alpha: float, dtype=torch.bfloat16, init_B_zero: bool = True) -> "NF4Linear":
+    @classmethod
+    def streamed_from(cls, weight: nn.Parameter, payload, bias: Optional[torch.Tensor] = None) -> "NF4Linear":
+        """Fused-mode layer fed by the streaming contract (ensure_weights / free_weights).
+
+        ``weight`` is the frozen placeholder parameter that carries the NF4
+        payload (``stratum_b200.upload.NF4_ATTR``); ``ensure_weights`` uploads
+        the packed bytes into this layer and ``free_weights`` drops them.
+        """
+        m = cls(None, None, bias=None)
+        m.weight = weight
+        weight.requires_grad_(False)
+        if bias is not None:
+            m.bias = bias if isinstance(bias, nn.Parameter) else nn.Parameter(bias, requires_grad=False)
+            m.bias.requires_grad_(False)
+        m.in_features = int(payload.shape[1])
+        m.out_features = int(payload.shape[0])
+        m.streamed = True
+        return m
+
+    def load_device_state(self, quantized: torch.Tensor, quant_state: QuantState) -> None:
+        self.quantized = quantized
+        self.quant_state = quant_state
+
+    def device_state_on(self, device: torch.device) -> bool:
+        return self.quantized is not None and self.quantized.device == device
+
+    def drop_device_state(self) -> bool:
+        had = self.quantized is not None
+        self.quantized = None
+        self.quant_state = None
+        return had
+
+    def attach_lora(self, r: int, alpha: float, dtype=torch.bfloat16, init_B_zero: bool = True,
+                    device=None) -> "NF4Linear":
         """Add a PEFT-style adapter: A kaiming-uniform(a=sqrt 5) [r, in], B zeros [out, r], scaling alpha/r."""
-        dev = self.quantized.device
+        dev = device if device is not None else (self.quantized.device if self.quantized is not None else "cpu")
         A = torch.empty(r, self.in_features, dtype=torch.float32, device=dev)
         nn.init.kaiming_uniform_(A, a=math.sqrt(5))
         B = torch.zeros(self.out_features, r, dtype=torch.float32, device=dev)
@@ -106,6 +142,8 @@ class NF4Linear(nn.Module):
         return dequantize_4bit(self.quantized, self.quant_state)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.quantized is None:
+            raise RuntimeError("NF4Linear: weights are not resident on the device; call ensure_weights() first")
         return _NF4LinearFn.apply(x, self.lora_A, self.lora_B, self.quantized, self.quant_state, self.bias,
                                   self.scaling)
 

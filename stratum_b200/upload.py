@@ -1,0 +1,723 @@
+"""NF4 weight streaming: the reference's ``stratum/upload.py`` contract on B200 kernels.
+
+Two phases, as in the reference (stratum/upload.py:1-12):
+
+* :func:`prepare_nf4` quantizes each frozen >= 2-D parameter to NF4 (on the
+  GPU, with the sm_100a quantizer), keeps the payload in pinned host memory on
+  the parameter under :data:`NF4_ATTR`, and drops the original data.
+* :func:`ensure_weights` / :func:`prefetch_weights` + :class:`NF4Prefetch`
+  upload payloads host -> device, :func:`free_weights` drops the device copy.
+
+Two ways a payload becomes usable on the device:
+
+* compat mode (the reference's behaviour, stratum/upload.py:1021-1040): the
+  payload is dequantized into ``param.data`` in ``payload.dtype`` so stock
+  ``nn.Linear`` / HF modules run unchanged;
+* fused mode: when the parameter belongs to an :class:`NF4Linear` built with
+  :func:`to_nf4_linear`, only the packed bytes (and absmax) are uploaded and
+  the fused GEMM consumes them directly -- the weight is never materialised.
+
+A module can also carry a coalesced pinned arena (:func:`build_layer_arena`):
+every NF4 payload of the module packed into one pinned buffer, uploaded with a
+single copy per layer instead of one per tensor.
+
+Cache files keep the reference's version-1 format (stratum/upload.py:287-302)
+and add a version-2 format carrying the double-quant fields.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import re
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Optional, cast
+
+import torch
+import torch.nn as nn
+
+from . import functional as F
+from .functional import QuantState
+
+NF4_ATTR = "roundpipe_nf4_payload"
+FP16_ATTR = "stratum_fp16_staged"
+ARENA_ATTR = "stratum_b200_nf4_arena"
+CACHE_VERSION = 2
+
+
+@dataclass
+class NF4Stats:
+    """NF4 preparation statistics (reference: stratum/upload.py:31-45)."""
+
+    tensors: int = 0
+    source_bytes: int = 0
+    payload_bytes: int = 0
+    cache_hits: int = 0
+    cache_misses: int = 0
+    cache_writes: int = 0
+
+    @property
+    def compression(self) -> float:
+        if self.payload_bytes == 0:
+            return 0.0
+        return self.source_bytes / self.payload_bytes
+
+
+def _pin_cpu(t: torch.Tensor) -> torch.Tensor:
+    """Copy *t* into pinned host memory (reference: stratum/upload.py:48-55)."""
+    t = t.detach().contiguous().cpu()
+    if t.is_pinned() or not torch.cuda.is_available():
+        return t
+    pinned = torch.empty_like(t, device=torch.device("cpu"), pin_memory=True)
+    pinned.copy_(t)
+    return pinned
+
+
+def _payload_bytes(*tensors: Optional[torch.Tensor]) -> int:
+    return sum(t.numel() * t.element_size() for t in tensors if t is not None)
+
+
+def _dtype_name(dtype: torch.dtype) -> str:
+    return str(dtype).removeprefix("torch.")
+
+
+def _dtype_from_name(name: str) -> torch.dtype:
+    return cast(torch.dtype, getattr(torch, name.removeprefix("torch.")))
+
+
+@dataclass
+class NF4Payload:
+    """NF4 payload of one frozen weight, kept in pinned host memory between steps.
+
+    The first ten fields are the reference's (stratum/upload.py:70-95).  When
+    ``nested`` is set the payload is double-quantized: ``absmax`` holds the
+    uint8 codes and ``absmax2`` / ``code2`` / ``offset`` the second level.
+    """
+
+    quantized: torch.Tensor
+    absmax: torch.Tensor
+    code: torch.Tensor
+    shape: tuple
+    dtype: torch.dtype
+    blocksize: int
+    quant_type: str
+    source_numel: int
+    source_bytes: int
+    payload_bytes: int
+    nested: bool = False
+    absmax2: Optional[torch.Tensor] = None
+    code2: Optional[torch.Tensor] = None
+    offset: Optional[torch.Tensor] = None
+    blocksize2: int = 256
+
+    def quant_state(self, device=None, absmax=None, absmax2=None, code=None, code2=None, offset=None) -> QuantState:
+        """QuantState over this payload (or over device copies of its tensors)."""
+        dev = lambda t: t if device is None else t.to(device, non_blocking=True)  # noqa: E731
+        if self.nested:
+            state2 = QuantState(absmax=absmax2 if absmax2 is not None else dev(self.absmax2),
+                                code=code2 if code2 is not None else dev(self.code2), blocksize=self.blocksize2,
+                                dtype=torch.float32)
+            return QuantState(absmax if absmax is not None else dev(self.absmax), self.shape,
+                              code if code is not None else dev(self.code), self.blocksize, self.quant_type,
+                              self.dtype, offset=offset if offset is not None else dev(self.offset), state2=state2)
+        return QuantState(absmax if absmax is not None else dev(self.absmax), self.shape,
+                          code if code is not None else dev(self.code), self.blocksize, self.quant_type, self.dtype)
+
+    def host_tensors(self) -> list[torch.Tensor]:
+        ts = [self.quantized, self.absmax, self.code]
+        if self.nested:
+            ts += [self.absmax2, self.code2, self.offset.reshape(1)]
+        return ts
+
+
+@dataclass
+class FP16StagedPayload:
+    """Frozen 16-bit weight kept pinned on the host for per-step upload (stratum/upload.py:98-108)."""
+
+    data: torch.Tensor
+    shape: tuple
+    dtype: torch.dtype
+    source_bytes: int
+
+
+# --------------------------------------------------------------------------------
+# owner bookkeeping
+# --------------------------------------------------------------------------------
+
+def _replace_param_data(param: nn.Parameter, new_data: torch.Tensor, owner: Optional[nn.Module] = None,
+                        pname: Optional[str] = None) -> None:
+    """Set ``param.data``; re-register the parameter when a subclass rejects it
+    (reference: stratum/upload.py:1286-1310)."""
+    try:
+        param.data = new_data
+        return
+    except (RuntimeError, TypeError):
+        pass
+    if owner is not None and pname is not None:
+        new_param = nn.Parameter(new_data, requires_grad=param.requires_grad)
+        for attr in (NF4_ATTR, FP16_ATTR):
+            if hasattr(param, attr):
+                setattr(new_param, attr, getattr(param, attr))
+        owner.register_parameter(pname, new_param)
+
+
+def _build_param_owner_map(module: nn.Module) -> dict[int, tuple[nn.Module, str]]:
+    pmap: dict[int, tuple[nn.Module, str]] = {}
+    for _, sub in module.named_modules():
+        for pname, p in sub.named_parameters(recurse=False):
+            pmap[id(p)] = (sub, pname)
+    return pmap
+
+
+def _fused_owner(owner: Optional[nn.Module], pname: Optional[str]):
+    """The NF4Linear that consumes this parameter's payload directly, if any."""
+    from .nf4_linear import NF4Linear
+
+    if isinstance(owner, NF4Linear) and pname == "weight" and owner.streamed:
+        return owner
+    return None
+
+
+# --------------------------------------------------------------------------------
+# cache (reference format v1, plus v2 with double-quant fields)
+# --------------------------------------------------------------------------------
+
+def _canonical_param_name(name: str) -> str:
+    return name.replace(".module.", ".")
+
+
+def _cache_path(cache_dir: Path, name: str) -> Path:
+    """``<sha1[:12]>-<sanitised name>.pt`` (reference naming, stratum/upload.py:236-240)."""
+    name = _canonical_param_name(name)
+    safe = re.sub(r"[^A-Za-z0-9_.-]+", "_", name)[-160:]
+    digest = hashlib.sha1(name.encode("utf-8")).hexdigest()[:12]
+    return cache_dir / f"{digest}-{safe}.pt"
+
+
+def _load_payload_from_cache(path: Path, param: nn.Parameter, *, blocksize: int, quant_type: str,
+                             compress_statistics: bool = False) -> Optional[NF4Payload]:
+    """Load a cached payload; ``None`` on a missing file, an unreadable file or
+    any metadata mismatch (reference: stratum/upload.py:243-284)."""
+    if not path.exists():
+        return None
+    try:
+        obj = torch.load(path, map_location="cpu", weights_only=False)
+    except Exception:
+        return None
+    if not isinstance(obj, dict) or obj.get("version") not in (1, 2):
+        return None
+    expected = {
+        "shape": tuple(param.shape),
+        "dtype": _dtype_name(param.dtype),
+        "blocksize": int(blocksize),
+        "quant_type": str(quant_type),
+        "source_numel": int(param.numel()),
+        "source_bytes": int(param.numel() * param.element_size()),
+    }
+    for key, value in expected.items():
+        got = obj.get(key)
+        if key == "shape" and got is not None:
+            got = tuple(got)
+        if got != value:
+            return None
+    nested = bool(obj.get("nested", False))
+    if nested != bool(compress_statistics):
+        return None
+    quantized = cast(torch.Tensor, obj["quantized"])
+    absmax = cast(torch.Tensor, obj["absmax"])
+    code = cast(torch.Tensor, obj["code"])
+    extra = {}
+    if nested:
+        extra = dict(nested=True, absmax2=_pin_cpu(obj["absmax2"]), code2=_pin_cpu(obj["code2"]),
+                     offset=_pin_cpu(obj["offset"].reshape(())), blocksize2=int(obj.get("blocksize2", 256)))
+    return NF4Payload(
+        quantized=_pin_cpu(quantized), absmax=_pin_cpu(absmax), code=_pin_cpu(code), shape=tuple(obj["shape"]),
+        dtype=_dtype_from_name(str(obj["dtype"])), blocksize=int(obj["blocksize"]),
+        quant_type=str(obj["quant_type"]), source_numel=int(obj["source_numel"]),
+        source_bytes=int(obj["source_bytes"]),
+        payload_bytes=_payload_bytes(quantized, absmax, code, obj.get("absmax2"), obj.get("code2")), **extra)
+
+
+def _save_payload_to_cache(path: Path, payload: NF4Payload) -> None:
+    """Atomic write (tmp file, then replace): version 1 unless the payload is nested."""
+    path.parent.mkdir(parents=True, exist_ok=True)
+    tmp = path.with_name(f"{path.name}.tmp")
+    obj = {
+        "version": 2 if payload.nested else 1,
+        "shape": tuple(payload.shape),
+        "dtype": _dtype_name(payload.dtype),
+        "blocksize": int(payload.blocksize),
+        "quant_type": str(payload.quant_type),
+        "source_numel": int(payload.source_numel),
+        "source_bytes": int(payload.source_bytes),
+        "quantized": payload.quantized.detach().contiguous().cpu(),
+        "absmax": payload.absmax.detach().contiguous().cpu(),
+        "code": payload.code.detach().contiguous().cpu(),
+    }
+    if payload.nested:
+        obj.update(nested=True, absmax2=payload.absmax2.detach().cpu(), code2=payload.code2.detach().cpu(),
+                   offset=payload.offset.detach().cpu(), blocksize2=int(payload.blocksize2))
+    torch.save(obj, tmp)
+    tmp.replace(path)
+
+
+# --------------------------------------------------------------------------------
+# phase 1: quantize
+# --------------------------------------------------------------------------------
+
+def _quantize_param(weight: torch.Tensor, blocksize: int, quant_type: str, compress_statistics: bool,
+                    orig_shape: tuple, source_bytes: int, device) -> NF4Payload:
+    w = weight.detach().contiguous()
+    if w.ndim > 2:  # stacked expert weights [E, A, B] -> [-1, last] (stratum/upload.py:361-366)
+        w = w.reshape(-1, w.shape[-1])
+    dev = torch.device(device) if device is not None else (
+        w.device if w.device.type == "cuda" else torch.device("cuda", torch.cuda.current_device()))
+    wd = w.to(dev, non_blocking=True)
+    packed, qs = F.quantize_4bit(wd, blocksize=blocksize, compress_statistics=compress_statistics,
+                                 quant_type=quant_type)
+    torch.cuda.current_stream(dev).synchronize()
+    kw = {}
+    if qs.nested:
+        kw = dict(nested=True, absmax2=_pin_cpu(qs.state2.absmax), code2=_pin_cpu(qs.state2.code),
+                  offset=_pin_cpu(qs.offset.reshape(())), blocksize2=int(qs.state2.blocksize))
+    pq, pa, pc = _pin_cpu(packed), _pin_cpu(qs.absmax), _pin_cpu(qs.code)
+    return NF4Payload(
+        quantized=pq, absmax=pa, code=pc, shape=tuple(orig_shape), dtype=qs.dtype, blocksize=int(qs.blocksize),
+        quant_type=str(qs.quant_type), source_numel=int(weight.numel()), source_bytes=int(source_bytes),
+        payload_bytes=_payload_bytes(pq, pa, pc, kw.get("absmax2"), kw.get("code2")), **kw)
+
+
+@torch.no_grad()
+def prepare_nf4(
+    module: nn.Module,
+    *,
+    min_numel: int = 4096,
+    cache_dir: Optional[Path | str] = None,
+    verbose: bool = True,
+    blocksize: int = 64,
+    quant_type: str = "nf4",
+    compress_statistics: bool = False,
+    device=None,
+) -> NF4Stats:
+    """Quantize frozen >= 2-D parameters to NF4, attach payloads, drop the originals.
+
+    Reference: stratum/upload.py:305-398 (same selection rules: frozen, ndim
+    >= 2, numel >= ``min_numel``, fp16/bf16/fp32; 3-D stacked experts are
+    quantized as ``[-1, last]`` and keep their original ``payload.shape``).
+    Quantization runs on a CUDA device (``device`` or the current one); the
+    reference quantizes on the CPU through bitsandbytes.
+    ``compress_statistics=True`` adds 8-bit double quantization of the absmax.
+    """
+    stats = NF4Stats()
+    for name, param in module.named_parameters():
+        if param.requires_grad or param.ndim < 2 or param.numel() < min_numel:
+            continue
+        if param.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+            continue
+        if hasattr(param, NF4_ATTR):
+            payload = cast(NF4Payload, getattr(param, NF4_ATTR))
+            stats.tensors += 1
+            stats.source_bytes += payload.source_bytes
+            stats.payload_bytes += payload.payload_bytes
+            continue
+        cache_path = _cache_path(Path(cache_dir), name) if cache_dir else None
+        payload = (_load_payload_from_cache(cache_path, param, blocksize=blocksize, quant_type=quant_type,
+                                            compress_statistics=compress_statistics)
+                   if cache_path is not None else None)
+        if payload is not None:
+            stats.cache_hits += 1
+        else:
+            if cache_path is not None:
+                stats.cache_misses += 1
+            payload = _quantize_param(param.data, blocksize, quant_type, compress_statistics, tuple(param.shape),
+                                      param.numel() * param.element_size(), device)
+            if cache_path is not None:
+                _save_payload_to_cache(cache_path, payload)
+                stats.cache_writes += 1
+        setattr(param, NF4_ATTR, payload)
+        param.data = torch.empty(0, dtype=payload.dtype, device=param.device)
+        stats.tensors += 1
+        stats.source_bytes += payload.source_bytes
+        stats.payload_bytes += payload.payload_bytes
+    if verbose:
+        print(f"  nf4 total: {stats.tensors} tensors, {stats.source_bytes / 1024**3:.2f} GiB -> "
+              f"{stats.payload_bytes / 1024**3:.2f} GiB payload (compression {stats.compression:.2f}x, "
+              f"cache hits={stats.cache_hits} misses={stats.cache_misses} writes={stats.cache_writes})", flush=True)
+    return stats
+
+
+@torch.no_grad()
+def prepare_nf4_from_cache(module: nn.Module, cache_dir: Path | str, *, min_numel: int = 4096,
+                           blocksize: int = 64, quant_type: str = "nf4", verbose: bool = True) -> NF4Stats:
+    """Attach cached payloads only (no quantization); parameters without a valid
+    cache entry are left untouched (reference: stratum/upload.py:1207-1283)."""
+    stats = NF4Stats()
+    for name, param in module.named_parameters():
+        if param.requires_grad or param.ndim < 2 or param.numel() < min_numel or hasattr(param, NF4_ATTR):
+            continue
+        path = _cache_path(Path(cache_dir), name)
+        payload = _load_payload_from_cache(path, param, blocksize=blocksize, quant_type=quant_type)
+        if payload is None:
+            payload = _load_payload_from_cache(path, param, blocksize=blocksize, quant_type=quant_type,
+                                               compress_statistics=True)
+        if payload is None:
+            stats.cache_misses += 1
+            continue
+        stats.cache_hits += 1
+        setattr(param, NF4_ATTR, payload)
+        param.data = torch.empty(0, dtype=payload.dtype, device=param.device)
+        stats.tensors += 1
+        stats.source_bytes += payload.source_bytes
+        stats.payload_bytes += payload.payload_bytes
+    if verbose:
+        print(f"  nf4 from cache: {stats.tensors} tensors (hits={stats.cache_hits} misses={stats.cache_misses})",
+              flush=True)
+    return stats
+
+
+@torch.no_grad()
+def prepare_fp16_staged(module: nn.Module, *, min_numel: int = 4096, verbose: bool = True) -> int:
+    """Pin frozen params for per-step 16-bit upload (reference: stratum/upload.py:111-160)."""
+    count = 0
+    for _, param in module.named_parameters():
+        if param.requires_grad or param.numel() < min_numel or param.ndim < 2:
+            continue
+        if hasattr(param, NF4_ATTR) or hasattr(param, FP16_ATTR):
+            continue
+        if param.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+            continue
+        payload = FP16StagedPayload(data=_pin_cpu(param.data), shape=tuple(param.shape), dtype=param.dtype,
+                                    source_bytes=param.numel() * param.element_size())
+        setattr(param, FP16_ATTR, payload)
+        param.data = torch.empty(0, dtype=param.dtype, device=param.device)
+        count += 1
+    if verbose:
+        total = sum(getattr(p, FP16_ATTR).source_bytes for p in module.parameters() if hasattr(p, FP16_ATTR))
+        print(f"  fp16 staged: {count} tensors, {total / 1024**3:.2f} GiB to upload per step", flush=True)
+    return count
+
+
+@torch.no_grad()
+def estimate_module_upload_gib(module: nn.Module) -> float:
+    """GB (1e9) a module occupies once materialised (reference: stratum/upload.py:401-422)."""
+    total, seen = 0, set()
+    for p in module.parameters():
+        if id(p) in seen:
+            continue
+        seen.add(id(p))
+        payload = getattr(p, NF4_ATTR, None)
+        total += payload.source_bytes if payload is not None else p.numel() * p.element_size()
+        if p.grad is not None:
+            total += p.grad.numel() * p.grad.element_size()
+    for b in module.buffers():
+        total += b.numel() * b.element_size()
+    return total / 10**9
+
+
+# --------------------------------------------------------------------------------
+# coalesced per-layer arena
+# --------------------------------------------------------------------------------
+
+_ALIGN = 256
+
+
+@dataclass
+class LayerArena:
+    """All NF4 payload tensors of one module in one pinned buffer (one H2D copy per layer)."""
+
+    host: torch.Tensor                                   # pinned uint8
+    slots: dict = field(default_factory=dict)           # (param id, index) -> (offset, nbytes, dtype, shape)
+
+    def views(self, dev_buf: torch.Tensor, pid: int, n: int) -> list[torch.Tensor]:
+        out = []
+        for i in range(n):
+            off, nbytes, dtype, shape = self.slots[(pid, i)]
+            out.append(dev_buf[off:off + nbytes].view(dtype).view(shape))
+        return out
+
+
+def build_layer_arena(module: nn.Module) -> Optional[LayerArena]:
+    """Coalesce every NF4 payload under ``module`` into one pinned arena (256-B aligned slots)."""
+    items = []
+    for p in module.parameters():
+        payload = getattr(p, NF4_ATTR, None)
+        if payload is not None:
+            items.append((p, payload.host_tensors()))
+    if not items:
+        return None
+    offset = 0
+    slots = {}
+    for p, ts in items:
+        for i, t in enumerate(ts):
+            nbytes = t.numel() * t.element_size()
+            slots[(id(p), i)] = (offset, nbytes, t.dtype, tuple(t.shape))
+            offset += (nbytes + _ALIGN - 1) // _ALIGN * _ALIGN
+    host = torch.empty(max(offset, _ALIGN), dtype=torch.uint8, pin_memory=torch.cuda.is_available())
+    for p, ts in items:
+        for i, t in enumerate(ts):
+            off, nbytes, _, _ = slots[(id(p), i)]
+            host[off:off + nbytes].copy_(t.contiguous().view(-1).view(torch.uint8))
+    arena = LayerArena(host=host, slots=slots)
+    setattr(module, ARENA_ATTR, arena)
+    return arena
+
+
+# --------------------------------------------------------------------------------
+# phase 2: upload / free
+# --------------------------------------------------------------------------------
+
+def _materialize(param, payload: NF4Payload, dev_tensors: list[torch.Tensor], owner, pname, device) -> None:
+    """Make an uploaded payload usable: fused owner -> NF4 state, else dequantize into param.data."""
+    q, a, c = dev_tensors[0], dev_tensors[1], dev_tensors[2]
+    if payload.nested:
+        qs = payload.quant_state(absmax=a, code=c, absmax2=dev_tensors[3], code2=dev_tensors[4],
+                                 offset=dev_tensors[5].reshape(()))
+    else:
+        qs = payload.quant_state(absmax=a, code=c)
+    fused = _fused_owner(owner, pname)
+    if fused is not None:
+        fused.load_device_state(q, qs)
+        return
+    _replace_param_data(param, F.dequantize_4bit(q, qs).contiguous(), owner=owner, pname=pname)
+
+
+def _device(device_id) -> torch.device:
+    return device_id if isinstance(device_id, torch.device) else torch.device(f"cuda:{int(device_id)}")
+
+
+def _is_resident(param, payload, owner, pname, device) -> bool:
+    fused = _fused_owner(owner, pname)
+    if fused is not None:
+        return fused.device_state_on(device)
+    return param.data.numel() > 0 and param.data.device == device
+
+
+@torch.no_grad()
+def ensure_weights(module: nn.Module, device_id: int) -> int:
+    """Upload NF4 payloads (and move other params/buffers) for *module* to ``cuda:device_id``.
+
+    Reference: stratum/upload.py:969-1069.  Issues its copies and kernels on
+    the current stream.  Returns the number of tensors made resident.
+    """
+    device = _device(device_id)
+    owner_map = _build_param_owner_map(module)
+    arena: Optional[LayerArena] = getattr(module, ARENA_ATTR, None)
+    arena_dev = None
+    tensors = 0
+    for name, param in module.named_parameters():
+        owner, pname = owner_map.get(id(param), (None, None))
+        fp16 = getattr(param, FP16_ATTR, None)
+        if fp16 is not None:
+            if param.data.numel() > 0 and param.data.device == device:
+                continue
+            dst = torch.empty(fp16.shape, dtype=fp16.dtype, device=device)
+            dst.copy_(fp16.data, non_blocking=True)
+            param.data = dst
+            tensors += 1
+            continue
+        payload = getattr(param, NF4_ATTR, None)
+        if payload is None:
+            if param.data.numel() > 0 and param.data.device != device:
+                if param.requires_grad:
+                    raise RuntimeError(
+                        f"trainable shared parameter {name!r} is on {param.data.device}, but module is running on "
+                        f"{device}; Stratum cannot safely move trainable parameters between stages")
+                param.data = param.data.to(device, non_blocking=True)
+                tensors += 1
+            continue
+        if _is_resident(param, payload, owner, pname, device):
+            continue
+        if device.type != "cuda":
+            raise RuntimeError(f"ensure_weights: NF4 payloads need a CUDA device, got {device}")
+        if arena is not None:
+            if arena_dev is None:
+                arena_dev = torch.empty(arena.host.numel(), dtype=torch.uint8, device=device)
+                arena_dev.copy_(arena.host, non_blocking=True)
+            dev_tensors = arena.views(arena_dev, id(param), len(payload.host_tensors()))
+        else:
+            dev_tensors = [t.to(device, non_blocking=True) for t in payload.host_tensors()]
+        _materialize(param, payload, dev_tensors, owner, pname, device)
+        tensors += 1
+    for buf in module.buffers():
+        if buf.device != device and buf.device.type != "meta":
+            buf.data = buf.data.to(device, non_blocking=True)
+            tensors += 1
+    return tensors
+
+
+@dataclass
+class _PrefetchEntry:
+    param: nn.Parameter
+    payload: NF4Payload
+    tensors: list
+    owner: Optional[nn.Module] = None
+    pname: Optional[str] = None
+
+
+@dataclass
+class NF4Prefetch:
+    """Pending asynchronous NF4 upload for one module (reference: stratum/upload.py:163-228).
+
+    ``finalize()`` makes the current stream wait for the copy event and then
+    materialises every entry (fused state or dequantized ``param.data``).
+    """
+
+    entries: list
+    device: torch.device
+    stream: Optional["torch.cuda.Stream"] = None
+    event: Optional["torch.cuda.Event"] = None
+    arena_buffer: Optional[torch.Tensor] = None
+
+    def finalize(self) -> int:
+        if not self.entries:
+            return 0
+        if self.device.type != "cuda" or not torch.cuda.is_available():
+            raise RuntimeError(f"CUDA is not available for NF4 prefetch finalize on {self.device}")
+        current = torch.cuda.current_stream(device=self.device)
+        if self.event is not None:
+            current.wait_event(self.event)
+        n = 0
+        with torch.cuda.device(self.device), torch.no_grad():
+            if self.arena_buffer is not None:
+                self.arena_buffer.record_stream(current)
+            for e in self.entries:
+                for t in e.tensors:
+                    t.record_stream(current)
+                if _is_resident(e.param, e.payload, e.owner, e.pname, self.device):
+                    continue
+                _materialize(e.param, e.payload, e.tensors, e.owner, e.pname, self.device)
+                n += 1
+        self.entries = []
+        return n
+
+    def wait(self) -> int:
+        return self.finalize()
+
+
+@torch.no_grad()
+def prefetch_weights(module: nn.Module, device_id: int, stream: Optional["torch.cuda.Stream"] = None) -> NF4Prefetch:
+    """Start the H2D copies of *module*'s NF4 payloads on a side stream (reference:
+    stratum/upload.py:1072-1125).  Nothing is mutated until :meth:`NF4Prefetch.finalize`."""
+    device = _device(device_id)
+    owner_map = _build_param_owner_map(module)
+    todo = []
+    for _, param in module.named_parameters():
+        payload = getattr(param, NF4_ATTR, None)
+        if payload is None:
+            continue
+        owner, pname = owner_map.get(id(param), (None, None))
+        if _is_resident(param, payload, owner, pname, device):
+            continue
+        todo.append((param, payload, owner, pname))
+    if not todo:
+        return NF4Prefetch([], device)
+    if device.type != "cuda" or not torch.cuda.is_available():
+        raise RuntimeError(f"CUDA is not available for NF4 prefetch to {device}")
+    stream = stream or torch.cuda.Stream(device=device)
+    arena: Optional[LayerArena] = getattr(module, ARENA_ATTR, None)
+    entries = []
+    buf = None
+    with torch.cuda.device(device), torch.cuda.stream(stream):
+        if arena is not None:
+            buf = torch.empty(arena.host.numel(), dtype=torch.uint8, device=device)
+            buf.copy_(arena.host, non_blocking=True)
+        for param, payload, owner, pname in todo:
+            n = len(payload.host_tensors())
+            ts = (arena.views(buf, id(param), n) if arena is not None
+                  else [t.to(device, non_blocking=True) for t in payload.host_tensors()])
+            entries.append(_PrefetchEntry(param, payload, ts, owner, pname))
+        event = torch.cuda.Event()
+        stream.record_event(event)
+    return NF4Prefetch(entries, device=device, stream=stream, event=event, arena_buffer=buf)
+
+
+@torch.no_grad()
+def ensure_prefetched_weights(module: nn.Module, device_id: int, prefetch: Optional[NF4Prefetch]) -> int:
+    """Finalize a matching prefetch, then ensure the rest (reference: stratum/upload.py:1128-1141)."""
+    if prefetch is None:
+        return ensure_weights(module, device_id)
+    if prefetch.device != _device(device_id):
+        raise ValueError(f"prefetch device {prefetch.device} does not match cuda:{device_id}")
+    return prefetch.finalize() + ensure_weights(module, device_id)
+
+
+@torch.no_grad()
+def free_weights(module: nn.Module) -> int:
+    """Drop the device copies of NF4 / FP16-staged params (reference: stratum/upload.py:1144-1159)."""
+    owner_map = _build_param_owner_map(module)
+    tensors = 0
+    for _, param in module.named_parameters():
+        if not hasattr(param, NF4_ATTR) and not hasattr(param, FP16_ATTR):
+            continue
+        owner, pname = owner_map.get(id(param), (None, None))
+        fused = _fused_owner(owner, pname) if hasattr(param, NF4_ATTR) else None
+        if fused is not None:
+            if fused.drop_device_state():
+                tensors += 1
+            continue
+        if param.data.numel() == 0:
+            continue
+        param.data = torch.empty(0, dtype=param.dtype, device=param.device)
+        tensors += 1
+    return tensors
+
+
+@torch.no_grad()
+def upload_stream(module: nn.Module, device_id: int, *, verbose: bool = True) -> int:
+    """Synchronous permanent upload of a whole module (reference: stratum/upload.py:907-966)."""
+    t0 = time.time()
+    n = ensure_weights(module, device_id)
+    torch.cuda.current_stream(_device(device_id)).synchronize()
+    if verbose:
+        print(f"  device {device_id}: {n} tensors in {time.time() - t0:.1f}s", flush=True)
+    return n
+
+
+@torch.no_grad()
+def snapshot_module_buffers(module: nn.Module) -> dict[str, torch.Tensor]:
+    """Copies of every buffer, for restoring after a recompute (stratum/upload.py:1162-1180)."""
+    return {name: b.detach().clone() for name, b in module.named_buffers()}
+
+
+@torch.no_grad()
+def restore_module_buffers(module: nn.Module, snapshot: dict[str, torch.Tensor]) -> int:
+    n = 0
+    for name, b in module.named_buffers():
+        if name in snapshot:
+            b.copy_(snapshot[name].to(b.device))
+            n += 1
+    return n
+
+
+# --------------------------------------------------------------------------------
+# fused mode: nn.Linear -> NF4Linear
+# --------------------------------------------------------------------------------
+
+@torch.no_grad()
+def to_nf4_linear(module: nn.Module, *, lora_r: int = 0, lora_alpha: float = 16.0,
+                  lora_dtype: torch.dtype = torch.bfloat16, target: Optional[callable] = None,
+                  lora_device=None) -> int:
+    """Replace every ``nn.Linear`` child whose frozen weight carries an NF4 payload
+    by a streamed :class:`NF4Linear` (fused mode).  With ``lora_r > 0`` each gets a
+    PEFT-style adapter.  Returns the number of layers converted."""
+    from .nf4_linear import NF4Linear
+
+    count = 0
+    for parent_name, parent in list(module.named_modules()):
+        for cname, child in list(parent.named_children()):
+            if not isinstance(child, nn.Linear):
+                continue
+            payload = getattr(child.weight, NF4_ATTR, None)
+            if payload is None or len(payload.shape) != 2:
+                continue
+            full = f"{parent_name}.{cname}" if parent_name else cname
+            if target is not None and not target(full):
+                continue
+            new = NF4Linear.streamed_from(child.weight, payload, bias=child.bias)
+            if lora_r > 0:
+                new.attach_lora(lora_r, lora_alpha, dtype=lora_dtype,
+                                device=lora_device if lora_device is not None else torch.device("cpu"))
+            setattr(parent, cname, new)
+            count += 1
+    return count
