@@ -314,6 +314,9 @@ def run_codec(args, world, rank, local):
     e2e = run_codec_e2e(args, wl, world)
     cpu = run_cpu_baseline_codec() if (world == 1 and rank == 0 and not args.no_cpu_baseline) else None
     clk = clocks.summary()
+    del wl
+    torch.cuda.empty_cache()
+    lin = None if args.no_linear else run_linear_metrics(args, world, flush)
     return {
         "metric": "nf4_dequant_GBps",
         "value": round(value, 1),
@@ -339,6 +342,7 @@ def run_codec(args, world, rank, local):
         "gpu_launches": int(dq_launches) * args.steps,
         "wall_s_timed": round(t_wall, 4),
         "clocks": clk,
+        "nf4_linear": lin,
     }
 
 
@@ -351,62 +355,75 @@ LINEAR_ALPHA = 128
 
 
 class LinearWorkload:
-    """Fused NF4 linear forward (+ LoRA r=64) at the config-5 micro-benchmark shapes."""
+    """NF4Linear forward + backward with LoRA r=64 at the config-5 micro-benchmark shapes.
+
+    One step, per weight: xa = s x A^T (cuBLAS), y = fused NF4 GEMM(x, W) + xa B^T,
+    dyb = s dy B (cuBLAS), dx = fused NF4 dX(dy, W) + dyb A, dA = dyb^T x, dB = dy^T xa
+    (cuBLAS) -- exactly the launches NF4Linear's autograd makes.
+    """
 
     def __init__(self, device, T=LINEAR_T):
         from stratum_b200 import functional as F
         from stratum_b200 import ops
 
         self.F, self.ops, self.device, self.T = F, ops, device, T
+        self.scaling = LINEAR_ALPHA / LINEAR_RANK
         g = torch.Generator(device=device).manual_seed(0)
         self.items = []
         for N, K in LINEAR_SHAPES:
             w = (torch.randn(N, K, generator=g, device=device) * 0.02).to(torch.float16)
             packed, qs = F.quantize_4bit(w)
             x = torch.randn(T, K, generator=g, device=device).to(torch.bfloat16)
+            dy = torch.randn(T, N, generator=g, device=device).to(torch.bfloat16)
             A = ((torch.rand(LINEAR_RANK, K, generator=g, device=device) * 2 - 1) / K**0.5).to(torch.bfloat16)
             B = (torch.randn(N, LINEAR_RANK, generator=g, device=device) * 0.01).to(torch.bfloat16)
-            xa = ops.lora_down(x, A, LINEAR_ALPHA / LINEAR_RANK)
-            self.items.append(dict(N=N, K=K, packed=packed, qs=qs, x=x, A=A, B=B, xa=xa,
+            self.items.append(dict(N=N, K=K, packed=packed, qs=qs, x=x, dy=dy, A=A, B=B,
                                    wbuf=torch.empty(N, K, dtype=torch.bfloat16, device=device)))
-        self.flops_main = sum(2.0 * T * it["N"] * it["K"] for it in self.items)
-        self.flops_lora = sum(2.0 * T * LINEAR_RANK * it["N"] for it in self.items)
+        r = LINEAR_RANK
+        self.flops_main = sum(4.0 * T * it["N"] * it["K"] for it in self.items)  # fwd + dX
+        self.flops_lora = sum(2.0 * T * r * (it["K"] + it["N"]) * 3 for it in self.items)  # fwd, dX, dA/dB
 
-    def fused_step(self, events=None):
+    def step(self, events=None):
+        ops, s = self.ops, self.scaling
         for it in self.items:
-            if events is not None:
-                e0 = torch.cuda.Event(enable_timing=True, external=True)
-                e1 = torch.cuda.Event(enable_timing=True, external=True)
-            # the LoRA down-projection (cuBLAS) runs inside the step; only the fused kernel is bracketed
-            xa = self.ops.lora_down(it["x"], it["A"], LINEAR_ALPHA / LINEAR_RANK)
-            if events is not None:
-                e0.record()
-            self.ops.nf4_gemm_fwd(it["x"], it["packed"], it["qs"], lora_A=it["A"], lora_B=it["B"],
-                                  scaling=LINEAR_ALPHA / LINEAR_RANK, xa=xa)
-            if events is not None:
-                e1.record()
-                events.append((it["N"], it["K"], e0, e1))
+            ev = lambda: torch.cuda.Event(enable_timing=True, external=True)  # noqa: E731
+            xa = ops.lora_down(it["x"], it["A"], s)
+            e0 = ev() if events is not None else None
+            if e0: e0.record()
+            y = ops.nf4_gemm_fwd(it["x"], it["packed"], it["qs"], lora_A=it["A"], lora_B=it["B"], scaling=s, xa=xa)
+            if e0:
+                e1 = ev(); e1.record(); events.append(("fwd", it["N"], it["K"], e0, e1))
+            dyb = ops.lora_down(it["dy"], it["B"].t(), s)
+            e0 = ev() if events is not None else None
+            if e0: e0.record()
+            dx = ops.nf4_gemm_dx(it["dy"], it["packed"], it["qs"], lora_A=it["A"], lora_B=it["B"], scaling=s, dyb=dyb)
+            if e0:
+                e1 = ev(); e1.record(); events.append(("dx", it["N"], it["K"], e0, e1))
+            dA = dyb[:, :LINEAR_RANK].t() @ it["x"]
+            dB = it["dy"].t() @ xa[:, :LINEAR_RANK]
+            del y, dx, dA, dB
 
     def unfused_step(self):
-        """Reference GPU path: dequantize to bf16, then cuBLAS (the reference's K2 + K3)."""
+        """Reference GPU path: dequantize to bf16, then cuBLAS forward and dX (the reference's K2 + K3)."""
         for it in self.items:
             self.F.dequantize_4bit(it["packed"], it["qs"], out=it["wbuf"], out_dtype=torch.bfloat16)
             torch.matmul(it["x"], it["wbuf"].t())
+            torch.matmul(it["dy"], it["wbuf"])
 
 
-def run_linear(args, world, rank, local):
+def run_linear_metrics(args, world, flush, clocks_ctx=True):
+    """Time LinearWorkload steps (CUDA-graph replays); returns a dict of results."""
     dev = torch.device("cuda", torch.cuda.current_device())
     wl = LinearWorkload(dev)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     ev = []
-    g_f, _, launches = capture(lambda: (ev.clear(), wl.fused_step(ev)))
+    g_f, _, launches = capture(lambda: (ev.clear(), wl.step(ev)))
     g_u, _, _ = capture(wl.unfused_step)
     for _ in range(args.warmup):
         g_f.replay()
         g_u.replay()
     torch.cuda.synchronize()
 
-    def timed(graph, n):
+    def timed(graph, n, collect=None):
         out = []
         for _ in range(n):
             flush.fill_(1)
@@ -417,56 +434,64 @@ def run_linear(args, world, rank, local):
             e1.record()
             e1.synchronize()
             out.append(e0.elapsed_time(e1))
+            if collect is not None:
+                collect += [(k, n_, k_, a.elapsed_time(b)) for k, n_, k_, a, b in ev]
         return out
 
     barrier(world)
     torch.cuda.synchronize()
     kern = []
+    nsteps = max(3, min(args.steps, 30))
     with ClockSampler(dev.index) as clocks:
-        step_ms = []
-        for _ in range(args.steps):
-            step_ms += timed(g_f, 1)
-            kern += [(n, k, a.elapsed_time(b)) for n, k, a, b in ev]
+        step_ms = timed(g_f, nsteps, kern)
         torch.cuda.synchronize()
         barrier(world)
-        base_ms = timed(g_u, max(3, args.steps // 4))
+        base_ms = timed(g_u, max(3, nsteps // 3))
     ms = max_over_ranks(statistics.mean(step_ms), world)
     flops = wl.flops_main + wl.flops_lora
-    value = flops * world / (ms * 1e-3) / 1e12
     peaks = load_peaks()
-    # dominant kernel: the fused GEMM launches (both shapes)
-    kflops = sum(2.0 * LINEAR_T * n * k for n, k, _ in kern)
-    kms = sum(t for _, _, t in kern)
+    per = {}
+    for kind in ("fwd", "dx"):
+        for N, K in LINEAR_SHAPES:
+            ts = [t for k, n, kk, t in kern if k == kind and n == N and kk == K]
+            per[f"{kind} {N}x{K}"] = round(2.0 * LINEAR_T * N * K / (statistics.mean(ts) * 1e-3) / 1e12, 1)
+    kflops = sum(2.0 * LINEAR_T * n * k for _, n, k, _ in kern)
+    kms = sum(t for _, _, _, t in kern)
     achieved = kflops / (kms * 1e-3) / 1e12
-    per_shape = {}
-    for N, K in LINEAR_SHAPES:
-        ts = [t for n, k, t in kern if n == N and k == K]
-        per_shape[f"{N}x{K}"] = round(2.0 * LINEAR_T * N * K / (statistics.mean(ts) * 1e-3) / 1e12, 1)
     base = statistics.mean(base_ms)
     return {
-        "metric": "nf4_linear_fwd_TFLOPs",
-        "value": round(value, 1),
+        "metric": "nf4_linear_fwd_bwd_TFLOPs",
+        "value": round(flops * world / (ms * 1e-3) / 1e12, 1),
         "unit": "TFLOP/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "bf16 (NF4 weights)",
-        "data": "synthetic: W ~N(0,0.02) fp16 -> NF4 bs64, x ~N(0,1) bf16, LoRA r=64 alpha=128",
-        "config": {"workload": f"fused NF4 linear forward + LoRA, T={LINEAR_T}, weights 14336x4096 and 4096x14336",
-                   "parallelism": f"replicas x{world}", "l2": "256 MiB fill between timed steps"},
-        "roofline": {"bound": "tensor", "kernel": "k_nf4_gemm_fwd<bf16>", "achieved": round(achieved, 1),
+        "workload": f"NF4Linear fwd+bwd (fused fwd, fused dX, LoRA r={LINEAR_RANK} grads), T={LINEAR_T}, "
+                    "weights 14336x4096 and 4096x14336, bf16 activations",
+        "roofline": {"bound": "tensor", "kernel": "k_nf4_gemm_fwd + k_nf4_gemm_dx", "achieved": round(achieved, 1),
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      "frac_of": peaks["source"], "frac_nominal_2250": round(achieved / 2250.0, 4),
-                     "per_shape_TFLOPs": per_shape, "traffic": None},
-        "gpu_reference_path": {"what": "dequantize_4bit -> bf16 + cuBLAS matmul (no LoRA)",
+                     "per_kernel_TFLOPs": per, "traffic": None},
+        "gpu_reference_path": {"what": "dequantize_4bit -> bf16, cuBLAS forward + cuBLAS dX (no LoRA)",
                                "TFLOPs": round(wl.flops_main / (base * 1e-3) / 1e12, 1), "ms_per_step": round(base, 4)},
-        "gpu_launches": int(launches) * args.steps,
+        "gpu_launches_per_step": int(launches),
         "clocks": clocks.summary(),
     }
+
+
+def run_linear(args, world, rank, local):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    r = run_linear_metrics(args, world, flush)
+    out = {
+        "metric": r["metric"], "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (NF4 weights)",
+        "data": "synthetic: W ~N(0,0.02) fp16 -> NF4 bs64, x, dY ~N(0,1) bf16, LoRA r=64 alpha=128",
+        "config": {"workload": r["workload"], "parallelism": f"replicas x{world}",
+                   "l2": "256 MiB fill between timed steps"},
+        "roofline": r["roofline"], "gpu_reference_path": r["gpu_reference_path"],
+        "gpu_launches": r["gpu_launches_per_step"] * args.steps, "clocks": r["clocks"],
+    }
+    return out
 
 
 def run_codec_e2e(args, wl, world):
@@ -613,6 +638,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("codec", "linear"), default="codec")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-linear", action="store_true", help="skip the NF4Linear fwd+bwd section of the codec run")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
