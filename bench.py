@@ -314,7 +314,8 @@ def run_codec(args, world, rank, local):
     e2e = run_codec_e2e(args, wl, world)
     cpu = run_cpu_baseline_codec() if (world == 1 and rank == 0 and not args.no_cpu_baseline) else None
     clk = clocks.summary()
-    del wl
+    n_total = wl.n_total
+    del wl, g_dq, g_q
     torch.cuda.empty_cache()
     lin = None if args.no_linear else run_linear_metrics(args, world, flush)
     return {
@@ -331,7 +332,7 @@ def run_codec(args, world, rank, local):
         "dtype": "u8->bf16",
         "data": "synthetic: seeded fp16 ~N(0,0.02) with 0.1% x20 outliers, NF4 blocksize 64 (BASELINE config 2)",
         "config": {"workload": "codec: dequant of 2048^2, 4096^2, 14336x4096, 4096x14336 to bf16, plain and "
-                               "double-quant absmax (one CUDA-graph replay per step)", "elements_per_step": wl.n_total,
+                               "double-quant absmax (one CUDA-graph replay per step)", "elements_per_step": n_total,
                    "blocksize": 64, "parallelism": f"replicas x{world}",
                    "l2": "256 MiB fill between timed steps (outside events)"},
         "quantize": {"value": round(qvalue, 1), "unit": "GB/s", "ms_per_step": round(qms, 4),
