@@ -51,3 +51,15 @@ def test_invalid_arguments_are_reported_without_a_gpu():
     rc = lib.stratum_nf4_quantize(None, 1, 64, 64, None, None, None, None)
     assert rc == _lib.STRATUM_ERR_INVALID
     assert lib.stratum_nf4_quantize(None, 1, 0, 64, None, None, None, None) == _lib.STRATUM_OK  # empty input
+
+
+def test_package_exports_exist():
+    import stratum_b200
+
+    missing = [n for n in stratum_b200.__all__ if not hasattr(stratum_b200, n)]
+    assert missing == []
+    # the reference's hot-path names are all present (stratum/__init__.py:51-54, stratum/upload.py)
+    for name in ("NF4Linear", "NF4Prefetch", "prefetch_weights", "ensure_prefetched_weights", "prepare_nf4",
+                 "ensure_weights", "free_weights", "DeviceStage", "assign_layers_to_devices", "NF4_ATTR"):
+        assert name in stratum_b200.__all__
+    assert stratum_b200.NF4_ATTR == "roundpipe_nf4_payload"
