@@ -4,7 +4,8 @@
  *
  * Every entry point:
  *   - takes plain device pointers, element counts and a cudaStream_t (passed
- *     as void*; NULL means the legacy default stream);
+ *     as void*) and runs on that stream's device; NULL means the legacy default
+ *     stream of the device chosen with stratum_set_device() (default 0);
  *   - enqueues work on that stream and returns without synchronising;
  *   - allocates no device memory (callers pass outputs and workspaces);
  *   - returns STRATUM_OK (0) or a nonzero status; stratum_last_error() then
@@ -46,6 +47,9 @@ int stratum_abi_version(void);
 
 /* Message for the last nonzero status returned on the calling thread. */
 const char *stratum_last_error(void);
+
+/* Select the device used for calls made with a NULL (legacy default) stream. */
+int stratum_set_device(int device);
 
 /* Number of this library's kernel launches issued so far by this process
  * (all threads).  Used by benchmarks to count launches in a timed region. */

@@ -35,6 +35,7 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_abi_version": (_int, []),
     "stratum_last_error": (ctypes.c_char_p, []),
     "stratum_launch_count": (ctypes.c_uint64, []),
+    "stratum_set_device": (_int, [_int]),
     "stratum_nf4_quantize": (_int, [_vp, _int, _i64, _int, _vp, _vp, _vp, _vp]),
     "stratum_nf4_dq_workspace_bytes": (_sz, [_i64]),
     "stratum_nf4_quantize_absmax_dq": (_int, [_vp, _i64, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
@@ -102,7 +103,15 @@ def ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
 
 
 def stream_of(device: torch.device) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    """The caller's current stream on ``device``.  The library runs each call on the
+    stream's device; for torch's legacy default stream (handle 0) the library's own
+    current device is selected here first."""
+    dev = torch.device(device)
+    index = dev.index if dev.index is not None else torch.cuda.current_device()
+    handle = torch.cuda.current_stream(dev).cuda_stream
+    if handle == 0:  # always: a call on another stream may have switched the library's device
+        check(lib().stratum_set_device(index), "set_device")
+    return ctypes.c_void_p(handle)
 
 
 def require_cuda(t: torch.Tensor, what: str) -> None:

@@ -35,15 +35,36 @@ inline int check_launch(const char *what) {
 }
 
 inline int sm_count() {
-    static int cached = 0;
-    if (cached == 0) {
-        int dev = 0, n = 0;
-        cudaGetDevice(&dev);
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (cached[dev] == 0) {
+        int n = 0;
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        cached = n > 0 ? n : 148;
+        cached[dev] = n > 0 ? n : 148;
     }
-    return cached;
+    return cached[dev];
 }
+
+// This library links its own CUDA runtime, whose current device is separate
+// from the caller's (torch's).  Every entry point makes the device of the
+// stream it was given current; a NULL stream (the legacy default stream) keeps
+// the library's current device, which stratum_set_device() selects.
+inline int bind_stream_device(void *stream) {
+    if (stream == nullptr) return STRATUM_OK;
+    int dev = -1;
+    cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &dev);
+    if (e != cudaSuccess) return fail(STRATUM_ERR_CUDA, "cannot query the stream's device: %s", cudaGetErrorString(e));
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != dev && (e = cudaSetDevice(dev)) != cudaSuccess)
+        return fail(STRATUM_ERR_CUDA, "cannot select device %d: %s", dev, cudaGetErrorString(e));
+    return STRATUM_OK;
+}
+
+#define STRATUM_BIND_STREAM(stream) \
+    do { int rc_ = ::stratum::bind_stream_device(stream); if (rc_) return rc_; } while (0)
 
 // Resident CTAs of `kernel` on the whole GPU (SM count x occupancy), cached per kernel.
 template <auto Kernel>

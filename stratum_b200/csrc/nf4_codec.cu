@@ -478,6 +478,12 @@ const char *stratum_last_error(void) { return g_last_error; }
 
 uint64_t stratum_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int stratum_set_device(int device) {
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return fail(STRATUM_ERR_CUDA, "set_device(%d): %s", device, cudaGetErrorString(e));
+    return STRATUM_OK;
+}
+
 int stratum_nf4_quantize(const void *src, int src_dtype, int64_t n, int blocksize, const float *thresholds,
                          uint8_t *packed, float *absmax, void *stream) {
     STRATUM_REQUIRE(n >= 0, "quantize: n < 0");
@@ -487,6 +493,7 @@ int stratum_nf4_quantize(const void *src, int src_dtype, int64_t n, int blocksiz
     STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(src) % 16 == 0, "quantize: src must be 16-byte aligned");
     STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(packed) % 4 == 0, "quantize: packed must be 4-byte aligned");
     (void)esz;
+    STRATUM_BIND_STREAM(stream);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (src_dtype) {
         case STRATUM_F16: return launch_quantize(static_cast<const __half *>(src), n, blocksize, thresholds, packed, absmax, st);
@@ -510,6 +517,7 @@ int stratum_nf4_quantize_absmax_dq(const float *absmax, int64_t nb, int blocksiz
     STRATUM_REQUIRE(workspace_bytes >= stratum_nf4_dq_workspace_bytes(nb), "quantize_absmax_dq: workspace too small (%zu < %zu)",
                     workspace_bytes, stratum_nf4_dq_workspace_bytes(nb));
     STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 8 == 0, "quantize_absmax_dq: workspace must be 8-byte aligned");
+    STRATUM_BIND_STREAM(stream);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     double *partial = static_cast<double *>(workspace);
     const int64_t nparts = (nb + kMeanChunk - 1) / kMeanChunk;
@@ -535,6 +543,7 @@ int stratum_nf4_dequantize(const uint8_t *packed, const float *absmax, const flo
         return fail(STRATUM_ERR_UNSUPPORTED, "dequantize: blocksize %d not a power of two in [32, 4096]", blocksize);
     DequantArgs a{};
     a.packed = packed; a.absmax = absmax; a.code16 = code16; a.n = n; a.log2bs = ilog2(blocksize);
+    STRATUM_BIND_STREAM(stream);
     return launch_dequant<false>(a, out, out_dtype, static_cast<cudaStream_t>(stream));
 }
 
@@ -550,6 +559,7 @@ int stratum_nf4_dequantize_dq(const uint8_t *packed, const uint8_t *absmax_q, co
     DequantArgs a{};
     a.packed = packed; a.absmax_q = absmax_q; a.absmax2 = absmax2; a.code2 = code2; a.offset = offset;
     a.log2bs2 = ilog2(blocksize2); a.code16 = code16; a.n = n; a.log2bs = ilog2(blocksize);
+    STRATUM_BIND_STREAM(stream);
     return launch_dequant<true>(a, out, out_dtype, static_cast<cudaStream_t>(stream));
 }
 

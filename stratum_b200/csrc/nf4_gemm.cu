@@ -808,6 +808,7 @@ extern "C" {
 
 int stratum_device_status(int *out, int reset, void *stream) {
     STRATUM_REQUIRE(out != nullptr, "device_status: null out");
+    STRATUM_BIND_STREAM(stream);
     int *dp = gemm::status_ptr();
     if (!dp) return fail(STRATUM_ERR_CUDA, "device_status: cannot resolve the status word");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -839,6 +840,7 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
     STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(packed) % 16 == 0,
                     "nf4_gemm_fwd: x and packed must be 16-byte aligned");
     STRATUM_REQUIRE(T <= (int64_t(1) << 31) && N <= (int64_t(1) << 31), "nf4_gemm_fwd: size too large");
+    STRATUM_BIND_STREAM(stream);
     int *status = gemm::status_ptr();
     if (!status) return fail(STRATUM_ERR_CUDA, "nf4_gemm_fwd: no status word");
 
@@ -913,6 +915,7 @@ int stratum_nf4_gemm_dx(const void *dy, int dtype, int64_t T, int64_t N, const u
     STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(dy) % 16 == 0 && reinterpret_cast<uintptr_t>(packed) % 16 == 0 &&
                         (r == 0 || reinterpret_cast<uintptr_t>(lora_a) % 16 == 0),
                     "nf4_gemm_dx: dy, packed and lora_A must be 16-byte aligned");
+    STRATUM_BIND_STREAM(stream);
     int *status = gemm::status_ptr();
     if (!status) return fail(STRATUM_ERR_CUDA, "nf4_gemm_dx: no status word");
     const bool bf16 = dtype == STRATUM_BF16;
