@@ -86,6 +86,23 @@ int stratum_nf4_quantize_absmax_dq(const float *absmax, int64_t nb, int blocksiz
                                    float *absmax2, float *offset, void *workspace,
                                    size_t workspace_bytes, void *stream);
 
+/* NF4 quantization with double quantization in one call, for callers that
+ * cannot allocate device memory for a workspace (an FFI host that only owns
+ * the buffers it passes in, or code running where allocation is not
+ * allowed).  This entry point has no counterpart in the reference.
+ * Blocksize 64 (blocksize2 256); outputs as stratum_nf4_quantize followed by
+ * stratum_nf4_quantize_absmax_dq.  Its scratch (the float32 absmax and the
+ * mean's chunk sums) is one fixed array inside the library: at most 2^20
+ * blocks (67,108,864 elements) per call, larger sizes return
+ * STRATUM_ERR_INVALID; the array takes 4 MiB + 8 KiB on every GPU that loads
+ * the library until the process exits.  A device's first call looks the array
+ * up, so make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU (other streams, other threads) race. */
+int stratum_nf4_quantize_dq_noalloc(const void *src, int src_dtype, int64_t n,
+                                    const float *thresholds, const float *thresholds2,
+                                    uint8_t *packed, uint8_t *absmax_q, float *absmax2,
+                                    float *offset, void *stream);
+
 /* K2: blockwise NF4 dequantization to F16/BF16/F32.
  * Replaces bitsandbytes.functional.dequantize_4bit(q, QuantState(...)) called at
  * stratum/upload.py:221, :946, :1038 and stratum/nf4_linear.py:44-46.

@@ -534,6 +534,73 @@ int stratum_nf4_quantize_absmax_dq(const float *absmax, int64_t nb, int blocksiz
     return check_launch("nf4_dq_quant");
 }
 
+// ------------------------------------------------------------------------
+// Allocation-free double-quant quantizer.
+//
+// Some callers of this library cannot allocate device memory for a
+// workspace: a host that binds the C ABI through an FFI and owns only the
+// buffers it was handed (every tensor belongs to the caller's allocator,
+// e.g. torch's caching allocator, and the library must not create device
+// memory behind its back), or code running where an allocation is not
+// allowed at that point.  NF4 quantization with double quantization needs
+// two pieces of scratch -- the float32 absmax of every block and the
+// chunk sums of the absmax mean -- so for those callers the scratch lives
+// in one file-scope __device__ array of a fixed size instead.
+//
+// Limit: at most kNoAllocMaxBlocks NF4 blocks of 64 elements per call
+// (64 Mi elements, e.g. a 14336 x 4096 weight).  The array costs 4 MiB +
+// 8 KiB on every GPU that loads the library, held until the process exits.
+constexpr int64_t kNoAllocMaxBlocks = int64_t(1) << 20;
+constexpr size_t kNoAllocAbsmaxBytes = size_t(kNoAllocMaxBlocks) * sizeof(float);
+constexpr size_t kNoAllocPartialBytes = size_t(kNoAllocMaxBlocks / kMeanChunk) * sizeof(double);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocAbsmaxBytes + kNoAllocPartialBytes];
+
+// Device address of g_noalloc_scratch on the current device.  The name is
+// only a host-side stand-in; the address comes from cudaGetSymbolAddress,
+// looked up once per device (on that device's first call) and cached.
+static int noalloc_scratch(unsigned char **out) {
+    static unsigned char *ptrs[64] = {nullptr};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64)
+        return fail(STRATUM_ERR_CUDA, "quantize_dq_noalloc: no current device (%s)", cudaGetErrorString(e));
+    if (ptrs[dev] == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(STRATUM_ERR_CUDA, "quantize_dq_noalloc: cannot resolve the scratch array on device %d: %s", dev,
+                        cudaGetErrorString(e));
+        ptrs[dev] = static_cast<unsigned char *>(p);
+    }
+    *out = ptrs[dev];
+    return STRATUM_OK;
+}
+
+int stratum_nf4_quantize_dq_noalloc(const void *src, int src_dtype, int64_t n, const float *thresholds,
+                                    const float *thresholds2, uint8_t *packed, uint8_t *absmax_q, float *absmax2,
+                                    float *offset, void *stream) {
+    STRATUM_REQUIRE(n > 0, "quantize_dq_noalloc: n must be > 0");
+    const int64_t nb = (n + 63) / 64;
+    if (nb > kNoAllocMaxBlocks)
+        return fail(STRATUM_ERR_INVALID,
+                    "quantize_dq_noalloc: %lld elements need %lld NF4 blocks, above this entry point's fixed scratch "
+                    "of %lld blocks (%lld elements); use stratum_nf4_quantize + stratum_nf4_quantize_absmax_dq with "
+                    "a caller-provided workspace",
+                    (long long)n, (long long)nb, (long long)kNoAllocMaxBlocks, (long long)(kNoAllocMaxBlocks * 64));
+    STRATUM_BIND_STREAM(stream);
+    unsigned char *scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    float *absmax = reinterpret_cast<float *>(scratch);
+    double *partial = reinterpret_cast<double *>(scratch + kNoAllocAbsmaxBytes);
+    // Both scratch regions are written in full before they are read (every
+    // block's absmax, every chunk's sum), so nothing carries over between calls.
+    rc = stratum_nf4_quantize(src, src_dtype, n, 64, thresholds, packed, absmax, stream);
+    if (rc) return rc;
+    return stratum_nf4_quantize_absmax_dq(absmax, nb, 256, thresholds2, absmax_q, absmax2, offset, partial,
+                                          kNoAllocPartialBytes, stream);
+}
+
 int stratum_nf4_dequantize(const uint8_t *packed, const float *absmax, const float *code16, int64_t n, int blocksize,
                            void *out, int out_dtype, void *stream) {
     STRATUM_REQUIRE(n >= 0, "dequantize: n < 0");
