@@ -47,6 +47,18 @@ SIGNATURES: dict[str, tuple] = {
                                     _vp, _int, _vp, _vp]),
     "stratum_nf4_gemm_dx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _int,
                                    _vp, _vp]),
+    # include/stratum_moe.h
+    "stratum_moe_route_workspace_bytes": (_sz, [_i64, _int]),
+    "stratum_moe_route": (_int, [_vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "stratum_moe_gather_rows": (_int, [_vp, _i64, _vp, _i64, _vp, _vp]),
+    "stratum_nf4_grouped_table_bytes": (_sz, [_i64, _int, _i64]),
+    "stratum_nf4_grouped_fwd": (_int, [_vp, _int, _i64, _int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int,
+                                       _int, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "stratum_nf4_grouped_dx": (_int, [_vp, _int, _i64, _int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int,
+                                      _vp, _vp, _sz, _vp]),
+    "stratum_moe_combine": (_int, [_vp, _int, _vp, _vp, _vp, _int, _i64, _int, _i64, _vp, _vp]),
+    "stratum_moe_combine_grad": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _vp, _vp, _vp]),
+    "stratum_swiglu_grad": (_int, [_vp, _vp, _int, _i64, _i64, _vp, _vp]),
 }
 
 ABI_VERSION = 1

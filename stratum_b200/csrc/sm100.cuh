@@ -20,6 +20,8 @@ enum DeviceError : int {
     kErrTimeoutDequant = 0x103,
     kErrTimeoutEpilogue = 0x104,
     kErrTimeoutTeardown = 0x105,
+    kErrBadOffsets = 0x201,  // grouped GEMM: expert offsets outside [0, total tokens]
+    kErrTileTable = 0x202,   // grouped GEMM: tile table smaller than the offsets need
 };
 
 // A wait that takes longer than this is a hang, never a slow pipeline stage

@@ -148,3 +148,198 @@ def nf4_gemm_dx(
             "nf4_gemm_dx",
         )
     return dx.reshape(*dy.shape[:-1], K)
+
+
+# --------------------------------------------------------------------------------
+# routed experts (include/stratum_moe.h)
+# --------------------------------------------------------------------------------
+
+class Routing:
+    """Expert-sorted layout of the router's (token, slot) pairs.
+
+    ``order[p]`` is the flat pair ``t*k + slot`` of sorted row ``p``, ``inv`` its
+    inverse, ``token_of[p] = order[p] // k``; expert ``e`` owns sorted rows
+    ``offsets[e]:offsets[e+1]``.  Pairs whose expert id lies outside
+    ``[0, n_experts)`` are dropped (sorted after ``offsets[E]``), as HF's
+    ``Qwen3MoeExperts.forward`` skips ``expert_idx == num_experts``.
+    """
+
+    __slots__ = ("order", "inv", "token_of", "offsets", "T", "k", "n_experts")
+
+    def __init__(self, order, inv, token_of, offsets, T, k, n_experts):
+        self.order, self.inv, self.token_of, self.offsets = order, inv, token_of, offsets
+        self.T, self.k, self.n_experts = T, k, n_experts
+
+    @property
+    def rows(self) -> int:
+        return self.T * self.k
+
+
+def moe_route(top_k_index: torch.Tensor, n_experts: int) -> Routing:
+    """Stable counting sort of ``top_k_index`` ([T, k] expert ids) by expert, on the GPU."""
+    _lib.require_cuda(top_k_index, "moe_route")
+    if top_k_index.dim() != 2:
+        raise ValueError(f"moe_route: top_k_index must be [T, k], got {tuple(top_k_index.shape)}")
+    dev = top_k_index.device
+    idx = top_k_index.to(torch.int64).contiguous()
+    T, k = int(idx.shape[0]), int(idx.shape[1])
+    n = T * k
+    order = torch.empty(n, dtype=torch.int32, device=dev)
+    inv = torch.empty(n, dtype=torch.int32, device=dev)
+    token_of = torch.empty(n, dtype=torch.int32, device=dev)
+    offsets = torch.empty(n_experts + 1, dtype=torch.int32, device=dev)
+    L = _lib.lib()
+    ws_bytes = int(L.stratum_moe_route_workspace_bytes(n, n_experts))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(L.stratum_moe_route(_lib.ptr(idx), T, k, n_experts, _lib.ptr(order), _lib.ptr(inv),
+                                       _lib.ptr(token_of), _lib.ptr(offsets), _lib.ptr(ws), ws_bytes,
+                                       _lib.stream_of(dev)), "moe_route")
+    return Routing(order, inv, token_of, offsets, T, k, n_experts)
+
+
+def moe_gather_rows(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """``src[idx]`` for a 2-D ``src`` with 16-byte rows (the expert dispatch gather)."""
+    _lib.require_cuda(src, "moe_gather_rows")
+    src = src.contiguous()
+    dst = torch.empty((idx.numel(), src.shape[1]), dtype=src.dtype, device=src.device)
+    L = _lib.lib()
+    with torch.cuda.device(src.device):
+        _lib.check(L.stratum_moe_gather_rows(_lib.ptr(src), src.shape[1] * src.element_size(), _lib.ptr(idx),
+                                             idx.numel(), _lib.ptr(dst), _lib.stream_of(src.device)),
+                   "moe_gather_rows")
+    return dst
+
+
+def _table(rows: int, n_experts: int, weight_dim: int, dev: torch.device) -> tuple[torch.Tensor, int]:
+    nbytes = int(_lib.lib().stratum_nf4_grouped_table_bytes(rows, n_experts, weight_dim))
+    return torch.empty(nbytes, dtype=torch.uint8, device=dev), nbytes
+
+
+def _expert_weight_shape(qs: QuantState, n_experts: int, what: str) -> tuple[int, int]:
+    """(N_e, K) of a flattened [E*N_e, K] NF4 expert weight."""
+    if qs.blocksize != 64 or len(qs.shape) != 2:
+        raise ValueError(f"{what}: needs a flattened 2-D NF4 expert weight with blocksize 64")
+    rows, K = int(qs.shape[0]), int(qs.shape[1])
+    if rows % n_experts:
+        raise ValueError(f"{what}: {rows} weight rows do not split into {n_experts} experts")
+    return rows // n_experts, K
+
+
+def nf4_grouped_fwd(x_sorted: torch.Tensor, routing: Routing, packed: torch.Tensor, qs: QuantState, *,
+                    swiglu: bool = False, rw: Optional[torch.Tensor] = None, keep_gate_up: bool = False):
+    """Grouped expert forward over expert-sorted rows (one launch for every expert).
+
+    ``qs.shape`` is ``(E*N_e, K)``.  Plain: returns ``x_sorted . W[e]^T`` (times
+    ``rw``, per sorted row, when given).  ``swiglu``: the weight is gate_up_proj and
+    the result is ``silu(gate) * up`` ([rows, N_e/2]); with ``keep_gate_up`` the
+    gate|up activations ([rows, N_e]) are returned as well.
+    """
+    _lib.require_cuda(x_sorted, "nf4_grouped_fwd")
+    if x_sorted.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"nf4_grouped_fwd: x must be bf16 or fp16, got {x_sorted.dtype}")
+    E = routing.n_experts
+    N_e, K = _expert_weight_shape(qs, E, "nf4_grouped_fwd")
+    if x_sorted.shape[-1] != K or x_sorted.shape[0] != routing.rows:
+        raise ValueError(f"nf4_grouped_fwd: x_sorted {tuple(x_sorted.shape)} does not match [{routing.rows}, {K}]")
+    dev = x_sorted.device
+    x2 = x_sorted.contiguous()
+    rows = x2.shape[0]
+    y = torch.empty((rows, N_e // 2 if swiglu else N_e), dtype=x2.dtype, device=dev)
+    gu = torch.empty((rows, N_e), dtype=x2.dtype, device=dev) if (swiglu and keep_gate_up) else None
+    if rw is not None:
+        rw = rw.to(device=dev, dtype=torch.float32).contiguous()
+    table, tbytes = _table(rows, E, max(N_e, K), dev)
+    absmax, absmax_q, absmax2, code2, offset, code16 = _weight_args(qs, dev)
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(
+            L.stratum_nf4_grouped_fwd(
+                _lib.ptr(x2), _lib.DTYPE_CODE[x2.dtype], rows, K, _lib.ptr(routing.offsets), E, _lib.ptr(packed),
+                _lib.ptr(absmax), _lib.ptr(absmax_q), _lib.ptr(absmax2), _lib.ptr(code2), _lib.ptr(offset),
+                _lib.ptr(code16), N_e, int(swiglu), _lib.ptr(rw), _lib.ptr(y), _lib.ptr(gu), _lib.ptr(table), tbytes,
+                _lib.stream_of(dev)),
+            "nf4_grouped_fwd",
+        )
+    return (y, gu) if keep_gate_up else y
+
+
+def nf4_grouped_dx(dy_sorted: torch.Tensor, routing: Routing, packed: torch.Tensor, qs: QuantState) -> torch.Tensor:
+    """Grouped expert input gradient: ``dy_sorted . W[e]`` for every sorted row."""
+    _lib.require_cuda(dy_sorted, "nf4_grouped_dx")
+    if dy_sorted.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"nf4_grouped_dx: dy must be bf16 or fp16, got {dy_sorted.dtype}")
+    E = routing.n_experts
+    N_e, K = _expert_weight_shape(qs, E, "nf4_grouped_dx")
+    if dy_sorted.shape[-1] != N_e or dy_sorted.shape[0] != routing.rows:
+        raise ValueError(f"nf4_grouped_dx: dy_sorted {tuple(dy_sorted.shape)} does not match [{routing.rows}, {N_e}]")
+    dev = dy_sorted.device
+    dy2 = dy_sorted.contiguous()
+    rows = dy2.shape[0]
+    dx = torch.empty((rows, K), dtype=dy2.dtype, device=dev)
+    table, tbytes = _table(rows, E, max(N_e, K), dev)
+    absmax, absmax_q, absmax2, code2, offset, code16 = _weight_args(qs, dev)
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(
+            L.stratum_nf4_grouped_dx(
+                _lib.ptr(dy2), _lib.DTYPE_CODE[dy2.dtype], rows, N_e, _lib.ptr(routing.offsets), E, _lib.ptr(packed),
+                _lib.ptr(absmax), _lib.ptr(absmax_q), _lib.ptr(absmax2), _lib.ptr(code2), _lib.ptr(offset),
+                _lib.ptr(code16), K, _lib.ptr(dx), _lib.ptr(table), tbytes, _lib.stream_of(dev)),
+            "nf4_grouped_dx",
+        )
+    return dx
+
+
+def moe_combine(rows: torch.Tensor, routing: Routing, weights: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out[t] = sum_s weights[t, s] * rows[inv[t*k+s]]`` (fp32 sum), [T, width] in ``rows.dtype``."""
+    _lib.require_cuda(rows, "moe_combine")
+    dev = rows.device
+    rows = rows.contiguous()
+    width = rows.shape[1]
+    out = torch.empty((routing.T, width), dtype=rows.dtype, device=dev)
+    if weights is not None:
+        weights = weights.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.stratum_moe_combine(_lib.ptr(rows), _lib.DTYPE_CODE[rows.dtype], _lib.ptr(routing.inv),
+                                         _lib.ptr(weights), _lib.ptr(routing.offsets), routing.n_experts, routing.T,
+                                         routing.k, width, _lib.ptr(out), _lib.stream_of(dev)), "moe_combine")
+    return out
+
+
+def moe_combine_grad(dout: torch.Tensor, routing: Routing, weights: Optional[torch.Tensor],
+                     rows: Optional[torch.Tensor]) -> tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Backward of :func:`moe_combine`: (dy_sorted, dweights [T*k] fp32 or None when ``rows`` is None)."""
+    _lib.require_cuda(dout, "moe_combine_grad")
+    dev = dout.device
+    dout = dout.contiguous()
+    width = dout.shape[1]
+    dy_sorted = torch.empty((routing.rows, width), dtype=dout.dtype, device=dev)
+    dw = torch.empty(routing.rows, dtype=torch.float32, device=dev) if rows is not None else None
+    if weights is not None:
+        weights = weights.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.stratum_moe_combine_grad(_lib.ptr(dout), _lib.DTYPE_CODE[dout.dtype], _lib.ptr(routing.order),
+                                              _lib.ptr(routing.token_of), _lib.ptr(weights), _lib.ptr(routing.offsets),
+                                              routing.n_experts, _lib.ptr(rows), routing.rows, width,
+                                              _lib.ptr(dy_sorted), _lib.ptr(dw), _lib.stream_of(dev)),
+                   "moe_combine_grad")
+    return dy_sorted, dw
+
+
+def swiglu_grad(gate_up: torch.Tensor, dh: torch.Tensor) -> torch.Tensor:
+    """d(gate|up) of ``h = silu(gate) * up`` given the saved gate|up and dh."""
+    _lib.require_cuda(gate_up, "swiglu_grad")
+    rows, inter = int(dh.shape[0]), int(dh.shape[1])
+    if tuple(gate_up.shape) != (rows, 2 * inter):
+        raise ValueError(f"swiglu_grad: gate_up {tuple(gate_up.shape)} does not match dh {tuple(dh.shape)}")
+    gate_up, dh = gate_up.contiguous(), dh.contiguous()
+    dgu = torch.empty_like(gate_up)
+    L = _lib.lib()
+    with torch.cuda.device(dh.device):
+        _lib.check(L.stratum_swiglu_grad(_lib.ptr(gate_up), _lib.ptr(dh),
+                                         _lib.DTYPE_CODE[dh.dtype], rows, inter, _lib.ptr(dgu),
+                                         _lib.stream_of(dh.device)), "swiglu_grad")
+    return dgu
