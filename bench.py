@@ -318,6 +318,7 @@ def run_codec(args, world, rank, local):
     del wl, g_dq, g_q
     torch.cuda.empty_cache()
     lin = None if args.no_linear else run_linear_metrics(args, world, flush)
+    moe = None if args.no_experts else run_experts_metrics(args, world, flush)
     return {
         "metric": "nf4_dequant_GBps",
         "value": round(value, 1),
@@ -344,6 +345,7 @@ def run_codec(args, world, rank, local):
         "wall_s_timed": round(t_wall, 4),
         "clocks": clk,
         "nf4_linear": lin,
+        "nf4_moe_experts": moe,
     }
 
 
@@ -495,6 +497,211 @@ def run_linear(args, world, rank, local):
     return out
 
 
+MOE_T, MOE_E, MOE_TOPK, MOE_H, MOE_I = 4096, 128, 8, 2048, 768  # one Qwen3-30B-A3B-shaped expert layer
+
+
+class ExpertsWorkload:
+    """Routed experts of one Qwen3-30B-A3B-shaped MoE layer, forward + backward.
+
+    4096 tokens, 128 experts, top-8 from a N(0, 0.02) router (data-dependent,
+    skewed routing), hidden 2048, expert intermediate 768; expert weights NF4
+    bs64.  ``step`` is what NF4Experts' autograd launches (route, gather, grouped
+    gate_up + SwiGLU, grouped down, combine; combine grad, grouped dX down, SwiGLU
+    grad, grouped dX gate_up, combine), with events around the grouped GEMMs.
+    ``module_step`` calls the module itself.  ``reference_step`` is the
+    reference's GPU path: dequantize every expert to bf16, then HF
+    Qwen3MoeExperts' per-expert loop forward + autograd backward.
+    """
+
+    def __init__(self, device):
+        from stratum_b200 import functional as F
+        from stratum_b200 import ops
+        from stratum_b200.experts import NF4Experts
+
+        self.F, self.ops, self.device = F, ops, device
+        g = torch.Generator(device=device).manual_seed(0)
+        E, H, I, T, k = MOE_E, MOE_H, MOE_I, MOE_T, MOE_TOPK
+        holder = torch.nn.Module()
+        holder.gate_up_proj = torch.nn.Parameter((torch.randn(E, 2 * I, H, generator=g, device=device) * 0.02).half(),
+                                                 requires_grad=False)
+        holder.down_proj = torch.nn.Parameter((torch.randn(E, H, I, generator=g, device=device) * 0.02).half(),
+                                              requires_grad=False)
+        holder.act_fn = torch.nn.SiLU()
+        self.mod = NF4Experts.from_experts(holder)
+        del holder
+        x = torch.randn(T, H, generator=g, device=device).to(torch.bfloat16)
+        wr = torch.randn(E, H, generator=g, device=device) * 0.02
+        probs = torch.softmax(x.float() @ wr.t(), dim=-1)
+        w, idx = torch.topk(probs, k, dim=-1)
+        w = w / w.sum(-1, keepdim=True)  # norm_topk_prob
+        self.idx = idx
+        self.x = x.requires_grad_()
+        self.w = w.requires_grad_()
+        self.dout = torch.randn(T, H, generator=g, device=device).to(torch.bfloat16)
+        counts = torch.bincount(idx.reshape(-1), minlength=E)
+        self.tokens_per_expert = {"mean": round(float(counts.float().mean()), 1), "max": int(counts.max()),
+                                  "min": int(counts.min())}
+        rows = T * k
+        self.flops_fwd = 2.0 * rows * (2 * I * H + H * I)
+        self.flops = 2.0 * self.flops_fwd  # forward + input gradient (the experts are frozen)
+        self.gu_buf = self.dn_buf = self.hf = None
+
+    def module_step(self):
+        self.x.grad = None
+        self.w.grad = None
+        out = self.mod(self.x, self.idx, self.w)
+        out.backward(self.dout)
+
+    def step(self, events=None):
+        ops, m = self.ops, self.mod
+        ev = lambda: torch.cuda.Event(enable_timing=True, external=True)  # noqa: E731
+
+        def start():
+            if events is None:
+                return None
+            e0 = ev()
+            e0.record()
+            return e0
+
+        def mark(name, e0):
+            if events is not None:
+                e1 = ev()
+                e1.record()
+                events.append((name, e0, e1))
+
+        r = ops.moe_route(self.idx, m.num_experts)
+        xs = ops.moe_gather_rows(self.x.detach(), r.token_of)
+        e0 = start()
+        h, gu = ops.nf4_grouped_fwd(xs, r, m.gate_up, m.gate_up_state, swiglu=True, keep_gate_up=True)
+        mark("fwd_gate_up_swiglu", e0)
+        e0 = start()
+        o = ops.nf4_grouped_fwd(h, r, m.down, m.down_state)
+        mark("fwd_down", e0)
+        w = self.w.detach().reshape(-1)
+        ops.moe_combine(o, r, w)
+        dys, dw = ops.moe_combine_grad(self.dout, r, w, o)
+        e0 = start()
+        dh = ops.nf4_grouped_dx(dys, r, m.down, m.down_state)
+        mark("dx_down", e0)
+        dgu = ops.swiglu_grad(gu, dh)
+        e0 = start()
+        dxs = ops.nf4_grouped_dx(dgu, r, m.gate_up, m.gate_up_state)
+        mark("dx_gate_up", e0)
+        ops.moe_combine(dxs, r, None)
+
+    def reference_step(self):
+        from transformers import Qwen3MoeConfig
+        from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeExperts
+
+        E, H, I = MOE_E, MOE_H, MOE_I
+        if self.hf is None:
+            cfg = Qwen3MoeConfig(hidden_size=H, moe_intermediate_size=I, num_experts=E, num_experts_per_tok=MOE_TOPK,
+                                 hidden_act="silu")
+            with torch.device("meta"):
+                self.hf = Qwen3MoeExperts(cfg)
+            self.gu_buf = torch.empty(E * 2 * I, H, dtype=torch.bfloat16, device=self.device)
+            self.dn_buf = torch.empty(E * H, I, dtype=torch.bfloat16, device=self.device)
+            self.hf.gate_up_proj = torch.nn.Parameter(self.gu_buf.view(E, 2 * I, H), requires_grad=False)
+            self.hf.down_proj = torch.nn.Parameter(self.dn_buf.view(E, H, I), requires_grad=False)
+        m = self.mod
+        self.F.dequantize_4bit(m.gate_up, m.gate_up_state, out=self.gu_buf, out_dtype=torch.bfloat16)
+        self.F.dequantize_4bit(m.down, m.down_state, out=self.dn_buf, out_dtype=torch.bfloat16)
+        self.x.grad = None
+        self.w.grad = None
+        out = self.hf(self.x, self.idx, self.w)
+        out.backward(self.dout)
+
+
+def run_experts_metrics(args, world, flush):
+    """Time ExpertsWorkload: the module (CUDA-graph replays), the per-kernel split, and the reference path."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    wl = ExpertsWorkload(dev)
+    ev = []
+    g_m, _, launches = capture(wl.module_step)
+    g_k, _, _ = capture(lambda: (ev.clear(), wl.step(ev)))
+    for _ in range(args.warmup):
+        g_m.replay()
+        g_k.replay()
+        wl.reference_step()
+    torch.cuda.synchronize()
+
+    def timed(run, n, collect=None):
+        out = []
+        for _ in range(n):
+            flush.fill_(1)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            run()
+            e1.record()
+            e1.synchronize()
+            out.append(e0.elapsed_time(e1))
+            if collect is not None:
+                collect += [(name, a.elapsed_time(b)) for name, a, b in ev]
+        return out
+
+    barrier(world)
+    torch.cuda.synchronize()
+    nsteps = max(3, min(args.steps, 30))
+    kern = []
+    with ClockSampler(dev.index) as clocks:
+        mod_ms = timed(g_m.replay, nsteps)
+        timed(g_k.replay, nsteps, kern)
+        torch.cuda.synchronize()
+        barrier(world)
+        ref_ms = timed(wl.reference_step, max(3, nsteps // 3))
+    ms = max_over_ranks(statistics.mean(mod_ms), world)
+    peaks = load_peaks()
+    E, H, I, rows = MOE_E, MOE_H, MOE_I, MOE_T * MOE_TOPK
+    kflops = {"fwd_gate_up_swiglu": 2.0 * rows * 2 * I * H, "fwd_down": 2.0 * rows * H * I,
+              "dx_down": 2.0 * rows * H * I, "dx_gate_up": 2.0 * rows * 2 * I * H}
+    per = {}
+    tot_f = tot_ms = 0.0
+    for name, f in kflops.items():
+        t = statistics.mean([t for n, t in kern if n == name])
+        per[name] = {"TFLOPs": round(f / (t * 1e-3) / 1e12, 1), "ms": round(t, 4)}
+        tot_f += f
+        tot_ms += t
+    achieved = tot_f / (tot_ms * 1e-3) / 1e12
+    ref = statistics.mean(ref_ms)
+    return {
+        "metric": "nf4_moe_experts_fwd_bwd_TFLOPs",
+        "value": round(wl.flops * world / (ms * 1e-3) / 1e12, 1),
+        "unit": "TFLOP/s",
+        "ms_per_step": round(ms, 4),
+        "tokens_per_s": round(MOE_T * world / (ms * 1e-3), 1),
+        "workload": f"NF4Experts fwd+bwd, one Qwen3-30B-A3B-shaped layer: T={MOE_T}, E={E}, top-{MOE_TOPK}, "
+                    f"H={H}, I={I}, N(0,0.02) router",
+        "tokens_per_expert": wl.tokens_per_expert,
+        "roofline": {"bound": "tensor", "kernel": "k_grouped_fwd + k_grouped_dx", "achieved": round(achieved, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "frac_of": peaks["source"], "per_kernel": per, "traffic": None},
+        "gpu_reference_path": {"what": "dequantize every expert to bf16, HF Qwen3MoeExperts per-expert loop fwd + "
+                                       "autograd bwd (the reference's path on a GPU)",
+                               "TFLOPs": round(wl.flops / (ref * 1e-3) / 1e12, 1), "ms_per_step": round(ref, 4),
+                               "speedup": round(ref / ms, 2)},
+        "gpu_launches_per_step": int(launches),
+        "clocks": clocks.summary(),
+    }
+
+
+def run_experts(args, world, rank, local):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    r = run_experts_metrics(args, world, flush)
+    return {
+        "metric": r["metric"], "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (NF4 weights)",
+        "data": "synthetic: expert weights ~N(0,0.02) fp16 -> NF4 bs64, x, dY ~N(0,1) bf16, router ~N(0,0.02)",
+        "config": {"workload": r["workload"], "parallelism": f"replicas x{world}",
+                   "l2": "256 MiB fill between timed steps"},
+        "tokens_per_s": r["tokens_per_s"], "tokens_per_expert": r["tokens_per_expert"],
+        "roofline": r["roofline"], "gpu_reference_path": r["gpu_reference_path"],
+        "gpu_launches": r["gpu_launches_per_step"] * args.steps, "clocks": r["clocks"],
+    }
+
+
 def run_codec_e2e(args, wl, world):
     """Same metric through the reference-facing call with host buffers.
 
@@ -637,9 +844,10 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("codec", "linear"), default="codec")
+    ap.add_argument("--workload", choices=("codec", "linear", "experts"), default="codec")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-linear", action="store_true", help="skip the NF4Linear fwd+bwd section of the codec run")
+    ap.add_argument("--no-experts", action="store_true", help="skip the MoE experts section of the codec run")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -650,7 +858,8 @@ def main():
         else:
             if not torch.cuda.is_available():
                 raise SystemExit("bench.py: no CUDA device (the product path has no CPU fallback)")
-            out = (run_linear if args.workload == "linear" else run_codec)(args, world, rank, local)
+            run = {"codec": run_codec, "linear": run_linear, "experts": run_experts}[args.workload]
+            out = run(args, world, rank, local)
         if rank == 0 and out is not None:
             print(json.dumps(out), flush=True)
     finally:

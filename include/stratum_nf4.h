@@ -5,7 +5,10 @@
  * Every entry point:
  *   - takes plain device pointers, element counts and a cudaStream_t (passed
  *     as void*) and runs on that stream's device; NULL means the legacy default
- *     stream of the device chosen with stratum_set_device() (default 0);
+ *     stream of the device chosen with stratum_set_device() (default 0); while
+ *     the stream is being captured into a CUDA graph its device cannot be
+ *     queried, so the device chosen with stratum_set_device() (or by the last
+ *     call) is used;
  *   - enqueues work on that stream and returns without synchronising;
  *   - allocates no device memory (callers pass outputs and workspaces);
  *   - returns STRATUM_OK (0) or a nonzero status; stratum_last_error() then

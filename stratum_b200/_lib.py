@@ -117,12 +117,14 @@ def ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
 
 def stream_of(device: torch.device) -> ctypes.c_void_p:
     """The caller's current stream on ``device``.  The library runs each call on the
-    stream's device; for torch's legacy default stream (handle 0) the library's own
-    current device is selected here first."""
+    stream's device; for torch's legacy default stream (handle 0), and while the
+    stream is being captured into a CUDA graph (when its device cannot be queried),
+    the library's own current device is selected here first."""
     dev = torch.device(device)
     index = dev.index if dev.index is not None else torch.cuda.current_device()
     handle = torch.cuda.current_stream(dev).cuda_stream
-    if handle == 0:  # always: a call on another stream may have switched the library's device
+    # always: a call on another stream may have switched the library's device
+    if handle == 0 or torch.cuda.is_current_stream_capturing():
         check(lib().stratum_set_device(index), "set_device")
     return ctypes.c_void_p(handle)
 

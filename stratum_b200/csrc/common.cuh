@@ -50,16 +50,34 @@ inline int sm_count() {
 // This library links its own CUDA runtime, whose current device is separate
 // from the caller's (torch's).  Every entry point makes the device of the
 // stream it was given current; a NULL stream (the legacy default stream) keeps
-// the library's current device, which stratum_set_device() selects.
+// the library's current device, which stratum_set_device() selects.  A stream
+// that is being captured into a CUDA graph cannot be asked for its device (the
+// query is not permitted during capture and would invalidate it), so while a
+// stream captures, the library's current device is used as well: callers that
+// capture on a device other than the last one used select it with
+// stratum_set_device() first.
 inline int bind_stream_device(void *stream) {
     if (stream == nullptr) return STRATUM_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(st, &cs);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(STRATUM_ERR_CUDA, "cannot query the stream's capture state: %s", cudaGetErrorString(e));
+    }
+    if (cs != cudaStreamCaptureStatusNone) return STRATUM_OK;
     int dev = -1;
-    cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &dev);
-    if (e != cudaSuccess) return fail(STRATUM_ERR_CUDA, "cannot query the stream's device: %s", cudaGetErrorString(e));
+    e = cudaStreamGetDevice(st, &dev);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(STRATUM_ERR_CUDA, "cannot query the stream's device: %s", cudaGetErrorString(e));
+    }
     int cur = -1;
     cudaGetDevice(&cur);
-    if (cur != dev && (e = cudaSetDevice(dev)) != cudaSuccess)
+    if (cur != dev && (e = cudaSetDevice(dev)) != cudaSuccess) {
+        cudaGetLastError();
         return fail(STRATUM_ERR_CUDA, "cannot select device %d: %s", dev, cudaGetErrorString(e));
+    }
     return STRATUM_OK;
 }
 
