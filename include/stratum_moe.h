@@ -73,9 +73,10 @@ size_t stratum_nf4_grouped_table_bytes(int64_t total_tokens, int n_experts, int6
  *   swiglu=0 : y is Ttot x N_e; rw (float32[Ttot], per sorted row, or NULL)
  *              scales each row (Qwen3MoeExperts' "* top_k_weights")
  *   swiglu=1 : W is gate_up_proj (rows [0, N_e/2) gate, [N_e/2, N_e) up); y is
- *              Ttot x N_e/2 holding h = silu(gate) * up, computed from the fp32
- *              accumulators; gate_up (Ttot x N_e, optional) receives gate|up
- *              themselves for the backward
+ *              Ttot x N_e/2 holding h = silu(gate) * up, computed from gate and
+ *              up rounded to dtype (as HF's forward in that dtype computes it);
+ *              gate_up (Ttot x N_e, optional) receives gate|up themselves for
+ *              the backward
  * Rows of y outside [offsets[0], offsets[E]) are not written.  Offsets that are
  * decreasing or outside [0, Ttot] write nothing and set the status word read
  * by stratum_device_status. */

@@ -17,8 +17,12 @@
 //   PLAIN  : y[t, n] (* rw[t] when given), stored row-masked through a
 //            swizzled staging tile;
 //   SWIGLU : a tile pairs 64 gate rows with the matching 64 up rows of W_gu, so
-//            h[t, j] = silu(gate) * up is formed from the fp32 accumulators and
-//            only h (half the width of gate_up) is written.
+//            h[t, j] = silu(gate) * up is formed in the epilogue (from the 16-bit
+//            gate and up, as HF's bf16 forward forms it) and only h -- half the
+//            width of gate_up -- is written, plus gate|up when the backward needs it.
+// A tile whose expert has fewer than 256 tokens left issues MMAs only as wide as
+// those tokens (rounded up to 16), so the tail tiles of skewed routing cost
+// tensor-core time in proportion to their tokens.
 #include "common.cuh"
 #include "nf4_decode.cuh"
 #include "sm100.cuh"
@@ -118,15 +122,43 @@ k_build_tiles(const int *__restrict__ offsets, int E, int m_tiles, int64_t Ttot,
     }
 }
 
+// Tokens of a tile that belong to its expert, and the MMA width that covers
+// them (a multiple of 16, at most BN): a tail tile of a few tokens issues a
+// narrow MMA instead of a full 256-column one.
+__device__ __forceinline__ int tile_cols(const Tile &t) { return t.t_end - t.t0 < BN ? t.t_end - t.t0 : BN; }
+__device__ __forceinline__ int tile_mma_n(const Tile &t) { return (tile_cols(t) + 15) & ~15; }
+
+template <bool BF16>
+__device__ __forceinline__ void unpack8(const uint4 v, float f[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (BF16) {
+            f[2 * i] = __uint_as_float(w[i] << 16);
+            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        } else {
+            const float2 h = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+            f[2 * i] = h.x;
+            f[2 * i + 1] = h.y;
+        }
+    }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint4 pack8(const float f[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = BF16 ? pack_bf16x2(f[2 * i], f[2 * i + 1]) : pack_f16x2(f[2 * i], f[2 * i + 1]);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // ------------------------------------------------------------- forward --
 
 constexpr int F_XS = 4, F_WS = 6, F_AS = 8;
 constexpr int F_W_BYTES = BM * BK / 2;
-constexpr int F_STAGE_BYTES = BN * BM * 2;                 // plain: [256 tokens][128 rows] 16-bit, 2 swizzled halves
-constexpr int F_SWIGLU_STAGE = BM * 33 * 4;                 // swiglu: fp32 [128 rows][32 tokens + 1 pad]
+constexpr int F_STAGE_BYTES = BN * BM * 2;  // [256 tokens][128 rows] 16-bit, 2 swizzled halves
 constexpr int F_SMEM = 1024 + F_XS * X_BYTES + F_STAGE_BYTES + F_WS * F_W_BYTES + 512 + 1088;
 static_assert(F_SMEM <= 232448, "smem");
-static_assert(F_SWIGLU_STAGE <= F_STAGE_BYTES, "smem");
 
 struct FwdParams {
     const Tile *tiles;
@@ -227,10 +259,10 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = idesc_f16(BF16, BM, BN);
             uint32_t it = 0;
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                const uint32_t idesc = idesc_f16(BF16, BM, tile_mma_n(tile_at(tl)));
                 if (!mbar_wait(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
@@ -307,101 +339,84 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
             if (!__all_sync(0xffffffffu, mbar_wait(accfull, tl & 1, p.status, kErrTimeoutEpilogue))) break;
             tc_fence_after();
             const Tile t = tile_at(tl);
-            const int ncols = t.t_end - t.t0 < BN ? t.t_end - t.t0 : BN;  // tokens of this expert in the tile
-            if constexpr (SWIGLU) {
-                float *F = reinterpret_cast<float *>(y0);  // [128 rows][33]
-                const int row = q * 32 + lane;
-                const int I = half_rows;
+            const int ncols = tile_cols(t);          // tokens of this expert in the tile
+            const int nb = tile_mma_n(t) / 16;       // accumulator column blocks the MMA wrote
+            // TMEM -> registers as 16x256b fragments (row = weight row, pairs of tokens)
+            // -> 16-bit -> stmatrix.trans into the [token][row] staging tile (two
+            // 128B-swizzled halves of 64 rows); the accumulator is released as soon as
+            // it has been read, so the next tile's MMAs overlap the rest of the epilogue.
+            named_bar_sync(1, 128);  // previous tile's readers are done with the staging tile
+            const int kq = lane >> 3, jr = lane & 7;
+            const int tok_in = jr + 8 * (kq >> 1);
+            const int nrow = q * 32 + 8 * (kq & 1);
 #pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(tmem + lane_addr + c * 32, v);
-                    tmem_ld_wait();
-                    if (c == BN / 32 - 1) {
-                        tc_fence_before();
-                        mbar_arrive(accempty);
+            for (int cb = 0; cb < nb; ++cb) {
+                uint32_t v[2][8];
+                tmem_ld_16x256b_x2(tmem + lane_addr + cb * 16, v[0]);
+                tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + cb * 16, v[1]);
+                tmem_ld_wait();
+                if (cb == nb - 1) {
+                    tc_fence_before();
+                    mbar_arrive(accempty);
+                }
+                float s0 = 1.f, s1 = 1.f, s2 = 1.f, s3 = 1.f;  // routing weights of this thread's 4 tokens
+                if (!SWIGLU && p.rw) {
+                    const int tk = cb * 16 + 2 * (lane & 3);
+                    s0 = tk < ncols ? p.rw[t.t0 + tk] : 0.f;
+                    s1 = tk + 1 < ncols ? p.rw[t.t0 + tk + 1] : 0.f;
+                    s2 = tk + 8 < ncols ? p.rw[t.t0 + tk + 8] : 0.f;
+                    s3 = tk + 9 < ncols ? p.rw[t.t0 + tk + 9] : 0.f;
+                }
+                const int tok = cb * 16 + tok_in;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t x4[4];
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        const float sa = (m < 2) ? s0 : s2, sb = (m < 2) ? s1 : s3;
+                        const float lo = __uint_as_float(v[h][2 * m]) * sa;
+                        const float hi = __uint_as_float(v[h][2 * m + 1]) * sb;
+                        x4[m] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
                     }
-                    named_bar_sync(1, 128);  // previous chunk's readers are done with F
+                    const int nr = nrow + 16 * h;
+                    const int half = nr >> 6, chunk = (nr & 63) >> 3;
+                    const uint8_t *dst = y0 + half * (F_STAGE_BYTES / 2) + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+                    stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
+                }
+            }
+            named_bar_sync(1, 128);
+            if constexpr (SWIGLU) {
+                // staging half 0 holds the tile's 64 gate rows, half 1 the matching 64 up
+                // rows: h = silu(gate) * up from the 16-bit gate and up (the values HF's
+                // bf16 forward multiplies), 8 columns per 16-byte chunk
+                const int I = half_rows;
+                for (int idx = etid; idx < ncols * 8; idx += 128) {
+                    const int tok = idx >> 3, chunk = idx & 7;
+                    const int off = tok * 128 + ((chunk ^ (tok & 7)) << 4);
+                    const uint4 gv = *reinterpret_cast<const uint4 *>(y0 + off);
+                    const uint4 uv = *reinterpret_cast<const uint4 *>(y0 + F_STAGE_BYTES / 2 + off);
+                    float g[8], u[8], h[8];
+                    unpack8<BF16>(gv, g);
+                    unpack8<BF16>(uv, u);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) F[row * 33 + i] = __uint_as_float(v[i]);
-                    named_bar_sync(1, 128);
-                    // 32 tokens x 32 row pairs: thread -> (token, pair) with 32 threads per token row
-#pragma unroll 1
-                    for (int idx = etid; idx < 32 * 32; idx += 128) {
-                        const int tt = idx >> 5, jp = idx & 31;
-                        const int tok = c * 32 + tt;
-                        if (tok < ncols) {
-                            float h[2], g[2], up[2];
-#pragma unroll
-                            for (int u = 0; u < 2; ++u) {
-                                g[u] = F[(2 * jp + u) * 33 + tt];
-                                up[u] = F[(64 + 2 * jp + u) * 33 + tt];
-                                h[u] = g[u] / (1.f + __expf(-g[u])) * up[u];
-                            }
-                            const int64_t trow = t.t0 + tok;
-                            const uint32_t pk = BF16 ? pack_bf16x2(h[0], h[1]) : pack_f16x2(h[0], h[1]);
-                            *reinterpret_cast<uint32_t *>(p.y + trow * I + t.m * 64 + 2 * jp) = pk;
-                            if (p.gu) {  // gate and up themselves, in gate_up's [gate | up] column order
-                                uint16_t *gr = p.gu + trow * (2 * I) + t.m * 64 + 2 * jp;
-                                *reinterpret_cast<uint32_t *>(gr) = BF16 ? pack_bf16x2(g[0], g[1]) : pack_f16x2(g[0], g[1]);
-                                *reinterpret_cast<uint32_t *>(gr + I) =
-                                    BF16 ? pack_bf16x2(up[0], up[1]) : pack_f16x2(up[0], up[1]);
-                            }
-                        }
+                    for (int i = 0; i < 8; ++i) h[i] = g[i] / (1.f + __expf(-g[i])) * u[i];
+                    const int64_t trow = t.t0 + tok;
+                    *reinterpret_cast<uint4 *>(p.y + trow * I + t.m * 64 + chunk * 8) = pack8<BF16>(h);
+                    if (p.gu) {  // gate and up themselves, in gate_up's [gate | up] column order
+                        uint16_t *gr = p.gu + trow * (2 * I) + t.m * 64 + chunk * 8;
+                        *reinterpret_cast<uint4 *>(gr) = gv;
+                        *reinterpret_cast<uint4 *>(gr + I) = uv;
                     }
                 }
             } else {
-                // stmatrix.trans into [256 tokens][128 rows] (two 128B-swizzled halves), then
-                // row-masked 16-byte copies to y (only this expert's tokens are stored)
-                named_bar_sync(1, 128);  // previous tile's copy-out is done with the staging tile
-                const int kq = lane >> 3, jr = lane & 7;
-                const int tok_in = jr + 8 * (kq >> 1);
-                const int nrow = q * 32 + 8 * (kq & 1);
-#pragma unroll 1
-                for (int cb = 0; cb < BN / 16; ++cb) {
-                    uint32_t v[2][8];
-                    tmem_ld_16x256b_x2(tmem + lane_addr + cb * 16, v[0]);
-                    tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + cb * 16, v[1]);
-                    tmem_ld_wait();
-                    if (cb == BN / 16 - 1) {
-                        tc_fence_before();
-                        mbar_arrive(accempty);
-                    }
-                    float s0 = 1.f, s1 = 1.f, s2 = 1.f, s3 = 1.f;  // routing weights of this thread's 4 tokens
-                    if (p.rw) {
-                        const int tk = cb * 16 + 2 * (lane & 3);
-                        s0 = tk < ncols ? p.rw[t.t0 + tk] : 0.f;
-                        s1 = tk + 1 < ncols ? p.rw[t.t0 + tk + 1] : 0.f;
-                        s2 = tk + 8 < ncols ? p.rw[t.t0 + tk + 8] : 0.f;
-                        s3 = tk + 9 < ncols ? p.rw[t.t0 + tk + 9] : 0.f;
-                    }
-                    const int tok = cb * 16 + tok_in;
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        uint32_t x4[4];
-#pragma unroll
-                        for (int m = 0; m < 4; ++m) {
-                            const float sa = (m < 2) ? s0 : s2, sb = (m < 2) ? s1 : s3;
-                            const float lo = __uint_as_float(v[h][2 * m]) * sa;
-                            const float hi = __uint_as_float(v[h][2 * m + 1]) * sb;
-                            x4[m] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
-                        }
-                        const int nr = nrow + 16 * h;
-                        const int half = nr >> 6, chunk = (nr & 63) >> 3;
-                        const uint8_t *dst = y0 + half * (F_STAGE_BYTES / 2) + tok * 128 + ((chunk ^ (tok & 7)) << 4);
-                        stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
-                    }
-                }
-                named_bar_sync(1, 128);
-                // 256 tokens x 16 chunks of 16 B; 128 threads -> 8 threads per 128-byte half row
-                for (int idx = etid; idx < BN * 16; idx += 128) {
+                // row-masked 16-byte copies to y (only this expert's tokens are stored):
+                // 16 chunks of 16 B per token, 8 threads per 128-byte half row
+                for (int idx = etid; idx < ncols * 16; idx += 128) {
                     const int tok = idx >> 4, hc = idx & 15, half = hc >> 3, chunk = hc & 7;
-                    if (tok < ncols) {
-                        const uint4 val = *reinterpret_cast<const uint4 *>(y0 + half * (F_STAGE_BYTES / 2) + tok * 128 +
-                                                                           ((chunk ^ (tok & 7)) << 4));
-                        *reinterpret_cast<uint4 *>(p.y + int64_t(t.t0 + tok) * p.N_e + t.m * BM + half * 64 +
-                                                   chunk * 8) = val;
-                    }
+                    const uint4 val = *reinterpret_cast<const uint4 *>(y0 + half * (F_STAGE_BYTES / 2) + tok * 128 +
+                                                                       ((chunk ^ (tok & 7)) << 4));
+                    *reinterpret_cast<uint4 *>(p.y + int64_t(t.t0 + tok) * p.N_e + t.m * BM + half * 64 + chunk * 8) =
+                        val;
                 }
             }
         }
@@ -515,10 +530,10 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = idesc_f16_amn(BF16, BM, BN);
             uint32_t it = 0;
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                const uint32_t idesc = idesc_f16_amn(BF16, BM, tile_mma_n(tile_at(tl)));
                 const int ab = tl & 1;
                 if (!mbar_wait(&accempty[ab], ((tl >> 1) & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                 tc_fence_after();
@@ -601,16 +616,17 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
             if (!__all_sync(0xffffffffu, mbar_wait(&accfull[ab], (tl >> 1) & 1, p.status, kErrTimeoutEpilogue))) break;
             tc_fence_after();
             const Tile t = tile_at(tl);
-            const int ncols = t.t_end - t.t0 < BN ? t.t_end - t.t0 : BN;
+            const int ncols = tile_cols(t);
+            const int nb = tile_mma_n(t) / 16;  // accumulator column blocks the MMA wrote
             const uint32_t acc = tmem + lane_addr + uint32_t(ab * 256);
             named_bar_sync(1, 128);
 #pragma unroll 1
-            for (int cb = 0; cb < BN / 16; ++cb) {
+            for (int cb = 0; cb < nb; ++cb) {
                 uint32_t v[2][8];
                 tmem_ld_16x256b_x2(acc + cb * 16, v[0]);
                 tmem_ld_16x256b_x2(acc + (16u << 16) + cb * 16, v[1]);
                 tmem_ld_wait();
-                if (cb == BN / 16 - 1) {
+                if (cb == nb - 1) {
                     tc_fence_before();
                     mbar_arrive(&accempty[ab]);
                 }
@@ -631,10 +647,10 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
             }
             named_bar_sync(1, 128);
             const int k0 = t.m * BM;
-            for (int idx = etid; idx < BN * 16; idx += 128) {
+            for (int idx = etid; idx < ncols * 16; idx += 128) {
                 const int tok = idx >> 4, hc = idx & 15, half = hc >> 3, chunk = hc & 7;
                 const int col = k0 + half * 64 + chunk * 8;
-                if (tok < ncols && col < p.K) {
+                if (col < p.K) {
                     const uint4 val = *reinterpret_cast<const uint4 *>(y0 + half * (D_STAGE_BYTES / 2) + tok * 128 +
                                                                        ((chunk ^ (tok & 7)) << 4));
                     *reinterpret_cast<uint4 *>(p.dx + int64_t(t.t0 + tok) * p.K + col) = val;
