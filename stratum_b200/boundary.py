@@ -1,0 +1,142 @@
+"""Pipeline boundaries: activations forward, gradients backward, GPU to GPU.
+
+Replaces the reference's host-staged boundary (stratum/host_staging.py:72-200,
+``HostStagingPool.transfer`` / ``transfer_async``: peer copy when available,
+else device -> pinned host -> device with a host sync) and its gradient hook
+(stratum/grad_hooks.py:8-30, ``make_boundary_hook``).  On an NVSwitch box every
+GPU reaches every other at full NVLink bandwidth, so no path goes through host
+memory:
+
+* one process driving several GPUs (``StratumPipeline``): a boundary is a
+  device-to-device copy on the destination's current stream, ordered after the
+  source's pending work by an event, and differentiable -- the gradient flows
+  back through the same kind of copy;
+* one process per GPU (``RankPipeline``): a boundary is an NCCL ``send`` /
+  ``recv`` pair between adjacent ranks (:class:`P2PChannel`), activations
+  forward and gradients backward, enqueued on the ranks' compute streams so the
+  host never waits for them.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+
+def _device(d) -> torch.device:
+    if isinstance(d, torch.device):
+        return d
+    if isinstance(d, str):
+        return torch.device(d)
+    return torch.device("cuda", int(d))
+
+
+class _DeviceCopy(torch.autograd.Function):
+    """``x`` copied to ``dst`` after the source device's current work; the
+    backward copies the gradient back the same way."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, dst: torch.device):
+        ctx.src = x.device
+        return _copy_after(x, dst)
+
+    @staticmethod
+    def backward(ctx, g: torch.Tensor):
+        return _copy_after(g, ctx.src), None
+
+
+def _copy_after(x: torch.Tensor, dst: torch.device) -> torch.Tensor:
+    if x.device == dst:
+        return x
+    if x.is_cuda and dst.type == "cuda":
+        # the destination stream waits for the source stream's pending writes of x
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(x.device))
+        out_stream = torch.cuda.current_stream(dst)
+        out_stream.wait_event(ev)
+        with torch.cuda.device(dst), torch.cuda.stream(out_stream):
+            out = torch.empty_like(x, device=dst)
+            out.copy_(x, non_blocking=True)  # peer copy over NVLink
+        # x must outlive the copy, which runs on the destination's stream
+        x.record_stream(out_stream)
+        return out
+    return x.to(dst)
+
+
+def transfer(x: torch.Tensor, dst_device) -> torch.Tensor:
+    """Move a boundary activation to ``dst_device`` (differentiable)."""
+    dst = _device(dst_device)
+    if x.device == dst:
+        return x
+    if x.requires_grad:
+        return _DeviceCopy.apply(x, dst)
+    return _copy_after(x, dst)
+
+
+class DeviceTransferPool:
+    """Drop-in for ``HostStagingPool`` (stratum/host_staging.py:47-200): same
+    ``transfer`` / ``transfer_async`` calls, but a direct device-to-device copy
+    with no host staging buffer and no host synchronisation."""
+
+    def ensure(self, size_bytes: int) -> None:  # no staging buffer to grow
+        return None
+
+    def transfer(self, tensor: torch.Tensor, dst_device, src_device=None) -> torch.Tensor:
+        return transfer(tensor, dst_device)
+
+    def transfer_async(self, tensor: torch.Tensor, dst_device, src_device=None):
+        out = transfer(tensor, dst_device)
+        ev = None
+        if out.is_cuda:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(out.device))
+        return out, ev
+
+
+def make_boundary_hook(prev_device, next_device, pool: Optional[DeviceTransferPool] = None):
+    """Gradient hook moving a boundary gradient from ``next_device`` back to
+    ``prev_device`` (stratum/grad_hooks.py:8-30), by a direct device copy."""
+    prev = _device(prev_device)
+
+    def hook(grad: torch.Tensor) -> torch.Tensor:
+        return _copy_after(grad, prev)
+
+    return hook
+
+
+class P2PChannel:
+    """NCCL point-to-point boundary between this rank and its pipeline neighbours.
+
+    ``send_forward`` / ``recv_forward`` carry the stage output to the next rank;
+    ``send_backward`` / ``recv_backward`` carry the gradient of the stage input
+    to the previous rank.  Every call is issued in the same order on both ends
+    (the schedule guarantees it); NCCL runs the transfer on its own stream,
+    ordered after the caller's current stream, and the received tensor is
+    ordered before the caller's next work, so the host does not block.
+    """
+
+    def __init__(self, rank: int, world: int, group=None):
+        self.rank, self.world, self.group = rank, world, group
+        self.prev = rank - 1 if rank > 0 else None
+        self.next = rank + 1 if rank + 1 < world else None
+
+    def _peer(self, r: int) -> int:
+        return dist.get_global_rank(self.group, r) if self.group is not None else r
+
+    def send_forward(self, x: torch.Tensor) -> None:
+        dist.send(x.contiguous(), self._peer(self.next), group=self.group)
+
+    def recv_forward(self, shape, dtype, device) -> torch.Tensor:
+        buf = torch.empty(shape, dtype=dtype, device=device)
+        dist.recv(buf, self._peer(self.prev), group=self.group)
+        return buf
+
+    def send_backward(self, g: torch.Tensor) -> None:
+        dist.send(g.contiguous(), self._peer(self.prev), group=self.group)
+
+    def recv_backward(self, shape, dtype, device) -> torch.Tensor:
+        buf = torch.empty(shape, dtype=dtype, device=device)
+        dist.recv(buf, self._peer(self.next), group=self.group)
+        return buf

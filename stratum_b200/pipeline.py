@@ -1,0 +1,488 @@
+"""Layer-parallel pipeline over the NF4 decoder layers.
+
+Two drivers over the same pieces:
+
+* :class:`StratumPipeline` -- the reference's class (stratum/pipeline.py:81-1115):
+  one process drives every GPU; ``forward(input_ids, attention_mask, labels)``
+  returns the loss and the caller runs ``loss.backward()``.  Stage boundaries
+  are direct NVLink copies (``boundary.transfer``) instead of host staging.
+* :class:`RankPipeline` -- one process per GPU (``torch.distributed``, NCCL):
+  each rank holds one stratum of layers (``assign.strata``); ``train_step``
+  runs a GPipe schedule over microbatches, boundary activations and gradients
+  move by NCCL send/recv (``boundary.P2PChannel``).  This is how the path
+  scales over the GPUs of one box.
+
+Both keep the reference's memory model (stratum/runtime.py:195-290,
+``anchor_explicit_group_backward``): a group of layers runs forward without an
+autograd graph and saves only its input; its backward recomputes the group and
+backpropagates through it.  Groups are single layers here.  With streamed NF4
+weights (fused-mode ``NF4Linear`` fed by ``upload.ensure_weights``), layer i+1
+uploads on a side stream while layer i computes (stratum/stage.py:51-137);
+``StratumPipeline`` frees a layer after its forward and uploads it again for
+its backward (as the reference does), ``RankPipeline`` uploads its stratum once
+per step, overlapped with the first microbatch, and frees it at the end.
+
+MoE layers: the router aux loss (HF ``load_balancing_loss_func``, the
+reference's stratum/moe.py:162-223) is a function of per-expert counts and
+summed router probabilities over every layer; the forward accumulates those
+sums (all-reduced across ranks), and each layer's recompute adds the aux
+term's gradient to its backward.
+"""
+
+from __future__ import annotations
+
+from contextlib import nullcontext
+from dataclasses import dataclass, field
+from typing import Any, Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from .boundary import P2PChannel, transfer
+from .nf4_linear import NF4Linear
+from .stage import DeviceStage
+from .upload import ensure_weights, free_weights
+
+
+def _dev(d) -> torch.device:
+    if isinstance(d, torch.device):
+        return d
+    if isinstance(d, str):
+        return torch.device(d)
+    return torch.device("cuda", int(d))
+
+
+def _on(device: torch.device):
+    """``torch.cuda.device`` for a CUDA device, nothing for the CPU (gloo tests)."""
+    return torch.cuda.device(device) if device.type == "cuda" else nullcontext()
+
+
+def _move_tree(value: Any, device: torch.device) -> Any:
+    if torch.is_tensor(value):
+        return value.to(device, non_blocking=True)
+    if isinstance(value, tuple):
+        return tuple(_move_tree(v, device) for v in value)
+    if isinstance(value, list):
+        return [_move_tree(v, device) for v in value]
+    if isinstance(value, dict):
+        return {k: _move_tree(v, device) for k, v in value.items()}
+    return value
+
+
+def _device_tensors(module: nn.Module) -> list[torch.Tensor]:
+    out = []
+    for m in module.modules():
+        if isinstance(m, NF4Linear) and m.quantized is not None:
+            out.append(m.quantized)
+            qs = m.quant_state
+            for t in (qs.absmax, qs.code, qs.offset):
+                if torch.is_tensor(t):
+                    out.append(t)
+            if qs.state2 is not None:
+                out += [t for t in (qs.state2.absmax, qs.state2.code) if torch.is_tensor(t)]
+    return out
+
+
+def _needs_streaming(module: nn.Module, device: torch.device) -> bool:
+    return any(isinstance(m, NF4Linear) and m.streamed and not m.device_state_on(device) for m in module.modules())
+
+
+# --------------------------------------------------------------------------------
+# weight streaming
+# --------------------------------------------------------------------------------
+
+class _Streamer:
+    """Per-layer NF4 upload on a side stream with event fences.
+
+    ``acquire(i)`` makes the compute stream wait for layer i's upload (issuing it
+    if nobody did); ``prefetch(i)`` issues it early; ``release(i)`` drops the
+    device copy once the compute stream is done with it (the blocks are marked
+    as used by that stream, so the allocator does not hand them to the next
+    upload early)."""
+
+    def __init__(self, layers: list[nn.Module], device: torch.device, enabled: bool):
+        self.layers, self.device = layers, device
+        self.enabled = bool(enabled) and device.type == "cuda"
+        self.stream = torch.cuda.Stream(device) if self.enabled else None
+        self.pending: dict[int, torch.cuda.Event] = {}
+        self.resident: set[int] = set()
+
+    def prefetch(self, i: int) -> None:
+        if not self.enabled or not (0 <= i < len(self.layers)) or i in self.pending or i in self.resident:
+            return
+        with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
+            ensure_weights(self.layers[i], self.device)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        self.pending[i] = ev
+
+    def acquire(self, i: int) -> None:
+        if not self.enabled or i in self.resident:
+            return
+        self.prefetch(i)
+        torch.cuda.current_stream(self.device).wait_event(self.pending.pop(i))
+        self.resident.add(i)
+
+    def release(self, i: int) -> None:
+        if not self.enabled or i not in self.resident:
+            return
+        cur = torch.cuda.current_stream(self.device)
+        for t in _device_tensors(self.layers[i]):
+            t.record_stream(cur)
+        free_weights(self.layers[i])
+        self.resident.discard(i)
+
+    def release_all(self) -> None:
+        for i in list(self.resident):
+            self.release(i)
+        self.pending.clear()
+
+
+# --------------------------------------------------------------------------------
+# router aux loss bookkeeping
+# --------------------------------------------------------------------------------
+
+@dataclass
+class _AuxState:
+    """Per-expert sums of one microbatch's router outputs over the layers seen so
+    far; ``finalize`` turns global sums into the aux term's gradient weights."""
+
+    n_experts: int
+    coef: float
+    counts: Optional[torch.Tensor] = None
+    psum: Optional[torch.Tensor] = None
+    rows: float = 0.0
+    weight: Optional[torch.Tensor] = None
+    value: Optional[torch.Tensor] = None
+    extra: list = field(default_factory=list)
+
+    def add(self, probs: torch.Tensor, indices: torch.Tensor) -> None:
+        from .decoder import load_balancing_terms
+
+        c, p = load_balancing_terms(probs.detach(), indices, self.n_experts)
+        self.counts = c if self.counts is None else self.counts + c
+        self.psum = p if self.psum is None else self.psum + p
+        self.rows += float(probs.shape[0])
+
+    def finalize(self, counts: torch.Tensor, psum: torch.Tensor, rows, grad_scale: float = 1.0) -> None:
+        # loss = E / N^2 * sum_e count_e * psum_e, psum_e = sum over rows of softmax(router output)_e,
+        # so d loss / d softmax(router output)[row, e] = E / N^2 * count_e (times the weight of this
+        # microbatch's loss in the step's loss)
+        n2 = torch.as_tensor(rows, dtype=torch.float32, device=counts.device).clamp_min(1.0) ** 2
+        self.value = self.coef * self.n_experts * (counts * psum).sum() / n2
+        self.weight = (self.coef * self.n_experts * grad_scale) * counts / n2
+
+
+class _Runner:
+    """Runs layers [i0, i1) of a stage on the 7-tuple, with streaming and router taps."""
+
+    def __init__(self, layers: list[nn.Module], i0: int, i1: int, rest: tuple, streamer: _Streamer,
+                 policy: str, sink=None, aux: Optional[_AuxState] = None, offload: bool = False):
+        self.layers, self.i0, self.i1, self.rest = layers, i0, i1, rest
+        self.streamer, self.policy, self.sink, self.aux, self.offload = streamer, policy, sink, aux, offload
+
+    def _run(self, hidden: torch.Tensor, collect_grad_probs: Optional[list]) -> torch.Tensor:
+        t = (hidden,) + self.rest
+        for i in range(self.i0, self.i1):
+            if self.sink is not None:
+                self.sink.clear()
+                self.sink.active = True
+            try:
+                t = self.layers[i](t)
+            finally:
+                if self.sink is not None:
+                    self.sink.active = False
+            if self.sink is not None:
+                for probs, idx in zip(self.sink.probs, self.sink.indices):
+                    if collect_grad_probs is None:
+                        self.aux.add(probs, idx)
+                    else:
+                        collect_grad_probs.append(probs)
+                self.sink.clear()
+        return t[0]
+
+    def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+        s = self.streamer
+        for i in range(self.i0, self.i1):
+            s.acquire(i)
+        s.prefetch(self.i1)
+        out = self._run(hidden, None)
+        if self.policy == "group":  # reference behaviour: free after forward, upload again for backward
+            last = len(self.layers) - 1
+            for i in range(self.i0, self.i1):
+                if i != last:
+                    s.release(i)
+        return out
+
+    def recompute(self, x: torch.Tensor):
+        s = self.streamer
+        for i in range(self.i0, self.i1):
+            s.acquire(i)
+        s.prefetch(self.i0 - 1)
+        probs: Optional[list] = [] if self.sink is not None else None
+        out = self._run(x, probs)
+        extra = []
+        if probs and self.aux is not None and self.aux.weight is not None:
+            term = sum((torch.softmax(p.float(), dim=-1) * self.aux.weight.to(p.device)).sum() for p in probs)
+            if term.requires_grad:  # else the term reaches no trainable parameter
+                extra.append(term)
+        return out, extra
+
+    def after_backward(self) -> None:
+        if self.policy == "group":
+            for i in range(self.i0, self.i1):
+                self.streamer.release(i)
+
+
+class _Anchor(torch.autograd.Function):
+    """Output of a layer group computed without a graph; its backward recomputes
+    the group from the saved input and backpropagates (LoRA gradients accumulate
+    into the parameters directly).  The group's trainable parameters are inputs
+    only so that the output requires grad when the input does not."""
+
+    @staticmethod
+    def forward(ctx, runner: _Runner, hidden: torch.Tensor, *params):
+        ctx.runner = runner
+        ctx.in_grad = hidden.requires_grad
+        saved = hidden.detach()
+        if runner.offload and saved.is_cuda:
+            saved = saved.to("cpu")
+        ctx.saved_hidden = saved
+        ctx.n_params = len(params)
+        with torch.no_grad():
+            out = runner.forward(hidden)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad: torch.Tensor):
+        runner: _Runner = ctx.runner
+        h = ctx.saved_hidden
+        if h.device != grad.device:
+            h = h.to(grad.device)
+        x = h.detach().requires_grad_(ctx.in_grad)
+        with torch.enable_grad():
+            out, extra = runner.recompute(x)
+        outs = [out] + extra
+        grads = [grad] + [torch.ones((), dtype=e.dtype, device=e.device) for e in extra]
+        torch.autograd.backward(outs, grads)
+        runner.after_backward()
+        ctx.runner = None
+        ctx.saved_hidden = None
+        return (None, x.grad if ctx.in_grad else None) + (None,) * ctx.n_params
+
+
+def _trainable(modules: list[nn.Module]) -> list[torch.Tensor]:
+    return [p for m in modules for p in m.parameters() if p.requires_grad]
+
+
+def _stage_layers(stage) -> list[nn.Module]:
+    return list(stage.layers)
+
+
+def _run_stage(stage, hidden: torch.Tensor, rest: tuple, streamer: _Streamer, policy: str, sink, aux,
+               offload: bool) -> torch.Tensor:
+    layers = _stage_layers(stage)
+    for i in range(len(layers)):
+        runner = _Runner(layers, i, i + 1, rest, streamer, policy, sink, aux, offload)
+        hidden = _Anchor.apply(runner, hidden, *_trainable([layers[i]]))
+    return hidden
+
+
+# --------------------------------------------------------------------------------
+# one process, several GPUs (the reference's class)
+# --------------------------------------------------------------------------------
+
+class StratumPipeline(nn.Module):
+    """A multi-GPU pipeline of DeviceStages driven by one process.
+
+    Same constructor and calls as the reference (stratum/pipeline.py:90-99,
+    646-652, 1027, 1073).  ``prefix`` runs on the first stage's device, each
+    stage on its own device, ``postfix`` on the last stage's device; boundaries
+    are NVLink device copies; every layer is a recompute group.  ``execute_plan``
+    is accepted for compatibility; the grouping is always one layer.
+    ``prefetch_nf4`` is accepted too: streamed layers always upload on a side
+    stream, one layer ahead.  ``offload_stage_inputs`` keeps each group's saved
+    input in host memory.  For MoE models pass the ``router_sink`` the layers
+    were built with and the aux-loss coefficient.
+    """
+
+    def __init__(self, prefix: nn.Module, stages: list, postfix: nn.Module, *, prefetch_nf4: bool = False,
+                 offload_stage_inputs: bool = False, execute_plan: Any = None, router_sink=None,
+                 router_aux_coef: float = 0.0, n_experts: int = 0):
+        super().__init__()
+        self.prefix = prefix
+        self.stages = nn.ModuleList(stages)
+        self.postfix = postfix
+        self.prefetch_nf4 = prefetch_nf4
+        self.offload_stage_inputs = offload_stage_inputs
+        self.execute_plan = execute_plan
+        self.router_sink = router_sink
+        self.router_aux_coef = float(router_aux_coef)
+        self.n_experts = int(n_experts)
+        self._streamers = [
+            _Streamer(_stage_layers(s), _dev(s.device_id), any(_needs_streaming(l, _dev(s.device_id))
+                                                               for l in s.layers))
+            for s in stages]
+        self.last_aux: Optional[torch.Tensor] = None
+
+    @property
+    def n_devices(self) -> int:
+        return len({int(_dev(s.device_id).index or 0) for s in self.stages})
+
+    def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
+                labels: Optional[torch.Tensor] = None, **kwargs):
+        """Run forward through all stages; returns the loss when labels are given."""
+        dev0 = _dev(self.stages[0].device_id)
+        if input_ids.device != dev0:
+            input_ids = input_ids.to(dev0, non_blocking=True)
+        if labels is not None and labels.device != dev0:
+            labels = labels.to(dev0, non_blocking=True)
+        if attention_mask is not None and attention_mask.device != dev0:
+            attention_mask = attention_mask.to(dev0, non_blocking=True)
+        tup = self.prefix(input_ids=input_ids, attention_mask=attention_mask, labels=labels, **kwargs)
+        aux = _AuxState(self.n_experts, self.router_aux_coef) if (self.router_sink is not None and
+                                                                  self.router_aux_coef) else None
+        sink = self.router_sink if aux is not None else None
+        hidden, rest = tup[0], tup[1:]
+        for si, stage in enumerate(self.stages):
+            dev = _dev(stage.device_id)
+            if hidden.device != dev:
+                hidden = transfer(hidden, dev)
+                rest = _move_tree(rest, dev)
+            with _on(dev):
+                hidden = _run_stage(stage, hidden, rest, self._streamers[si], "group", sink, aux,
+                                    self.offload_stage_inputs)
+        last = _dev(self.stages[-1].device_id)
+        with _on(last):
+            loss = self.postfix((hidden,) + tuple(rest))
+        if aux is not None and aux.counts is not None:
+            aux.finalize(aux.counts, aux.psum, aux.rows)
+            self.last_aux = aux.value.detach()
+            if loss is not None:
+                loss = loss + aux.value.detach().to(loss.device)
+        return loss
+
+    def free_all_weights(self) -> None:
+        """Drop every streamed layer's device copy (reference: call after backward)."""
+        for s in self._streamers:
+            s.release_all()
+        for stage in self.stages:
+            free_weights(stage)
+
+    def forward_batch(self, batch: Any, *, ignore_index: int = -100):
+        """Forward on a dict-like batch with ``input_ids`` / ``attention_mask`` / ``labels``."""
+        get = (lambda k: batch[k]) if isinstance(batch, dict) else (lambda k: getattr(batch, k))
+        return self(get("input_ids"), attention_mask=get("attention_mask"), labels=get("labels"))
+
+
+# --------------------------------------------------------------------------------
+# one process per GPU
+# --------------------------------------------------------------------------------
+
+class RankPipeline(nn.Module):
+    """This rank's stratum of a layer-parallel pipeline (one process per GPU).
+
+    Every rank holds a ``prefix`` for its rotary context (rank 0's also embeds
+    tokens); the last rank holds the ``postfix``.  ``train_step`` runs forward
+    and backward over ``microbatches`` sequences with a GPipe schedule: all
+    forwards (each rank sends its stratum's output to the next rank as soon as
+    it is computed), then all backwards in reverse order (gradients go back the
+    same way).  Input ids are read on rank 0, labels on the last rank.
+    Returns the mean loss on the last rank, ``None`` elsewhere.
+    """
+
+    def __init__(self, stage: DeviceStage, *, prefix: nn.Module, postfix: Optional[nn.Module], rank: int,
+                 world: int, group=None, hidden_size: int, offload_stage_inputs: bool = False, router_sink=None,
+                 router_aux_coef: float = 0.0, n_experts: int = 0, hidden_dtype=torch.bfloat16):
+        super().__init__()
+        if (postfix is None) != (rank + 1 < world):
+            raise ValueError("RankPipeline: the postfix lives on the last rank only")
+        self.stage, self.prefix, self.postfix = stage, prefix, postfix
+        self.rank, self.world, self.group = rank, world, group
+        self.device = _dev(stage.device_id)
+        self.hidden_size, self.hidden_dtype = hidden_size, hidden_dtype
+        self.offload = offload_stage_inputs
+        self.router_sink = router_sink
+        self.router_aux_coef = float(router_aux_coef)
+        self.n_experts = int(n_experts)
+        self.chan = P2PChannel(rank, world, group)
+        self.streamer = _Streamer(_stage_layers(stage), self.device,
+                                  any(_needs_streaming(l, self.device) for l in stage.layers))
+        self.last_aux: Optional[torch.Tensor] = None
+
+    def _aux_reduce(self, states: list[_AuxState]) -> None:
+        E = self.n_experts
+        M = len(states)
+        buf = torch.zeros(M, 2 * E + 1, dtype=torch.float32, device=self.device)
+        for m, a in enumerate(states):
+            if a.counts is not None:
+                buf[m, :E] = a.counts
+                buf[m, E:2 * E] = a.psum
+                buf[m, 2 * E] = a.rows
+        if self.world > 1 and dist.is_initialized():
+            dist.all_reduce(buf, group=self.group)
+        for m, a in enumerate(states):  # the step's loss is the mean over its M microbatches
+            a.finalize(buf[m, :E], buf[m, E:2 * E], buf[m, 2 * E], grad_scale=1.0 / M)
+
+    def train_step(self, input_ids: Optional[torch.Tensor] = None, labels: Optional[torch.Tensor] = None, *,
+                   microbatches: int = 1, seq_len: Optional[int] = None):
+        M = int(microbatches)
+        first, last = self.rank == 0, self.rank + 1 == self.world
+        dev = self.device
+        if first:
+            ids = input_ids.reshape(M, 1, -1).to(dev, non_blocking=True)
+            seq_len = ids.shape[-1]
+        if last:
+            labs = labels.reshape(M, 1, -1).to(dev, non_blocking=True)
+            seq_len = labs.shape[-1]
+        if seq_len is None:
+            raise ValueError("RankPipeline.train_step: seq_len is needed on middle ranks")
+        shape = (1, seq_len, self.hidden_size)
+        use_aux = self.router_sink is not None and self.router_aux_coef != 0.0 and self.n_experts > 0
+        sink = self.router_sink if use_aux else None
+        records = []
+        losses = []
+        with _on(dev):
+            for i in range(len(self.stage.layers)):  # the stratum's upload, overlapped with microbatch 0
+                self.streamer.prefetch(i)
+            for m in range(M):
+                if first:
+                    tup = self.prefix(input_ids=ids[m])
+                    h_in = tup[0]
+                else:
+                    h_in = self.chan.recv_forward(shape, self.hidden_dtype, dev).requires_grad_(True)
+                    tup = self.prefix.context(h_in)
+                aux = _AuxState(self.n_experts, self.router_aux_coef) if use_aux else None
+                rest = tup[1:]
+                out = _run_stage(self.stage, h_in, rest, self.streamer, "step", sink, aux, self.offload)
+                if last:
+                    losses.append(self.postfix((out,) + rest[:4] + (labs[m],) + rest[5:]))
+                else:
+                    self.chan.send_forward(out.detach())
+                records.append((h_in, out, aux))
+            aux_states = [r[2] for r in records]
+            if use_aux:
+                self._aux_reduce(aux_states)
+            for m in reversed(range(M)):
+                h_in, out, aux = records[m]
+                if last:
+                    (losses[m] / M).backward()
+                else:
+                    g = self.chan.recv_backward(shape, self.hidden_dtype, dev)
+                    torch.autograd.backward(out, g)
+                if not first:
+                    self.chan.send_backward(h_in.grad)
+                records[m] = None
+            self.streamer.release_all()
+        if use_aux:
+            self.last_aux = torch.stack([r.value for r in aux_states]).mean()
+        if not last:
+            return None
+        loss = torch.stack([l.detach() for l in losses]).mean()
+        if use_aux:
+            loss = loss + self.last_aux.to(loss.device)
+        return loss
+
+
+__all__ = ["StratumPipeline", "RankPipeline"]

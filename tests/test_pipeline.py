@@ -1,0 +1,193 @@
+"""Pipeline schedule and boundary logic on the CPU (no GPU, gloo ranks).
+
+A toy model with the reference's 7-tuple layer interface (frozen weights, a
+trainable low-rank term per layer, and optionally a top-k router whose outputs
+feed the router aux loss) runs through ``StratumPipeline`` (one process) and
+``RankPipeline`` (two gloo ranks, NCCL's role played by gloo send/recv).  Loss
+and every trainable gradient must match plain autograd over the same model:
+the recompute anchors, the boundary gradients and the aux-loss injection are
+exact up to float reassociation."""
+
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+import torch.nn as nn
+import torch.nn.functional as TF
+
+from stratum_b200.decoder import RouterLogitsSink, _RouterTap
+from stratum_b200.pipeline import RankPipeline, StratumPipeline
+from stratum_b200.stage import DeviceStage
+
+H, V, S, E, K = 32, 50, 12, 6, 2
+COEF = 0.05
+
+
+class ToyRouter(nn.Module):
+    def __init__(self, g):
+        super().__init__()
+        self.weight = nn.Parameter(torch.randn(E, H, generator=g) * 0.3, requires_grad=False)
+
+    def forward(self, h):
+        probs = torch.softmax(TF.linear(h, self.weight), dim=-1, dtype=torch.float)
+        top, idx = torch.topk(probs, K, dim=-1)
+        return probs, top, idx
+
+
+class ToyLayer(nn.Module):
+    def __init__(self, i, sink=None):
+        super().__init__()
+        g = torch.Generator().manual_seed(100 + i)
+        self.W = nn.Parameter(torch.randn(H, H, generator=g) / H**0.5, requires_grad=False)
+        self.A = nn.Parameter(torch.randn(4, H, generator=g) * 0.1)
+        self.B = nn.Parameter(torch.randn(H, 4, generator=g) * 0.1)
+        self.gate = _RouterTap(ToyRouter(g), sink) if sink is not None else None
+
+    def forward(self, tup):
+        h = tup[0]
+        y = h + torch.tanh(h @ self.W.t()) + (h @ self.A.t()) @ self.B.t()
+        if self.gate is not None:
+            _, top, _ = self.gate(h.reshape(-1, H))
+            y = y + 0.1 * top.sum(-1).reshape(h.shape[:-1]).unsqueeze(-1).to(y.dtype) * h
+        return (y,) + tuple(tup[1:])
+
+
+class ToyPrefix(nn.Module):
+    def __init__(self):
+        super().__init__()
+        g = torch.Generator().manual_seed(7)
+        self.table = nn.Parameter(torch.randn(V, H, generator=g), requires_grad=False)
+
+    def context(self, hidden, labels=None, **kw):
+        pos = torch.arange(hidden.shape[1]).unsqueeze(0)
+        return (hidden, None, pos, None, kw, labels, 0)
+
+    def forward(self, input_ids=None, attention_mask=None, labels=None, **kw):
+        return self.context(self.table[input_ids], labels=labels)
+
+
+class ToyPostfix(nn.Module):
+    def __init__(self):
+        super().__init__()
+        g = torch.Generator().manual_seed(8)
+        self.head = nn.Parameter(torch.randn(V, H, generator=g) / H**0.5, requires_grad=False)
+
+    def forward(self, tup):
+        h, labels = tup[0], tup[5]
+        logits = h[:, :-1] @ self.head.t()
+        return TF.cross_entropy(logits.reshape(-1, V), labels[:, 1:].reshape(-1))
+
+
+def _model(n_layers, moe, sink=None):
+    return [ToyLayer(i, sink if moe else None) for i in range(n_layers)]
+
+
+def _data(m):
+    g = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, V, (m, S), generator=g)
+    return ids, ids.clone()
+
+
+def _hf_aux(probs):
+    """The reference's load_balancing_loss_func (stratum/moe.py:162-223) restated."""
+    cat = torch.cat(probs, 0)
+    rw = torch.softmax(cat, dim=-1)
+    _, sel = torch.topk(rw, K, dim=-1)
+    mask = TF.one_hot(sel, E).float()
+    return torch.sum(mask.mean(0) * rw.mean(0).unsqueeze(0)) * E
+
+
+def _reference(n_layers, moe, ids, labels):
+    """Plain autograd, microbatch by microbatch; returns (mean loss, grads)."""
+    prefix, postfix = ToyPrefix(), ToyPostfix()
+    sink = RouterLogitsSink()
+    layers = _model(n_layers, moe, sink)
+    total = 0.0
+    M = ids.shape[0]
+    for m in range(M):
+        sink.clear()
+        sink.active = moe
+        tup = prefix(input_ids=ids[m:m + 1], labels=labels[m:m + 1])
+        for l in layers:
+            tup = l(tup)
+        sink.active = False
+        loss = postfix(tup)
+        if moe:
+            loss = loss + COEF * _hf_aux(list(sink.probs))
+        (loss / M).backward()
+        total += float(loss.detach()) / M
+    grads = {f"{i}.{n}": p.grad.clone() for i, l in enumerate(layers) for n, p in l.named_parameters()
+             if p.requires_grad}
+    return total, grads
+
+
+@pytest.mark.parametrize("moe", [False, True])
+def test_single_process_pipeline_matches_autograd(moe):
+    ids, labels = _data(1)
+    ref_loss, ref_grads = _reference(6, moe, ids, labels)
+    sink = RouterLogitsSink()
+    layers = _model(6, moe, sink)
+    stages = [DeviceStage(layers[:2], "cpu"), DeviceStage(layers[2:5], "cpu"), DeviceStage(layers[5:], "cpu")]
+    pipe = StratumPipeline(ToyPrefix(), stages, ToyPostfix(), router_sink=sink if moe else None,
+                           router_aux_coef=COEF if moe else 0.0, n_experts=E)
+    loss = pipe(ids, labels=labels)
+    loss.backward()
+    assert abs(float(loss) - ref_loss) < 1e-5
+    got = {f"{i}.{n}": p.grad for i, l in enumerate(layers) for n, p in l.named_parameters() if p.requires_grad}
+    for k, g in ref_grads.items():
+        torch.testing.assert_close(got[k], g, rtol=1e-4, atol=1e-6, msg=k)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_dir, moe, M, n_layers):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from stratum_b200.assign import assign_layers_to_devices, strata
+
+        sink = RouterLogitsSink()
+        layers = _model(n_layers, moe, sink)
+        parts = strata(assign_layers_to_devices(n_layers, n_devices=world))
+        mine = parts[rank][1]
+        stage = DeviceStage([layers[i] for i in mine], "cpu")
+        pipe = RankPipeline(stage, prefix=ToyPrefix(), postfix=ToyPostfix() if rank == world - 1 else None,
+                            rank=rank, world=world, hidden_size=H, hidden_dtype=torch.float32,
+                            router_sink=sink if moe else None, router_aux_coef=COEF if moe else 0.0,
+                            n_experts=E if moe else 0)
+        ids, labels = _data(M)
+        loss = pipe.train_step(ids if rank == 0 else None, labels if rank == world - 1 else None,
+                               microbatches=M, seq_len=S)
+        grads = {f"{i}.{n}": p.grad for i in mine for n, p in layers[i].named_parameters() if p.requires_grad}
+        torch.save({"loss": None if loss is None else float(loss), "grads": grads},
+                   os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("moe", [False, True])
+def test_two_rank_pipeline_matches_autograd(moe):
+    M, n_layers, world = 3, 5, 2
+    ids, labels = _data(M)
+    ref_loss, ref_grads = _reference(n_layers, moe, ids, labels)
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_rank_main, args=(world, _free_port(), d, moe, M, n_layers), nprocs=world,
+                           start_method="spawn", join=True)
+        outs = [torch.load(os.path.join(d, f"rank{r}.pt")) for r in range(world)]
+    assert outs[0]["loss"] is None
+    assert abs(outs[-1]["loss"] - ref_loss) < 1e-5
+    got = {}
+    for o in outs:
+        got.update(o["grads"])
+    assert set(got) == set(ref_grads)
+    for k, g in ref_grads.items():
+        torch.testing.assert_close(got[k], g, rtol=1e-4, atol=1e-6, msg=k)
