@@ -319,6 +319,9 @@ def run_codec(args, world, rank, local):
     torch.cuda.empty_cache()
     lin = None if args.no_linear else run_linear_metrics(args, world, flush)
     moe = None if args.no_experts else run_experts_metrics(args, world, flush)
+    del flush
+    torch.cuda.empty_cache()
+    pipe = None if args.no_pipeline else run_pipeline_metrics(args, world, rank, local)
     return {
         "metric": "nf4_dequant_GBps",
         "value": round(value, 1),
@@ -346,6 +349,7 @@ def run_codec(args, world, rank, local):
         "clocks": clk,
         "nf4_linear": lin,
         "nf4_moe_experts": moe,
+        "pipeline": pipe,
     }
 
 
@@ -702,6 +706,134 @@ def run_experts(args, world, rank, local):
     }
 
 
+PIPE_SEQ = {"llama3-8b": 8192, "qwen3-0.6b": 2048, "qwen3-30b-a3b": 4096}
+
+
+def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None, steps=None, warmup=None):
+    """Layer-parallel training step of a BASELINE decoder config through RankPipeline.
+
+    Each rank builds only its stratum (``assign.strata``); config 5 (llama3-8b)
+    streams its NF4 + double-quant weights from pinned host every step.  One
+    step = forward + backward of ``microbatches`` sequences (GPipe); tokens/s
+    counts every sequence's tokens once.  Also times the sequential schedule
+    (one sequence per step, the reference's execution) and an end-to-end step
+    whose token ids come from pinned host memory and whose loss is read back.
+    """
+    import torch.distributed as dist
+
+    from stratum_b200 import _lib
+    from stratum_b200 import decoder as D
+    from stratum_b200.assign import assign_layers_to_devices, strata
+    from stratum_b200.pipeline import RankPipeline
+    from stratum_b200.stage import DeviceStage
+
+    model = model or args.model
+    spec = D.SPECS[model]
+    seq = PIPE_SEQ[model]
+    M = int(microbatches or args.microbatches or 4 * world)
+    steps = max(1, int(steps if steps is not None else args.pipe_steps))
+    warmup = max(1, int(warmup if warmup is not None else args.pipe_warmup))
+    dev = torch.device("cuda", local)
+    first, last = rank == 0, rank == world - 1
+    mine = strata(assign_layers_to_devices(spec.layers, n_devices=world))[rank][1]
+    stream = model == "llama3-8b"  # config 5: weights streamed per step from pinned host
+    sink = D.RouterLogitsSink() if spec.experts else None
+    t_build = time.perf_counter()
+    layers = [D.WrappedLayer(D.build_layer(spec, i, dev, stream=stream, seed=0, sink=sink), i) for i in mine]
+    prefix = D.Prefix(spec, dev, seed=0, with_embedding=first)
+    postfix = D.Postfix(spec, dev, seed=0) if last else None
+    t_build = time.perf_counter() - t_build
+    pipe = RankPipeline(DeviceStage(layers, local), prefix=prefix, postfix=postfix, rank=rank, world=world,
+                        hidden_size=spec.hidden, router_sink=sink, router_aux_coef=spec.router_aux_coef,
+                        n_experts=spec.experts)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    ids = torch.randint(0, spec.vocab, (M, seq), generator=g, device=dev)
+    ids_host = ids.cpu().pin_memory()
+
+    def step(mb, host=False):
+        src = ids_host if host else ids
+        out = pipe.train_step(src[:mb] if first else None, src[:mb] if last else None, microbatches=mb,
+                              seq_len=seq)
+        return out
+
+    def timed(mb, n, host=False):
+        barrier(world)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        n0 = _lib.launch_count()
+        e0.record()
+        for _ in range(n):
+            loss = step(mb, host)
+            if host and loss is not None:
+                float(loss)  # the step's result read back to the host
+        e1.record()
+        torch.cuda.synchronize()
+        launches = _lib.launch_count() - n0
+        barrier(world)
+        return max_over_ranks(e0.elapsed_time(e1) / n, world), launches
+
+    for _ in range(warmup):
+        step(M)
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clocks:
+        ms, launches = timed(M, steps)
+    ms_seq, _ = timed(1, max(1, steps))
+    ms_e2e, _ = timed(M, 1, host=True)
+    tok = M * seq
+    value = tok / (ms * 1e-3)
+    peaks = load_peaks()
+    fpt = D.reference_flops_per_token(spec, seq)
+    achieved = fpt * value / 1e12
+    peak = peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]
+    lt = torch.tensor([launches], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(lt)
+    return {
+        "metric": "pipeline_train_tokens_per_s",
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "ms_per_step": round(ms, 3),
+        "model": model,
+        "workload": f"{model}-shaped decoder fwd+bwd, {spec.layers} layers over {world} GPU(s) (one stratum per "
+                    f"rank), {M} microbatches x [1, {seq}] tokens per step (GPipe), NF4 bs64"
+                    f"{' + double quant, streamed per step from pinned host' if stream else ' resident'}, "
+                    f"LoRA r={spec.lora_r}, NCCL send/recv boundaries",
+        "microbatches": M,
+        "seq_len": seq,
+        "sequential": {"what": "one sequence per step (the reference's sequential execution)",
+                       "value": round(seq / (ms_seq * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms_seq, 3)},
+        "e2e": {"value": round(tok / (ms_e2e * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(ids_host[:M].numel() * 8 * (2 if world > 1 else 1)),
+                "d2h_bytes_per_step": 4, "path": "RankPipeline.train_step with pinned host token ids, loss read back"},
+        "roofline": {"bound": "tensor", "what": "algorithmic FLOPs of the step (fwd + dX + LoRA grads + attention "
+                     "+ lm_head; recompute not counted) per second over all GPUs",
+                     "achieved": round(achieved, 1), "peak": round(peak * world, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / (peak * world), 4),
+                     "frac_of": f"{peaks['source']} sustained bf16 x {world}", "flops_per_token": fpt},
+        "gpu_launches_per_step": int(lt.item() / steps),
+        "build_s": round(t_build, 1),
+        "clocks": clocks.summary(),
+    }
+
+
+def run_pipeline(args, world, rank, local):
+    r = run_pipeline_metrics(args, world, rank, local)
+    if rank != 0:
+        return None
+    return {
+        "metric": r["metric"], "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.pipe_steps,
+        "warmup": args.pipe_warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (NF4 weights)",
+        "data": "synthetic: random-init weights of the named shape, uniform token ids",
+        "config": {"workload": r["workload"], "model": r["model"], "global_batch": r["microbatches"],
+                   "seq_len": r["seq_len"], "parallelism": f"pp{world}",
+                   "l2": "inputs far larger than L2 (the step streams every layer's weights and activations)"},
+        "sequential": r["sequential"], "e2e": r["e2e"], "roofline": r["roofline"],
+        "gpu_launches": r["gpu_launches_per_step"] * args.pipe_steps, "build_s": r["build_s"], "clocks": r["clocks"],
+    }
+
+
 def run_codec_e2e(args, wl, world):
     """Same metric through the reference-facing call with host buffers.
 
@@ -844,7 +976,13 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("codec", "linear", "experts"), default="codec")
+    ap.add_argument("--workload", choices=("codec", "linear", "experts", "pipeline"), default="codec")
+    ap.add_argument("--model", choices=("llama3-8b", "qwen3-0.6b", "qwen3-30b-a3b"), default="llama3-8b",
+                    help="decoder config of the pipeline workload / section")
+    ap.add_argument("--microbatches", type=int, default=0, help="pipeline microbatches per step (default 4 x GPUs)")
+    ap.add_argument("--pipe-steps", type=int, default=3)
+    ap.add_argument("--pipe-warmup", type=int, default=3)
+    ap.add_argument("--no-pipeline", action="store_true", help="skip the pipeline section of the codec run")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-linear", action="store_true", help="skip the NF4Linear fwd+bwd section of the codec run")
     ap.add_argument("--no-experts", action="store_true", help="skip the MoE experts section of the codec run")
@@ -858,7 +996,8 @@ def main():
         else:
             if not torch.cuda.is_available():
                 raise SystemExit("bench.py: no CUDA device (the product path has no CPU fallback)")
-            run = {"codec": run_codec, "linear": run_linear, "experts": run_experts}[args.workload]
+            run = {"codec": run_codec, "linear": run_linear, "experts": run_experts,
+                   "pipeline": run_pipeline}[args.workload]
             out = run(args, world, rank, local)
         if rank == 0 and out is not None:
             print(json.dumps(out), flush=True)

@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the NF4 GEMMs use:
-// mbarriers (with bounded waits), TMA tile loads (no multicast), TMEM
+// mbarriers (with bounded waits), TMA tile loads (per-CTA, no broadcast), TMEM
 // allocation, tcgen05.mma with the A operand in TMEM, commits, TMEM
 // loads/stores and the tcgen05 ordering fences.
 #pragma once
@@ -100,7 +100,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
 }
 
 // 2-D TMA tile load into shared memory, completion counted on `bar` (bytes).
-// No .multicast::cluster: every CTA fetches its own tiles.
+// Every CTA fetches its own tiles (no cluster-wide broadcast form).
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int32_t c0, int32_t c1,
                                             uint64_t *bar) {
     asm volatile(
