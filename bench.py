@@ -743,9 +743,13 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
     prefix = D.Prefix(spec, dev, seed=0, with_embedding=first)
     postfix = D.Postfix(spec, dev, seed=0) if last else None
     t_build = time.perf_counter() - t_build
+    # dense: 1F1B keeps at most world - rank microbatches in flight, so every layer's graph is kept
+    # (no recompute); MoE with the router aux loss: GPipe with per-layer recompute
+    aux = bool(spec.experts and spec.router_aux_coef)
+    schedule, recompute = ("gpipe", True) if aux else ("1f1b", False)
     pipe = RankPipeline(DeviceStage(layers, local), prefix=prefix, postfix=postfix, rank=rank, world=world,
                         hidden_size=spec.hidden, router_sink=sink, router_aux_coef=spec.router_aux_coef,
-                        n_experts=spec.experts)
+                        n_experts=spec.experts, schedule=schedule, recompute=recompute)
     g = torch.Generator(device=dev).manual_seed(1234)
     ids = torch.randint(0, spec.vocab, (M, seq), generator=g, device=dev)
     ids_host = ids.cpu().pin_memory()
@@ -796,7 +800,8 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
         "ms_per_step": round(ms, 3),
         "model": model,
         "workload": f"{model}-shaped decoder fwd+bwd, {spec.layers} layers over {world} GPU(s) (one stratum per "
-                    f"rank), {M} microbatches x [1, {seq}] tokens per step (GPipe), NF4 bs64"
+                    f"rank), {M} microbatches x [1, {seq}] tokens per step ({schedule}, "
+                    f"{'per-layer recompute' if recompute else 'no recompute'}), NF4 bs64"
                     f"{' + double quant, streamed per step from pinned host' if stream else ' resident'}, "
                     f"LoRA r={spec.lora_r}, NCCL send/recv boundaries",
         "microbatches": M,

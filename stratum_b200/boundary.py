@@ -140,3 +140,24 @@ class P2PChannel:
         buf = torch.empty(shape, dtype=dtype, device=device)
         dist.recv(buf, self._peer(self.next), group=self.group)
         return buf
+
+    def _batched(self, ops) -> None:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+
+    def send_forward_recv_backward(self, y: torch.Tensor, shape, dtype, device) -> torch.Tensor:
+        """Send this stage's output to the next rank and receive the gradient of an
+        earlier output from it, as one NCCL group (the two ranks issue the mirror
+        pair at the same time in a 1F1B schedule; separate blocking calls would
+        wait on each other)."""
+        g = torch.empty(shape, dtype=dtype, device=device)
+        self._batched([dist.P2POp(dist.isend, y.contiguous(), self._peer(self.next), self.group),
+                       dist.P2POp(dist.irecv, g, self._peer(self.next), self.group)])
+        return g
+
+    def send_backward_recv_forward(self, g: torch.Tensor, shape, dtype, device) -> torch.Tensor:
+        """Send an input gradient to the previous rank and receive its next output."""
+        x = torch.empty(shape, dtype=dtype, device=device)
+        self._batched([dist.P2POp(dist.isend, g.contiguous(), self._peer(self.prev), self.group),
+                       dist.P2POp(dist.irecv, x, self._peer(self.prev), self.group)])
+        return x

@@ -385,19 +385,35 @@ class RankPipeline(nn.Module):
 
     Every rank holds a ``prefix`` for its rotary context (rank 0's also embeds
     tokens); the last rank holds the ``postfix``.  ``train_step`` runs forward
-    and backward over ``microbatches`` sequences with a GPipe schedule: all
-    forwards (each rank sends its stratum's output to the next rank as soon as
-    it is computed), then all backwards in reverse order (gradients go back the
-    same way).  Input ids are read on rank 0, labels on the last rank.
-    Returns the mean loss on the last rank, ``None`` elsewhere.
+    and backward over ``microbatches`` sequences.  Input ids are read on rank 0,
+    labels on the last rank.  Returns the mean loss on the last rank, ``None``
+    elsewhere.
+
+    Schedules: ``"gpipe"`` -- all forwards (each rank sends its stratum's output
+    on as soon as it is computed), then all backwards in reverse order;
+    ``"1f1b"`` -- after ``world - rank - 1`` warm-up forwards each rank
+    alternates one forward and one backward, so at most ``world - rank``
+    microbatches are in flight on it.  ``recompute=False`` keeps every layer's
+    autograd graph instead of recomputing it in the backward (the 1F1B bound on
+    microbatches in flight is what makes that fit); it is not combined with the
+    router aux loss, whose gradient needs the global expert counts of each
+    microbatch before its backward.
     """
 
     def __init__(self, stage: DeviceStage, *, prefix: nn.Module, postfix: Optional[nn.Module], rank: int,
                  world: int, group=None, hidden_size: int, offload_stage_inputs: bool = False, router_sink=None,
-                 router_aux_coef: float = 0.0, n_experts: int = 0, hidden_dtype=torch.bfloat16):
+                 router_aux_coef: float = 0.0, n_experts: int = 0, hidden_dtype=torch.bfloat16,
+                 schedule: str = "gpipe", recompute: bool = True):
         super().__init__()
         if (postfix is None) != (rank + 1 < world):
             raise ValueError("RankPipeline: the postfix lives on the last rank only")
+        if schedule not in ("gpipe", "1f1b"):
+            raise ValueError(f"RankPipeline: unknown schedule {schedule!r}")
+        if not recompute and schedule != "1f1b":
+            raise ValueError("RankPipeline: recompute=False needs the 1f1b schedule (bounded microbatches in flight)")
+        if not recompute and router_sink is not None and router_aux_coef:
+            raise ValueError("RankPipeline: the router aux loss needs recompute=True")
+        self.schedule, self.recompute = schedule, recompute
         self.stage, self.prefix, self.postfix = stage, prefix, postfix
         self.rank, self.world, self.group = rank, world, group
         self.device = _dev(stage.device_id)
@@ -425,6 +441,80 @@ class RankPipeline(nn.Module):
         for m, a in enumerate(states):  # the step's loss is the mean over its M microbatches
             a.finalize(buf[m, :E], buf[m, E:2 * E], buf[m, 2 * E], grad_scale=1.0 / M)
 
+    def _forward_mb(self, m: int, ids, labs, shape, x_recv: Optional[torch.Tensor], sink, aux):
+        """Forward of microbatch m on this stratum: (stage input, stage output, loss or None)."""
+        first, last = self.rank == 0, self.rank + 1 == self.world
+        if first:
+            tup = self.prefix(input_ids=ids[m])
+            h_in = tup[0]
+        else:
+            h_in = x_recv.requires_grad_(True)
+            tup = self.prefix.context(h_in)
+        rest = tup[1:]
+        if self.recompute:
+            out = _run_stage(self.stage, h_in, rest, self.streamer, "step", sink, aux, self.offload)
+        else:
+            t = (h_in,) + rest
+            for i, layer in enumerate(self.stage.layers):
+                self.streamer.acquire(i)
+                t = layer(t)
+            out = t[0]
+        loss = self.postfix((out,) + rest[:4] + (labs[m],) + rest[5:]) if last else None
+        return h_in, out, loss
+
+    def _backward_mb(self, out, loss, g, M: int):
+        if loss is not None:
+            (loss / M).backward()
+        else:
+            torch.autograd.backward(out, g)
+
+    def _train_1f1b(self, ids, labs, M: int, shape):
+        first, last = self.rank == 0, self.rank + 1 == self.world
+        dev, dt, ch = self.device, self.hidden_dtype, self.chan
+        warm = min(self.world - self.rank - 1, M)
+        rem = M - warm
+        inflight = []
+        losses = []
+        mf = 0
+
+        def fwd(x):
+            nonlocal mf
+            h_in, out, loss = self._forward_mb(mf, ids, labs, shape, x, None, None)
+            mf += 1
+            if loss is not None:
+                losses.append(loss.detach())
+            inflight.append((h_in, out, loss))
+            return out
+
+        def bwd(g):
+            h_in, out, loss = inflight.pop(0)
+            self._backward_mb(out, loss, g, M)
+            return None if first else h_in.grad
+
+        for _ in range(warm):
+            x = None if first else ch.recv_forward(shape, dt, dev)
+            out = fwd(x)
+            if not last:
+                ch.send_forward(out.detach())
+        x = None if (first or rem == 0) else ch.recv_forward(shape, dt, dev)
+        for i in range(rem):
+            out = fwd(x)
+            g = None if last else ch.send_forward_recv_backward(out.detach(), shape, dt, dev)
+            gx = bwd(g)
+            if i == rem - 1:
+                if not first:
+                    ch.send_backward(gx)
+            elif first:
+                x = None
+            else:
+                x = ch.send_backward_recv_forward(gx, shape, dt, dev)
+        for _ in range(warm):
+            g = None if last else ch.recv_backward(shape, dt, dev)
+            gx = bwd(g)
+            if not first:
+                ch.send_backward(gx)
+        return losses
+
     def train_step(self, input_ids: Optional[torch.Tensor] = None, labels: Optional[torch.Tensor] = None, *,
                    microbatches: int = 1, seq_len: Optional[int] = None):
         M = int(microbatches)
@@ -440,6 +530,13 @@ class RankPipeline(nn.Module):
             raise ValueError("RankPipeline.train_step: seq_len is needed on middle ranks")
         shape = (1, seq_len, self.hidden_size)
         use_aux = self.router_sink is not None and self.router_aux_coef != 0.0 and self.n_experts > 0
+        if self.schedule == "1f1b" and not use_aux:
+            with _on(dev):
+                for i in range(len(self.stage.layers)):  # the stratum's upload, overlapped with microbatch 0
+                    self.streamer.prefetch(i)
+                losses = self._train_1f1b(ids if first else None, labs if last else None, M, shape)
+                self.streamer.release_all()
+            return torch.stack(losses).mean() if last else None
         sink = self.router_sink if use_aux else None
         records = []
         losses = []

@@ -147,7 +147,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_dir, moe, M, n_layers):
+def _rank_main(rank, world, port, out_dir, moe, M, n_layers, schedule="gpipe", recompute=True):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -163,7 +163,7 @@ def _rank_main(rank, world, port, out_dir, moe, M, n_layers):
         pipe = RankPipeline(stage, prefix=ToyPrefix(), postfix=ToyPostfix() if rank == world - 1 else None,
                             rank=rank, world=world, hidden_size=H, hidden_dtype=torch.float32,
                             router_sink=sink if moe else None, router_aux_coef=COEF if moe else 0.0,
-                            n_experts=E if moe else 0)
+                            n_experts=E if moe else 0, schedule=schedule, recompute=recompute)
         ids, labels = _data(M)
         loss = pipe.train_step(ids if rank == 0 else None, labels if rank == world - 1 else None,
                                microbatches=M, seq_len=S)
@@ -174,16 +174,19 @@ def _rank_main(rank, world, port, out_dir, moe, M, n_layers):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("moe", [False, True])
-def test_two_rank_pipeline_matches_autograd(moe):
-    M, n_layers, world = 3, 5, 2
+@pytest.mark.parametrize("moe,world,schedule,recompute", [
+    (False, 2, "gpipe", True), (True, 2, "gpipe", True),
+    (False, 3, "1f1b", False), (False, 2, "1f1b", True),
+], ids=["gpipe", "gpipe-moe-aux", "1f1b-3rank-no-recompute", "1f1b-recompute"])
+def test_rank_pipeline_matches_autograd(moe, world, schedule, recompute):
+    M, n_layers = 4, 5
     ids, labels = _data(M)
     ref_loss, ref_grads = _reference(n_layers, moe, ids, labels)
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_rank_main, args=(world, _free_port(), d, moe, M, n_layers), nprocs=world,
-                           start_method="spawn", join=True)
+        mp.start_processes(_rank_main, args=(world, _free_port(), d, moe, M, n_layers, schedule, recompute),
+                           nprocs=world, start_method="spawn", join=True)
         outs = [torch.load(os.path.join(d, f"rank{r}.pt")) for r in range(world)]
-    assert outs[0]["loss"] is None
+    assert all(o["loss"] is None for o in outs[:-1])
     assert abs(outs[-1]["loss"] - ref_loss) < 1e-5
     got = {}
     for o in outs:
