@@ -59,6 +59,13 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_moe_combine": (_int, [_vp, _int, _vp, _vp, _vp, _int, _i64, _int, _i64, _vp, _vp]),
     "stratum_moe_combine_grad": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _vp, _vp, _vp]),
     "stratum_swiglu_grad": (_int, [_vp, _vp, _int, _i64, _i64, _vp, _vp]),
+    # include/stratum_layers.h
+    "stratum_rmsnorm_fwd": (_int, [_vp, _vp, _int, _i64, _i64, _f32, _vp, _vp, _vp]),
+    "stratum_rmsnorm_bwd": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _i64, _vp, _vp]),
+    "stratum_rope_to_heads": (_int, [_vp, _vp, _vp, _int, _int, _int, _int, _vp, _vp]),
+    "stratum_rope_from_heads": (_int, [_vp, _vp, _vp, _int, _int, _int, _int, _vp, _vp]),
+    "stratum_swiglu_fwd": (_int, [_vp, _vp, _int, _i64, _vp, _vp]),
+    "stratum_swiglu_bwd": (_int, [_vp, _vp, _vp, _int, _i64, _vp, _vp, _vp]),
 }
 
 ABI_VERSION = 1

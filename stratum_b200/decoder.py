@@ -121,6 +121,14 @@ def _layer_classes(spec: DecoderSpec):
     return m.Qwen3MoeDecoderLayer, m.Qwen3MoeRotaryEmbedding, m.Qwen3MoeRMSNorm
 
 
+def _device(device) -> torch.device:
+    """``device`` with its index filled in (``"cuda"`` -> the current CUDA device)."""
+    dev = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    return dev
+
+
 # --------------------------------------------------------------------------------
 # router side channel (router aux loss)
 # --------------------------------------------------------------------------------
@@ -184,16 +192,18 @@ def _random_init_(module: nn.Module, std: float, gen: torch.Generator) -> None:
 
 
 def build_layer(spec: DecoderSpec, idx: int, device, *, stream: bool = False, seed: int = 0,
-                sink: Optional[RouterLogitsSink] = None) -> nn.Module:
+                sink: Optional[RouterLogitsSink] = None, fused: bool = True) -> nn.Module:
     """One random-init decoder layer on ``device`` with NF4 frozen weights.
 
     Frozen linears are quantized on the GPU (``upload.prepare_nf4``), replaced by
     fused-mode ``NF4Linear``\\ s with a LoRA adapter of rank ``spec.lora_r``
     (``upload.to_nf4_linear``), and uploaded once (``stream=False``) or left as
     pinned host payloads for per-step streaming (``stream=True``).  Routed experts
-    become a resident ``NF4Experts``; the router stays bf16 and frozen.
+    become a resident ``NF4Experts``; the router stays bf16 and frozen.  With
+    ``fused`` the layer's RMSNorms, attention and (dense) MLP become the
+    single-kernel modules of :mod:`stratum_b200.fused` around the same NF4Linears.
     """
-    dev = torch.device(device)
+    dev = _device(device)
     cls, _, _ = _layer_classes(spec)
     cfg = hf_config(spec)
     gen = torch.Generator(device=dev).manual_seed(seed * 1000003 + idx)
@@ -212,6 +222,15 @@ def build_layer(spec: DecoderSpec, idx: int, device, *, stream: bool = False, se
         upload.prepare_nf4(t, verbose=False, compress_statistics=spec.double_quant, device=dev)
         upload.to_nf4_linear(t, lora_r=spec.lora_r, lora_alpha=spec.lora_alpha, lora_dtype=torch.bfloat16,
                              lora_device=dev)
+    if fused:
+        from .fused import FusedAttention, FusedMLP, FusedRMSNorm
+
+        layer.input_layernorm = FusedRMSNorm.from_hf(layer.input_layernorm)
+        layer.post_attention_layernorm = FusedRMSNorm.from_hf(layer.post_attention_layernorm)
+        layer.self_attn = FusedAttention.from_hf(layer.self_attn, spec.heads, spec.kv_heads, spec.head_dim)
+        if not spec.experts:
+            mlp = layer.mlp
+            layer.mlp = FusedMLP(mlp.gate_proj, mlp.up_proj, mlp.down_proj)
     with torch.no_grad():  # adapters drawn from the layer's own generator: builds are reproducible
         for m in layer.modules():
             if isinstance(m, NF4Linear) and m.lora_A is not None:
@@ -235,7 +254,7 @@ class Prefix(nn.Module):
     def __init__(self, spec: DecoderSpec, device, *, seed: int = 0, with_embedding: bool = True):
         super().__init__()
         _, rot_cls, _ = _layer_classes(spec)
-        dev = torch.device(device)
+        dev = _device(device)
         self.spec = spec
         self.embed_tokens = None
         if with_embedding:
@@ -295,7 +314,7 @@ class Postfix(nn.Module):
     def __init__(self, spec: DecoderSpec, device, *, seed: int = 0, token_chunk: int = 4096):
         super().__init__()
         _, _, norm_cls = _layer_classes(spec)
-        dev = torch.device(device)
+        dev = _device(device)
         self.spec = spec
         self.token_chunk = token_chunk
         with torch.device(dev):

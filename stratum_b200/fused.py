@@ -1,0 +1,232 @@
+"""Fused decoder-layer pieces around the NF4 GEMMs: RMSNorm, rotary, SwiGLU.
+
+Drop-in modules for the parts of HF's Llama / Qwen3 decoder layers that the
+reference runs as chains of small torch kernels (stratum/model/llama.py and
+stratum/model/qwen3.py build those layers; the reference patches only their
+attention kernel): ``FusedRMSNorm`` for ``LlamaRMSNorm`` / ``Qwen3RMSNorm``,
+``FusedMLP`` for ``LlamaMLP`` (gate / up / down NF4Linears with one SwiGLU
+kernel between them), ``FusedAttention`` for ``LlamaAttention`` /
+``Qwen3Attention`` (q/k/v/o NF4Linears, optional per-head q/k RMSNorm, one
+kernel that applies the rotary embedding and lays q and k out head-major for
+the attention kernel, torch's SDPA -- cuDNN on B200 -- with GQA, one kernel
+back to token-major for o_proj).  Each kernel reproduces the forward's bf16
+roundings (csrc/fused_ops.cu); the backwards are the exact adjoints in fp32.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as TF
+
+from . import _lib
+
+
+def _call(name: str, *args) -> None:
+    L = _lib.lib()
+    _lib.check(getattr(L, name)(*args), name)
+
+
+def _stream(t: torch.Tensor):
+    return _lib.stream_of(t.device)
+
+
+class _RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        n = x.shape[-1]
+        x2 = x.reshape(-1, n).contiguous()
+        y = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        with torch.cuda.device(x.device):
+            _call("stratum_rmsnorm_fwd", _lib.ptr(x2), _lib.ptr(weight), _lib.DTYPE_CODE[x.dtype], x2.shape[0], n,
+                  float(eps), _lib.ptr(y), _lib.ptr(rstd), _stream(x))
+        ctx.save_for_backward(x2, weight, rstd)
+        ctx.shape = x.shape
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, weight, rstd = ctx.saved_tensors
+        n = x2.shape[1]
+        dy2 = dy.reshape(-1, n).contiguous()
+        dx = torch.empty_like(x2)
+        with torch.cuda.device(dy.device):
+            _call("stratum_rmsnorm_bwd", _lib.ptr(x2), _lib.ptr(weight), _lib.ptr(dy2), _lib.ptr(rstd),
+                  _lib.DTYPE_CODE[dy.dtype], x2.shape[0], n, _lib.ptr(dx), _stream(dy))
+        return dx.view(ctx.shape), None, None
+
+
+class FusedRMSNorm(nn.Module):
+    """``weight * round(x * rsqrt(mean(x^2) + eps))`` over the last dimension, frozen weight."""
+
+    def __init__(self, weight: torch.Tensor, eps: float = 1e-6):
+        super().__init__()
+        self.weight = nn.Parameter(weight.detach().contiguous(), requires_grad=False)
+        self.variance_epsilon = float(eps)
+
+    @classmethod
+    def from_hf(cls, norm: nn.Module) -> "FusedRMSNorm":
+        return cls(norm.weight, getattr(norm, "variance_epsilon", getattr(norm, "eps", 1e-6)))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _lib.require_cuda(x, "FusedRMSNorm")
+        w = self.weight if self.weight.dtype == x.dtype else self.weight.to(x.dtype)
+        return _RMSNormFn.apply(x, w, self.variance_epsilon)
+
+
+class _SwiGLUFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, g, u):
+        g, u = g.contiguous(), u.contiguous()
+        h = torch.empty_like(g)
+        with torch.cuda.device(g.device):
+            _call("stratum_swiglu_fwd", _lib.ptr(g), _lib.ptr(u), _lib.DTYPE_CODE[g.dtype], g.numel(), _lib.ptr(h),
+                  _stream(g))
+        ctx.save_for_backward(g, u)
+        return h
+
+    @staticmethod
+    def backward(ctx, dh):
+        g, u = ctx.saved_tensors
+        dh = dh.contiguous()
+        dg, du = torch.empty_like(g), torch.empty_like(u)
+        with torch.cuda.device(dh.device):
+            _call("stratum_swiglu_bwd", _lib.ptr(g), _lib.ptr(u), _lib.ptr(dh), _lib.DTYPE_CODE[g.dtype], g.numel(),
+                  _lib.ptr(dg), _lib.ptr(du), _stream(dh))
+        return dg, du
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` with HF's bf16 roundings, one kernel each way."""
+    _lib.require_cuda(gate, "swiglu")
+    return _SwiGLUFn.apply(gate, up)
+
+
+class FusedMLP(nn.Module):
+    """``down(swiglu(gate(x), up(x)))`` (LlamaMLP / Qwen3MLP with SiLU)."""
+
+    def __init__(self, gate_proj: nn.Module, up_proj: nn.Module, down_proj: nn.Module):
+        super().__init__()
+        self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.down_proj(swiglu(self.gate_proj(x), self.up_proj(x)))
+
+
+class _HeadsFn(torch.autograd.Function):
+    """[S, H*D] token-major -> [1, H, S, D] head-major, rotated when cos/sin are given."""
+
+    @staticmethod
+    def forward(ctx, x, cos, sin, H, D):
+        S = x.shape[0]
+        x = x.contiguous()
+        y = torch.empty((1, H, S, D), dtype=x.dtype, device=x.device)
+        with torch.cuda.device(x.device):
+            _call("stratum_rope_to_heads", _lib.ptr(x), _lib.ptr(cos), _lib.ptr(sin), _lib.DTYPE_CODE[x.dtype], S, H,
+                  D, _lib.ptr(y), _stream(x))
+        ctx.save_for_backward(cos, sin) if cos is not None else ctx.save_for_backward()
+        ctx.rot = cos is not None
+        ctx.dims = (S, H, D)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        S, H, D = ctx.dims
+        cos, sin = ctx.saved_tensors if ctx.rot else (None, None)
+        dy = dy.contiguous()
+        dx = torch.empty((S, H * D), dtype=dy.dtype, device=dy.device)
+        with torch.cuda.device(dy.device):
+            _call("stratum_rope_from_heads", _lib.ptr(dy), _lib.ptr(cos), _lib.ptr(sin), _lib.DTYPE_CODE[dy.dtype], S,
+                  H, D, _lib.ptr(dx), _stream(dy))
+        return dx, None, None, None, None
+
+
+class _TokensFn(torch.autograd.Function):
+    """[1, H, S, D] head-major -> [S, H*D] token-major (no rotation)."""
+
+    @staticmethod
+    def forward(ctx, y):
+        _, H, S, D = y.shape
+        y = y.contiguous()
+        x = torch.empty((S, H * D), dtype=y.dtype, device=y.device)
+        with torch.cuda.device(y.device):
+            _call("stratum_rope_from_heads", _lib.ptr(y), None, None, _lib.DTYPE_CODE[y.dtype], S, H, D, _lib.ptr(x),
+                  _stream(y))
+        ctx.dims = (S, H, D)
+        return x
+
+    @staticmethod
+    def backward(ctx, dx):
+        S, H, D = ctx.dims
+        dx = dx.contiguous()
+        dy = torch.empty((1, H, S, D), dtype=dx.dtype, device=dx.device)
+        with torch.cuda.device(dx.device):
+            _call("stratum_rope_to_heads", _lib.ptr(dx), None, None, _lib.DTYPE_CODE[dx.dtype], S, H, D, _lib.ptr(dy),
+                  _stream(dx))
+        return dy
+
+
+def to_heads(x: torch.Tensor, H: int, D: int, cos: Optional[torch.Tensor] = None,
+             sin: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x`` [S, H*D] -> [1, H, S, D]; with ``cos``/``sin`` ([S, D]) the rotary embedding
+    is applied as HF's ``apply_rotary_pos_emb`` does."""
+    _lib.require_cuda(x, "to_heads")
+    if cos is not None:
+        cos = cos.reshape(-1, D).to(x.dtype).contiguous()
+        sin = sin.reshape(-1, D).to(x.dtype).contiguous()
+    return _HeadsFn.apply(x, cos, sin, H, D)
+
+
+def to_tokens(y: torch.Tensor) -> torch.Tensor:
+    """[1, H, S, D] -> [S, H*D]."""
+    return _TokensFn.apply(y)
+
+
+class FusedAttention(nn.Module):
+    """Causal self-attention with NF4 projections (LlamaAttention / Qwen3Attention
+    forward, no KV cache, no padding mask).  Returns ``(output, None)`` like HF."""
+
+    def __init__(self, q_proj, k_proj, v_proj, o_proj, heads: int, kv_heads: int, head_dim: int,
+                 q_norm: Optional[nn.Module] = None, k_norm: Optional[nn.Module] = None):
+        super().__init__()
+        self.q_proj, self.k_proj, self.v_proj, self.o_proj = q_proj, k_proj, v_proj, o_proj
+        self.heads, self.kv_heads, self.head_dim = heads, kv_heads, head_dim
+        self.q_norm, self.k_norm = q_norm, k_norm
+        self.scaling = head_dim ** -0.5
+
+    @classmethod
+    def from_hf(cls, attn: nn.Module, heads: int, kv_heads: int, head_dim: int) -> "FusedAttention":
+        qn = FusedRMSNorm.from_hf(attn.q_norm) if hasattr(attn, "q_norm") else None
+        kn = FusedRMSNorm.from_hf(attn.k_norm) if hasattr(attn, "k_norm") else None
+        return cls(attn.q_proj, attn.k_proj, attn.v_proj, attn.o_proj, heads, kv_heads, head_dim, qn, kn)
+
+    def forward(self, hidden_states: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
+                position_ids=None, past_key_values=None, use_cache=False, position_embeddings=None, **kwargs):
+        if attention_mask is not None:
+            raise ValueError("FusedAttention: causal attention only (no materialised mask)")
+        if past_key_values is not None:
+            raise ValueError("FusedAttention: no KV cache")
+        B, S, _ = hidden_states.shape
+        H, Hk, D = self.heads, self.kv_heads, self.head_dim
+        cos, sin = position_embeddings
+        q = self.q_proj(hidden_states)
+        k = self.k_proj(hidden_states)
+        v = self.v_proj(hidden_states)
+        if self.q_norm is not None:
+            q = self.q_norm(q.view(B, S, H, D)).view(B, S, H * D)
+            k = self.k_norm(k.view(B, S, Hk, D)).view(B, S, Hk * D)
+        outs = []
+        for b in range(B):
+            qh = to_heads(q[b], H, D, cos[b if cos.shape[0] > 1 else 0], sin[b if sin.shape[0] > 1 else 0])
+            kh = to_heads(k[b], Hk, D, cos[b if cos.shape[0] > 1 else 0], sin[b if sin.shape[0] > 1 else 0])
+            vh = to_heads(v[b], Hk, D)
+            o = TF.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=self.scaling, enable_gqa=(H != Hk))
+            outs.append(to_tokens(o))
+        o = torch.stack(outs, 0) if B > 1 else outs[0].unsqueeze(0)
+        return self.o_proj(o), None
+
+
+__all__ = ["FusedRMSNorm", "FusedMLP", "FusedAttention", "swiglu", "to_heads", "to_tokens"]
