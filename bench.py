@@ -707,6 +707,8 @@ def run_experts(args, world, rank, local):
 
 
 PIPE_SEQ = {"llama3-8b": 8192, "qwen3-0.6b": 2048, "qwen3-30b-a3b": 4096}
+# postfix (lm_head fwd + dX + cross entropy) cost per microbatch in decoder-layer units, measured
+PIPE_TAIL_COST = {"llama3-8b": 1.5, "qwen3-0.6b": 8.0, "qwen3-30b-a3b": 2.0}
 
 
 def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None, steps=None, warmup=None):
@@ -723,7 +725,7 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
 
     from stratum_b200 import _lib
     from stratum_b200 import decoder as D
-    from stratum_b200.assign import assign_layers_to_devices, strata
+    from stratum_b200.assign import balanced_strata
     from stratum_b200.pipeline import RankPipeline
     from stratum_b200.stage import DeviceStage
 
@@ -735,7 +737,8 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
     warmup = max(1, int(warmup if warmup is not None else args.pipe_warmup))
     dev = torch.device("cuda", local)
     first, last = rank == 0, rank == world - 1
-    mine = strata(assign_layers_to_devices(spec.layers, n_devices=world))[rank][1]
+    # the last rank also runs the postfix (lm_head + cross entropy): give it fewer layers
+    mine = balanced_strata(spec.layers, world, tail_cost=PIPE_TAIL_COST[model])[rank]
     stream = model == "llama3-8b"  # config 5: weights streamed per step from pinned host
     sink = D.RouterLogitsSink() if spec.experts else None
     t_build = time.perf_counter()
@@ -800,7 +803,7 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
         "ms_per_step": round(ms, 3),
         "model": model,
         "workload": f"{model}-shaped decoder fwd+bwd, {spec.layers} layers over {world} GPU(s) (one stratum per "
-                    f"rank), {M} microbatches x [1, {seq}] tokens per step ({schedule}, "
+                    f"rank, last rank lighter by the postfix), {M} microbatches x [1, {seq}] tokens per step ({schedule}, "
                     f"{'per-layer recompute' if recompute else 'no recompute'}), NF4 bs64"
                     f"{' + double quant, streamed per step from pinned host' if stream else ' resident'}, "
                     f"LoRA r={spec.lora_r}, NCCL send/recv boundaries",

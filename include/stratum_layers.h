@@ -48,6 +48,18 @@ int stratum_swiglu_fwd(const void *gate, const void *up, int dtype, int64_t n, v
 int stratum_swiglu_bwd(const void *gate, const void *up, const void *dh, int dtype, int64_t n, void *dgate, void *dup,
                        void *stream);
 
+/* Next-token cross entropy of one row of logits per token, forward and gradient
+ * in one pass (replaces the log_softmax / nll / autograd chain of the reference's
+ * chunked_linear_cross_entropy, stratum/model/chunked_loss.py):
+ *   loss[row]  = logsumexp(logits[row]) - logits[row][labels[row]]   (0 where
+ *                labels[row] == ignore_index), computed in fp32
+ *   logits[row] is overwritten with (softmax(logits[row]) - onehot) * scale
+ *                (zeros for ignored rows), in dtype
+ * logits: rows x vocab, vocab % 8 == 0; labels int64[rows] in [0, vocab) or
+ * ignore_index (any other value is treated as ignored); loss float32[rows]. */
+int stratum_ce_fwd_grad(void *logits, int dtype, const int64_t *labels, int64_t rows, int64_t vocab,
+                        int64_t ignore_index, float scale, float *loss, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

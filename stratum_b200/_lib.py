@@ -66,6 +66,7 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_rope_from_heads": (_int, [_vp, _vp, _vp, _int, _int, _int, _int, _vp, _vp]),
     "stratum_swiglu_fwd": (_int, [_vp, _vp, _int, _i64, _vp, _vp]),
     "stratum_swiglu_bwd": (_int, [_vp, _vp, _vp, _int, _i64, _vp, _vp, _vp]),
+    "stratum_ce_fwd_grad": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
 }
 
 ABI_VERSION = 1

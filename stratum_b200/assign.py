@@ -59,3 +59,36 @@ def strata(assignment: dict[int, int]) -> list[tuple[int, list[int]]]:
         else:
             out.append((dev, [layer]))
     return out
+
+
+def balanced_strata(n_layers: int, n_devices: int, *, tail_cost: float = 0.0,
+                    head_cost: float = 0.0) -> list[list[int]]:
+    """Contiguous layer strata, one per device, minimising the largest per-device
+    load when the first device also runs the prefix (``head_cost``) and the last
+    the postfix (``tail_cost``), both in units of one decoder layer.
+
+    The reference splits by user weights with a cumulative rule
+    (stratum/assign.py:9-83, :func:`assign_layers_to_devices`), which rounds a
+    cost-aware split unevenly; this picks the integer layer counts directly."""
+    if n_devices <= 0:
+        raise ValueError("n_devices must be positive")
+    extra = [0.0] * n_devices
+    extra[0] += head_cost
+    extra[-1] += tail_cost
+    cands = sorted({k + e for e in extra for k in range(n_layers + 1)})
+    counts = None
+    for m in cands:  # smallest max load whose floor(m - extra) counts cover every layer
+        c = [max(int(m - e + 1e-9), 0) for e in extra]
+        if sum(c) >= n_layers:
+            counts = c
+            break
+    surplus = sum(counts) - n_layers
+    while surplus > 0:  # drop layers from the most loaded devices first
+        r = max(range(n_devices), key=lambda i: (counts[i] + extra[i], counts[i]))
+        counts[r] -= 1
+        surplus -= 1
+    out, start = [], 0
+    for c in counts:
+        out.append(list(range(start, start + c)))
+        start += c
+    return out

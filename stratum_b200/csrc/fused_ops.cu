@@ -225,6 +225,94 @@ __global__ void k_swiglu_bwd(const uint4 *__restrict__ g, const uint4 *__restric
     }
 }
 
+// ------------------------------------------------------------ cross entropy --
+
+// Next-token cross entropy over bf16/fp16 logits, forward and gradient in one
+// pass per row (the reference's chunked_linear_cross_entropy,
+// stratum/model/chunked_loss.py, computes log_softmax in fp32 from the 16-bit
+// logits and lets autograd form the gradient).  One block per row: an online
+// max / sum-exp over the row, then the row is overwritten with
+//     dlogits = (softmax - onehot(label)) * scale      (16-bit)
+// and loss[row] = logsumexp - logit[label] (0 for ignored rows).
+constexpr int kCeThreads = 512;
+
+template <bool BF16>
+__global__ void __launch_bounds__(kCeThreads)
+k_ce_fwd_grad(uint4 *__restrict__ logits, const int64_t *__restrict__ labels, int64_t rows, int vpr,
+              int64_t ignore_index, float scale, float *__restrict__ loss) {
+    __shared__ float red_m[kCeThreads / 32], red_s[kCeThreads / 32];
+    __shared__ float row_stats[2];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        uint4 *row = logits + r * vpr;
+        const int64_t lab = labels[r];
+        float m = -INFINITY, sum = 0.f;
+        for (int c = threadIdx.x; c < vpr; c += kCeThreads) {
+            float f[8];
+            unpack8<BF16>(row[c], f);
+            float lm = f[0];
+#pragma unroll
+            for (int i = 1; i < 8; ++i) lm = fmaxf(lm, f[i]);
+            if (lm > m) {
+                sum *= expf(m - lm);
+                m = lm;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sum += expf(f[i] - m);
+        }
+        // combine (m, sum) across the warp, then across warps
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            const float om = __shfl_xor_sync(0xffffffffu, m, d), os = __shfl_xor_sync(0xffffffffu, sum, d);
+            const float nm = fmaxf(m, om);
+            sum = (m == -INFINITY ? 0.f : sum * expf(m - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
+            m = nm;
+        }
+        if (lane == 0) {
+            red_m[wid] = m;
+            red_s[wid] = sum;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float M = red_m[0], Ssum = red_s[0];
+            for (int w = 1; w < kCeThreads / 32; ++w) {
+                if (red_m[w] == -INFINITY) continue;  // a warp that saw no element of the row
+                const float nm = fmaxf(M, red_m[w]);
+                Ssum = (M == -INFINITY ? 0.f : Ssum * expf(M - nm)) + red_s[w] * expf(red_m[w] - nm);
+                M = nm;
+            }
+            row_stats[0] = M;
+            row_stats[1] = logf(Ssum);
+        }
+        __syncthreads();
+        const float M = row_stats[0], lse_off = row_stats[1];  // logsumexp = M + lse_off
+        // labels outside [0, vocab) other than ignore_index are treated as ignored
+        const bool live = lab != ignore_index && lab >= 0 && lab < int64_t(vpr) * 8;
+        if (threadIdx.x == 0) {
+            float l = 0.f;
+            if (live) {
+                const uint16_t *h = reinterpret_cast<const uint16_t *>(row);
+                l = (M + lse_off) - ld1<BF16>(h[lab]);
+            }
+            loss[r] = l;
+        }
+        __syncthreads();  // the label's logit is read before the row is overwritten
+        const float sc = live ? scale : 0.f;
+        for (int c = threadIdx.x; c < vpr; c += kCeThreads) {
+            float f[8];
+            unpack8<BF16>(row[c], f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float p = expf(f[i] - M - lse_off);
+                if (int64_t(c) * 8 + i == lab) p -= 1.f;
+                f[i] = p * sc;
+            }
+            row[c] = pack8<BF16>(f);
+        }
+        __syncthreads();  // row_stats reused by the next row
+    }
+}
+
 inline int grid_for(int64_t work, int threads) {
     const int64_t blocks = (work + threads - 1) / threads;
     const int64_t cap = int64_t(sm_count()) * 8;
@@ -378,6 +466,26 @@ int stratum_swiglu_bwd(const void *gate, const void *up, const void *dh, int dty
                                                   static_cast<const uint4 *>(dh), nv, static_cast<uint4 *>(dgate),
                                                   static_cast<uint4 *>(dup));
     return check_launch("swiglu_bwd");
+}
+
+int stratum_ce_fwd_grad(void *logits, int dtype, const int64_t *labels, int64_t rows, int64_t vocab,
+                        int64_t ignore_index, float scale, float *loss, void *stream) {
+    STRATUM_REQUIRE(rows >= 0 && vocab > 0, "ce_fwd_grad: bad sizes");
+    if (rows == 0) return STRATUM_OK;
+    FUSED_DTYPE_CHECK(dtype, "ce_fwd_grad");
+    STRATUM_REQUIRE(logits && labels && loss, "ce_fwd_grad: null pointer");
+    STRATUM_REQUIRE(vocab % 8 == 0 && a16(logits), "ce_fwd_grad: vocab % 8 and 16-byte alignment");
+    STRATUM_BIND_STREAM(stream);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t cap = int64_t(sm_count()) * 4;
+    const int grid = int(rows < cap ? rows : cap);
+    if (dtype == STRATUM_BF16)
+        k_ce_fwd_grad<true><<<grid, kCeThreads, 0, st>>>(static_cast<uint4 *>(logits), labels, rows, int(vocab / 8),
+                                                         ignore_index, scale, loss);
+    else
+        k_ce_fwd_grad<false><<<grid, kCeThreads, 0, st>>>(static_cast<uint4 *>(logits), labels, rows, int(vocab / 8),
+                                                          ignore_index, scale, loss);
+    return check_launch("ce_fwd_grad");
 }
 
 }  // extern "C"

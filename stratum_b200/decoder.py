@@ -23,8 +23,6 @@ from typing import Optional
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as TF
-from torch.utils.checkpoint import checkpoint
 
 from . import upload
 from .experts import NF4Experts
@@ -299,17 +297,50 @@ class WrappedLayer(nn.Module):
         return (out, causal_mask, pos_ids, pos_emb, kwargs, labels, lk)
 
 
-def _ce_chunk(h: torch.Tensor, lm_head: nn.Module, labels: torch.Tensor) -> torch.Tensor:
-    logits = lm_head(h).float()
-    return TF.cross_entropy(logits, labels, ignore_index=-100, reduction="sum")
+class _LMHeadCE(torch.autograd.Function):
+    """Mean next-token cross entropy of ``h . W_lm^T`` with the gradient formed in
+    the forward: the NF4 GEMM writes bf16 logits, one kernel turns each row into
+    its loss and (softmax - onehot) in place, and the backward is one fused NF4
+    input-gradient GEMM over those rows.  The 1/N mean is applied as a tensor, so
+    nothing waits on the host."""
+
+    @staticmethod
+    def forward(ctx, h, labels, lm_head):
+        from . import _lib, ops
+
+        qs = lm_head.quant_state
+        logits = ops.nf4_gemm_fwd(h, lm_head.quantized, qs)
+        rows, vocab = logits.shape
+        loss_rows = torch.empty(rows, dtype=torch.float32, device=h.device)
+        lab = labels.to(torch.int64).contiguous()
+        with torch.cuda.device(h.device):
+            _lib.check(_lib.lib().stratum_ce_fwd_grad(_lib.ptr(logits), _lib.DTYPE_CODE[logits.dtype], _lib.ptr(lab),
+                                                      rows, vocab, -100, 1.0, _lib.ptr(loss_rows),
+                                                      _lib.stream_of(h.device)), "ce_fwd_grad")
+        n = (lab != -100).sum().clamp_min(1).to(torch.float32)
+        ctx.save_for_backward(logits, n)
+        ctx.lm_head = lm_head
+        return loss_rows.sum() / n
+
+    @staticmethod
+    def backward(ctx, g):
+        from . import ops
+
+        dlogits, n = ctx.saved_tensors
+        m = ctx.lm_head
+        dh = ops.nf4_gemm_dx(dlogits, m.quantized, m.quant_state)
+        return dh * (g / n).to(dh.dtype), None, None
 
 
 class Postfix(nn.Module):
     """Final norm + lm_head + next-token cross entropy (stratum/model/llama.py:334-399).
 
-    The lm_head is a frozen NF4Linear; the loss is computed in token chunks whose
-    logits are recomputed in the backward (checkpointed), so [tokens, vocab]
-    never exists whole.  Returns the mean loss over non-ignored tokens."""
+    The lm_head is a frozen NF4Linear.  The reference chunks the loss over tokens
+    and recomputes each chunk's logits in the backward; here the bf16 logits of
+    the microbatch are formed once and overwritten with their own gradient by
+    the cross-entropy kernel, so the backward is a single NF4 input-gradient GEMM
+    (the 16-bit [tokens, vocab] buffer lives until the backward).  Returns the
+    mean loss over non-ignored tokens."""
 
     def __init__(self, spec: DecoderSpec, device, *, seed: int = 0, token_chunk: int = 4096):
         super().__init__()
@@ -335,13 +366,7 @@ class Postfix(nn.Module):
     def loss(self, hidden: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         h = self.norm(hidden)[:, :-1, :].reshape(-1, self.spec.hidden)
         y = labels[:, 1:].reshape(-1)
-        n = (y != -100).sum().clamp_min(1)
-        total = None
-        for s in range(0, h.shape[0], self.token_chunk):
-            part = checkpoint(_ce_chunk, h[s:s + self.token_chunk], self.lm_head, y[s:s + self.token_chunk],
-                              use_reentrant=False)
-            total = part if total is None else total + part
-        return total / n
+        return _LMHeadCE.apply(h, y, self.lm_head)
 
     def forward(self, input_data):
         hidden, _, _, _, _, labels, _ = input_data

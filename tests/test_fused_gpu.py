@@ -122,3 +122,24 @@ def test_fused_layer_matches_hf_layer(family):
     assert set(grads[1][1]) == set(grads[0][1])
     for k in grads[0][1]:
         assert relative_error(grads[1][1][k].float(), grads[0][1][k].float()) < 1e-2, k
+
+
+def test_lm_head_cross_entropy_matches_torch():
+    """Postfix's fused lm_head + CE against F.cross_entropy over the same bf16 logits."""
+    spec = D.DecoderSpec("t", "llama", 1, 256, 512, 4, 2, 64, 1000, 5e5)
+    post = D.Postfix(spec, DEV, seed=1)
+    g0 = torch.Generator(device=DEV).manual_seed(4)
+    hidden = torch.randn(1, 300, 256, generator=g0, device=DEV).to(torch.bfloat16).requires_grad_()
+    labels = torch.randint(0, 1000, (1, 300), generator=g0, device=DEV)
+    labels[0, 10:20] = -100
+    loss = post.loss(hidden, labels)
+    loss.backward()
+    gh = hidden.grad.clone()
+    hidden.grad = None
+    w = post.lm_head.weight_dequantized.to(torch.bfloat16)
+    h = post.norm(hidden)[:, :-1].reshape(-1, 256)
+    logits = (h @ w.t()).float()
+    ref = TF.cross_entropy(logits, labels[:, 1:].reshape(-1), ignore_index=-100)
+    ref.backward()
+    assert abs(float(loss) - float(ref)) < 1e-2 * abs(float(ref))
+    assert relative_error(gh.float(), hidden.grad.float()) < 1e-2
