@@ -120,6 +120,30 @@ int stratum_nf4_dequantize_dq(const uint8_t *packed, const uint8_t *absmax_q,
                               int blocksize2, const float *code16, int64_t n, int blocksize,
                               void *out, int out_dtype, void *stream);
 
+/* One NF4 tensor of a stratum_nf4_dequantize_many call: packed bytes, either
+ * absmax (plain) or, with absmax == NULL, the double-quant set, its element
+ * count and its output buffer. */
+typedef struct stratum_nf4_tensor {
+    const uint8_t *packed;
+    const float *absmax;
+    const uint8_t *absmax_q;
+    const float *absmax2;
+    const float *code2;
+    const float *offset;
+    int64_t n;
+    void *out;
+} stratum_nf4_tensor;
+
+/* Dequantize `count` tensors (host array of descriptors) with one kernel launch
+ * per 32 tensors of the same kind (plain / double quant), e.g. every frozen
+ * weight of a layer.  Replaces the per-parameter dequantize_4bit loop of
+ * ensure_weights (stratum/upload.py:1021-1040).  Same blocksize and out_dtype
+ * for all; tensors whose n is not a multiple of 64 or whose buffers are not
+ * 16-byte aligned fall back to one launch each.  Results are those of
+ * stratum_nf4_dequantize / stratum_nf4_dequantize_dq. */
+int stratum_nf4_dequantize_many(const stratum_nf4_tensor *tensors, int count, const float *code16,
+                                int blocksize, int blocksize2, int out_dtype, void *stream);
+
 /* -------------------------------------------------------------- GEMMs -- */
 
 /* Status word written by the GEMM kernels when a bounded device-side wait gives

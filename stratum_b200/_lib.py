@@ -43,6 +43,7 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_nf4_dequantize_dq": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _int, _vp, _int, _vp]),
     "stratum_device_status": (_int, [ctypes.POINTER(ctypes.c_int), _int, _vp]),
     "stratum_nf4_quantize_dq_noalloc": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "stratum_nf4_dequantize_many": (_int, [_vp, _int, _vp, _int, _int, _int, _vp]),
     "stratum_nf4_gemm_fwd": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _int, _vp,
                                     _vp, _int, _vp, _vp]),
     "stratum_nf4_gemm_dx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _int,

@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(kThreads) k_dequant(DequantArgs a, OutT *__res
 // 16-byte-chunk XOR swizzle (conflict-free), then the warp stores the 4 KiB as
 // eight fully coalesced 512-byte rows.
 template <bool BF16, bool DQ>
-__global__ void __launch_bounds__(kThreads) k_dequant_seg(DequantArgs a, uint4 *__restrict__ out) {
+__global__ void __launch_bounds__(kThreads, 4) k_dequant_seg(DequantArgs a, uint4 *__restrict__ out) {
     __shared__ float lv_s[16];
     __shared__ float c2[DQ ? 256 : 1];
     __shared__ uint4 stage[kThreads / 32][32 * 8];  // per warp: 32 rows x 8 chunks of 16 B
@@ -205,6 +205,89 @@ __global__ void __launch_bounds__(kThreads) k_dequant_seg(DequantArgs a, uint4 *
             const uint32_t q = (e & 1) ? (byte & 0xFu) : (byte >> 4);
             Out8<OutT>::store1(o, e, __fmul_rn(lv_s[q], block_absmax<DQ>(a, c2, offset, e >> a.log2bs)));
         }
+    }
+}
+
+// Several tensors in one launch (one layer's weights, or any list): the same
+// per-warp 4 KiB output tiles as k_dequant_seg, numbered across the tensors;
+// a warp finds its tensor in the prefix table of tile counts.  Every tensor has
+// n % 64 == 0 and 16-byte aligned packed / out; the double-quant tables are read
+// per tensor through the read-only cache.
+constexpr int kMaxMany = 32;
+
+struct DequantMany {
+    int count;
+    int log2bs, log2bs2;
+    const float *code16;
+    int64_t tile0[kMaxMany + 1];  // first warp tile of each tensor; tile0[count] = total
+    int64_t nseg[kMaxMany];       // 64-element segments of each tensor
+    const uint8_t *packed[kMaxMany];
+    const float *absmax[kMaxMany];
+    const uint8_t *absmax_q[kMaxMany];
+    const float *absmax2[kMaxMany];
+    const float *code2[kMaxMany];
+    const float *offset[kMaxMany];
+    uint4 *out[kMaxMany];
+};
+
+template <bool BF16, bool DQ>
+__global__ void __launch_bounds__(kThreads, 3) k_dequant_many(const __grid_constant__ DequantMany m) {
+    __shared__ float lv_s[16];
+    __shared__ uint4 stage[kThreads / 32][32 * 8];
+    if (threadIdx.x < 16) lv_s[threadIdx.x] = m.code16[threadIdx.x];
+    __syncthreads();
+    float lv[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
+    const int lane = threadIdx.x & 31;
+    uint4 *buf = stage[threadIdx.x >> 5];
+    const int64_t total = m.tile0[m.count];
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t gt = warp; gt < total; gt += nwarps) {
+        int lo = 0, hi = m.count - 1;  // the last tensor whose first tile is <= gt
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (m.tile0[mid] <= gt) lo = mid;
+            else hi = mid - 1;
+        }
+        const int t = lo;
+        const int64_t wt = gt - m.tile0[t];
+        const int64_t nseg = m.nseg[t];
+        const int64_t g = (wt << 5) + lane;
+        const uint4 *pk = reinterpret_cast<const uint4 *>(m.packed[t]);
+        uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
+        float am = 0.f;
+        if (g < nseg) {
+            p0 = __ldcs(pk + 2 * g);
+            p1 = __ldcs(pk + 2 * g + 1);
+            const int64_t blk = (g << 6) >> m.log2bs;
+            if constexpr (DQ) {
+                am = __fadd_rn(__fmul_rn(__ldg(m.code2[t] + m.absmax_q[t][blk]),
+                                         __ldg(m.absmax2[t] + (blk >> m.log2bs2))),
+                               __ldg(m.offset[t]));
+            } else {
+                am = __ldg(m.absmax[t] + blk);
+            }
+        }
+        const Nf4Tables tb = nf4_build_tables<BF16>(lv, am);
+        const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            uint32_t r[4];
+            nf4_decode_word(tb, w[i], r);
+            buf[lane * 8 + (i ^ (lane & 7))] = make_uint4(r[0], r[1], r[2], r[3]);
+        }
+        __syncwarp();
+        const int64_t rows_valid = nseg - (wt << 5);
+        uint4 *out = m.out[t];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int c = k * 32 + lane;
+            const int row = c >> 3;
+            if (row < rows_valid) out[(wt << 8) + c] = buf[row * 8 + ((c & 7) ^ (row & 7))];
+        }
+        __syncwarp();
     }
 }
 
@@ -628,6 +711,94 @@ int stratum_nf4_dequantize_dq(const uint8_t *packed, const uint8_t *absmax_q, co
     a.log2bs2 = ilog2(blocksize2); a.code16 = code16; a.n = n; a.log2bs = ilog2(blocksize);
     STRATUM_BIND_STREAM(stream);
     return launch_dequant<true>(a, out, out_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int stratum_nf4_dequantize_many(const stratum_nf4_tensor *tensors, int count, const float *code16, int blocksize,
+                                int blocksize2, int out_dtype, void *stream) {
+    STRATUM_REQUIRE(count >= 0 && (count == 0 || tensors), "dequantize_many: bad tensor list");
+    if (count == 0) return STRATUM_OK;
+    STRATUM_REQUIRE(code16 != nullptr, "dequantize_many: null code16");
+    if (!is_pow2(blocksize) || blocksize < 32 || blocksize > 4096)
+        return fail(STRATUM_ERR_UNSUPPORTED, "dequantize_many: blocksize %d not a power of two in [32, 4096]", blocksize);
+    for (int i = 0; i < count; ++i) {
+        const stratum_nf4_tensor &t = tensors[i];
+        STRATUM_REQUIRE(t.n >= 0, "dequantize_many: tensor %d: n < 0", i);
+        if (t.n == 0) continue;
+        STRATUM_REQUIRE(t.packed && t.out, "dequantize_many: tensor %d: null pointer", i);
+        STRATUM_REQUIRE(t.absmax || (t.absmax_q && t.absmax2 && t.code2 && t.offset),
+                        "dequantize_many: tensor %d: needs absmax or the double-quant set", i);
+        if (!t.absmax && !is_pow2(blocksize2))
+            return fail(STRATUM_ERR_UNSUPPORTED, "dequantize_many: blocksize2 %d not a power of two", blocksize2);
+    }
+    STRATUM_BIND_STREAM(stream);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool wide = out_dtype == STRATUM_BF16 || out_dtype == STRATUM_F16;
+    const int log2bs = ilog2(blocksize);
+    // tensors the batched kernel takes; the rest go one by one through the single-tensor path
+    DequantMany groups[2];
+    for (auto &g : groups) {
+        memset(&g, 0, sizeof(g));
+        g.log2bs = log2bs;
+        g.log2bs2 = ilog2(blocksize2 > 0 ? blocksize2 : 256);
+        g.code16 = code16;
+    }
+    auto flush = [&](int dq) -> int {
+        DequantMany &g = groups[dq];
+        if (g.count == 0) return STRATUM_OK;
+        const int64_t tiles = g.tile0[g.count];
+        const int64_t want = (tiles + kThreads / 32 - 1) / (kThreads / 32);
+        int64_t cap;
+        if (out_dtype == STRATUM_BF16)
+            cap = dq ? resident_grid<k_dequant_many<true, true>>(kThreads) : resident_grid<k_dequant_many<true, false>>(kThreads);
+        else
+            cap = dq ? resident_grid<k_dequant_many<false, true>>(kThreads) : resident_grid<k_dequant_many<false, false>>(kThreads);
+        const int grid = int(want < 1 ? 1 : (want > cap ? cap : want));
+        if (out_dtype == STRATUM_BF16) {
+            if (dq) k_dequant_many<true, true><<<grid, kThreads, 0, st>>>(g);
+            else k_dequant_many<true, false><<<grid, kThreads, 0, st>>>(g);
+        } else {
+            if (dq) k_dequant_many<false, true><<<grid, kThreads, 0, st>>>(g);
+            else k_dequant_many<false, false><<<grid, kThreads, 0, st>>>(g);
+        }
+        const int rc = check_launch("nf4_dequantize_many");
+        const int keep_log2bs2 = g.log2bs2;
+        memset(&g, 0, sizeof(g));
+        g.log2bs = log2bs;
+        g.log2bs2 = keep_log2bs2;
+        g.code16 = code16;
+        return rc;
+    };
+    for (int i = 0; i < count; ++i) {
+        const stratum_nf4_tensor &t = tensors[i];
+        if (t.n == 0) continue;
+        const bool dq = t.absmax == nullptr;
+        const bool batchable = wide && t.n % 64 == 0 && log2bs >= 6 && reinterpret_cast<uintptr_t>(t.packed) % 16 == 0 &&
+                               reinterpret_cast<uintptr_t>(t.out) % 16 == 0;
+        int rc = STRATUM_OK;
+        if (!batchable) {
+            rc = dq ? stratum_nf4_dequantize_dq(t.packed, t.absmax_q, t.absmax2, t.code2, t.offset, blocksize2, code16,
+                                                t.n, blocksize, t.out, out_dtype, stream)
+                    : stratum_nf4_dequantize(t.packed, t.absmax, code16, t.n, blocksize, t.out, out_dtype, stream);
+            if (rc) return rc;
+            continue;
+        }
+        DequantMany &g = groups[dq];
+        const int k = g.count;
+        g.nseg[k] = t.n >> 6;
+        g.tile0[k + 1] = g.tile0[k] + ((g.nseg[k] + 31) >> 5);
+        g.packed[k] = t.packed;
+        g.absmax[k] = t.absmax;
+        g.absmax_q[k] = t.absmax_q;
+        g.absmax2[k] = t.absmax2;
+        g.code2[k] = t.code2;
+        g.offset[k] = t.offset;
+        g.out[k] = static_cast<uint4 *>(t.out);
+        g.count = k + 1;
+        if (g.count == kMaxMany && (rc = flush(dq))) return rc;
+    }
+    int rc = flush(0);
+    if (rc) return rc;
+    return flush(1);
 }
 
 }  // extern "C"

@@ -226,3 +226,76 @@ def dequantize_4bit(
     if home != dev:
         res = res.to(home)
     return res
+
+
+class _Nf4Tensor(__import__("ctypes").Structure):
+    """``stratum_nf4_tensor`` of include/stratum_nf4.h."""
+
+    _fields_ = [("packed", _lib._vp), ("absmax", _lib._vp), ("absmax_q", _lib._vp), ("absmax2", _lib._vp),
+                ("code2", _lib._vp), ("offset", _lib._vp), ("n", _lib._i64), ("out", _lib._vp)]
+
+
+def dequantize_4bit_many(items, *, out_dtype: Optional[torch.dtype] = None) -> list[torch.Tensor]:
+    """Dequantize several NF4 tensors with one launch per 32 of the same kind.
+
+    ``items``: sequence of ``(A, quant_state)`` or ``(A, quant_state, out)``, all on
+    one CUDA device with the same blocksize and NF4 code.  Returns the outputs
+    (``quant_state.dtype`` / ``out_dtype``, ``quant_state.shape``), equal to what
+    :func:`dequantize_4bit` returns for each.  Used by ``upload.ensure_weights``
+    to dequantize a whole layer at once.
+    """
+    items = list(items)
+    if not items:
+        return []
+    first_qs = items[0][1]
+    dev = _compute_device(items[0][0], "dequantize_4bit_many")
+    bs = int(first_qs.blocksize)
+    bs2 = 256
+    dtype = out_dtype or first_qs.dtype or torch.float16
+    if dtype not in _lib.DTYPE_CODE:
+        raise ValueError(f"dequantize_4bit_many: unsupported output dtype {dtype}")
+    code = first_qs.code if first_qs.code is not None else codebook.nf4_code(dev)
+    code = _f32_on(code, dev)
+    keep: list[torch.Tensor] = [code]
+    descs = (_Nf4Tensor * len(items))()
+    outs: list[torch.Tensor] = []
+    for i, item in enumerate(items):
+        A, qs = item[0], item[1]
+        out = item[2] if len(item) > 2 else None
+        _check_quant_type(qs.quant_type or "nf4")
+        if int(qs.blocksize) != bs:
+            raise ValueError("dequantize_4bit_many: all tensors need the same blocksize")
+        if A.device != dev:
+            raise ValueError("dequantize_4bit_many: all tensors must be on one device")
+        shape = tuple(qs.shape)
+        n = 1
+        for s in shape:
+            n *= int(s)
+        packed = A if A.is_contiguous() else A.contiguous()
+        if packed.numel() < (n + 1) // 2:
+            raise ValueError(f"dequantize_4bit_many: tensor {i}: packed has {packed.numel()} bytes, need {(n + 1) // 2}")
+        res = out if out is not None else torch.empty(shape, dtype=dtype, device=dev)
+        if res.dtype != dtype or res.numel() != n or res.device != dev or not res.is_contiguous():
+            raise ValueError(f"dequantize_4bit_many: tensor {i}: out has the wrong dtype, size, device or layout")
+        d = descs[i]
+        d.packed, d.n, d.out = packed.data_ptr(), n, res.data_ptr()
+        keep += [packed, res]
+        if qs.nested:
+            s2 = qs.state2
+            bs2 = int(s2.blocksize)
+            aq = qs.absmax.to(dev, non_blocking=True)
+            a2, c2, off = _f32_on(s2.absmax, dev), _f32_on(s2.code, dev), _f32_on(qs.offset.reshape(()), dev)
+            keep += [aq, a2, c2, off]
+            d.absmax_q, d.absmax2, d.code2, d.offset = aq.data_ptr(), a2.data_ptr(), c2.data_ptr(), off.data_ptr()
+        else:
+            am = _f32_on(qs.absmax, dev)
+            keep.append(am)
+            d.absmax = am.data_ptr()
+        outs.append(res)
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.stratum_nf4_dequantize_many(__import__("ctypes").cast(descs, _lib._vp), len(items), _lib.ptr(code),
+                                                 bs, bs2, _lib.DTYPE_CODE[dtype],
+                                                 _lib.stream_of(dev)), "dequantize_4bit_many")
+    del keep
+    return outs

@@ -467,19 +467,42 @@ def build_layer_arena(module: nn.Module) -> Optional[LayerArena]:
 # phase 2: upload / free
 # --------------------------------------------------------------------------------
 
-def _materialize(param, payload: NF4Payload, dev_tensors: list[torch.Tensor], owner, pname, device) -> None:
-    """Make an uploaded payload usable: fused owner -> NF4 state, else dequantize into param.data."""
-    q, a, c = dev_tensors[0], dev_tensors[1], dev_tensors[2]
+def _device_state(payload: NF4Payload, dev_tensors: list[torch.Tensor]):
+    a, c = dev_tensors[1], dev_tensors[2]
     if payload.nested:
-        qs = payload.quant_state(absmax=a, code=c, absmax2=dev_tensors[3], code2=dev_tensors[4],
-                                 offset=dev_tensors[5].reshape(()))
-    else:
-        qs = payload.quant_state(absmax=a, code=c)
+        return payload.quant_state(absmax=a, code=c, absmax2=dev_tensors[3], code2=dev_tensors[4],
+                                   offset=dev_tensors[5].reshape(()))
+    return payload.quant_state(absmax=a, code=c)
+
+
+def _materialize(param, payload: NF4Payload, dev_tensors: list[torch.Tensor], owner, pname, device,
+                 pending: Optional[list] = None) -> None:
+    """Make an uploaded payload usable: fused owner -> NF4 state, else dequantize into
+    param.data -- right away, or (with ``pending``) queued for one batched launch
+    per layer by :func:`_flush_dequant`."""
+    q = dev_tensors[0]
+    qs = _device_state(payload, dev_tensors)
     fused = _fused_owner(owner, pname)
     if fused is not None:
         fused.load_device_state(q, qs)
         return
+    if pending is not None:
+        pending.append((param, q, qs, owner, pname))
+        return
     _replace_param_data(param, F.dequantize_4bit(q, qs).contiguous(), owner=owner, pname=pname)
+
+
+def _flush_dequant(pending: list) -> None:
+    """Dequantize queued payloads, one batched launch per (blocksize, dtype) group."""
+    groups: dict = {}
+    for item in pending:
+        qs = item[2]
+        groups.setdefault((int(qs.blocksize), qs.dtype), []).append(item)
+    for (_, dtype), items in groups.items():
+        outs = F.dequantize_4bit_many([(q, qs) for _, q, qs, _, _ in items], out_dtype=dtype)
+        for (param, _, _, owner, pname), out in zip(items, outs):
+            _replace_param_data(param, out, owner=owner, pname=pname)
+    pending.clear()
 
 
 def _device(device_id) -> torch.device:
@@ -505,6 +528,7 @@ def ensure_weights(module: nn.Module, device_id: int) -> int:
     arena: Optional[LayerArena] = getattr(module, ARENA_ATTR, None)
     arena_dev = None
     tensors = 0
+    pending: list = []  # compat-mode payloads, dequantized together after the loop
     for name, param in module.named_parameters():
         owner, pname = owner_map.get(id(param), (None, None))
         fp16 = getattr(param, FP16_ATTR, None)
@@ -537,8 +561,10 @@ def ensure_weights(module: nn.Module, device_id: int) -> int:
             dev_tensors = arena.views(arena_dev, id(param), len(payload.host_tensors()))
         else:
             dev_tensors = [t.to(device, non_blocking=True) for t in payload.host_tensors()]
-        _materialize(param, payload, dev_tensors, owner, pname, device)
+        _materialize(param, payload, dev_tensors, owner, pname, device, pending)
         tensors += 1
+    if pending:
+        _flush_dequant(pending)
     for buf in module.buffers():
         if buf.device != device and buf.device.type != "meta":
             buf.data = buf.data.to(device, non_blocking=True)
@@ -581,13 +607,16 @@ class NF4Prefetch:
         with torch.cuda.device(self.device), torch.no_grad():
             if self.arena_buffer is not None:
                 self.arena_buffer.record_stream(current)
+            pending: list = []
             for e in self.entries:
                 for t in e.tensors:
                     t.record_stream(current)
                 if _is_resident(e.param, e.payload, e.owner, e.pname, self.device):
                     continue
-                _materialize(e.param, e.payload, e.tensors, e.owner, e.pname, self.device)
+                _materialize(e.param, e.payload, e.tensors, e.owner, e.pname, self.device, pending)
                 n += 1
+            if pending:
+                _flush_dequant(pending)
         self.entries = []
         return n
 

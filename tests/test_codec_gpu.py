@@ -174,3 +174,21 @@ def test_config_sizes_bit_exact_and_idempotent(oracle_c, shape):
     dq16 = F.dequantize_4bit(packed_dq, st_dq, out_dtype=torch.bfloat16)
     ref_dq = oracle_c.dequantize_dq(p_c, q_c, a2_c, c2_c, off_c, w.numel(), 64, "bfloat16")
     assert np.array_equal(_np_bits(dq16), ref_dq)
+
+
+def test_dequantize_many_matches_single_tensor_calls():
+    """One batched launch per 32 tensors of a kind gives exactly the per-tensor results:
+    plain and double-quant mixed, sizes that take the one-by-one fallback (n % 64 != 0),
+    and more than 32 tensors (several launches)."""
+    g = torch.Generator(device="cuda").manual_seed(77)
+    shapes = [(4096, 4096), (1000, 1000), (64, 64), (7, 9)] + [(256, 320)] * 36 + [(14336, 512)]
+    items, refs = [], []
+    for i, shp in enumerate(shapes):
+        w = (torch.randn(*shp, generator=g, device="cuda") * 0.02).half()
+        packed, qs = F.quantize_4bit(w, compress_statistics=(i % 3 == 1))
+        items.append((packed, qs))
+        refs.append(F.dequantize_4bit(packed, qs, out_dtype=torch.bfloat16))
+    outs = F.dequantize_4bit_many(items, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    for i, (o, r) in enumerate(zip(outs, refs)):
+        assert torch.equal(o, r), f"tensor {i} {shapes[i]}"

@@ -216,3 +216,34 @@ def test_two_gpu_nccl_pipeline_matches_one_gpu():
     for o in outs:
         got.update(o["grads"])
     _compare(outs[1]["loss"], got, ref_loss.cpu(), ref)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_stratum_pipeline_across_two_devices_matches_one_device():
+    """Two stages on two GPUs (NVLink boundary copies, gradient copied back the same
+    way) against the same layers on one GPU."""
+    spec = TINY_LLAMA
+    ids, labels = _data(spec)
+    prefix, layers, postfix, _ = _build(spec, stream=True)
+    one = StratumPipeline(prefix, [DeviceStage(layers, 0)], postfix, prefetch_nf4=True)
+    loss1 = one(ids, labels=labels)
+    loss1.backward()
+    ref = _lora_grads(layers)
+    # the same model with layers 2.. and the postfix on cuda:1
+    prefix2 = D.Prefix(spec, "cuda:0", seed=0)
+    l0 = [D.WrappedLayer(D.build_layer(spec, i, "cuda:0", stream=True, seed=0), i) for i in range(2)]
+    l1 = [D.WrappedLayer(D.build_layer(spec, i, "cuda:1", stream=True, seed=0), i) for i in range(2, spec.layers)]
+    post2 = D.Postfix(spec, "cuda:1", seed=0, token_chunk=96)
+    with torch.no_grad():
+        g = torch.Generator(device=DEV).manual_seed(5)
+        for l in l0 + l1:
+            for n, p in l.named_parameters():
+                if n.endswith("lora_B"):
+                    p.copy_(torch.empty(p.shape, dtype=p.dtype, device=DEV).normal_(0.0, 0.02, generator=g))
+    two = StratumPipeline(prefix2, [DeviceStage(l0, 0), DeviceStage(l1, 1)], post2, prefetch_nf4=True)
+    loss2 = two(ids, labels=labels)
+    loss2.backward()
+    torch.cuda.synchronize(0)
+    torch.cuda.synchronize(1)
+    got = {k: v.to(DEV) for k, v in _lora_grads(l0 + l1).items()}
+    _compare(loss2.detach().to(DEV), got, loss1.detach(), ref)
