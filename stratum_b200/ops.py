@@ -32,9 +32,11 @@ def _weight_args(qs: QuantState, dev: torch.device):
 
 def lora_down(x2: torch.Tensor, lora_A: torch.Tensor, scaling: float) -> torch.Tensor:
     """xa = scaling * x . lora_A^T in x's dtype, zero-padded to a multiple of 64 columns."""
-    xa = torch.matmul(x2, lora_A.t())
-    if scaling != 1.0:
-        xa = (xa.float() * scaling).to(x2.dtype)
+    if scaling != 1.0:  # the scale rides on cuBLAS's alpha (beta = 0: the buffer is not read)
+        xa = torch.addmm(torch.empty((x2.shape[0], lora_A.shape[0]), dtype=x2.dtype, device=x2.device), x2,
+                         lora_A.t(), beta=0, alpha=scaling)
+    else:
+        xa = torch.matmul(x2, lora_A.t())
     r = xa.shape[1]
     pad = (-r) % LORA_CHUNK
     if pad:
