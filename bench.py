@@ -734,7 +734,7 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
     model = model or args.model
     spec = D.SPECS[model]
     seq = PIPE_SEQ[model]
-    M = int(microbatches or args.microbatches or 4 * world)
+    M = int(microbatches or args.microbatches or 8 * world)
     steps = max(1, int(steps if steps is not None else args.pipe_steps))
     warmup = max(1, int(warmup if warmup is not None else args.pipe_warmup))
     dev = torch.device("cuda", local)
@@ -748,10 +748,9 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
     prefix = D.Prefix(spec, dev, seed=0, with_embedding=first)
     postfix = D.Postfix(spec, dev, seed=0) if last else None
     t_build = time.perf_counter() - t_build
-    # dense: 1F1B keeps at most world - rank microbatches in flight, so every layer's graph is kept
-    # (no recompute); MoE with the router aux loss: GPipe with per-layer recompute
-    aux = bool(spec.experts and spec.router_aux_coef)
-    schedule, recompute = ("gpipe", True) if aux else ("1f1b", False)
+    # 1F1B keeps at most world - rank microbatches in flight, so every layer's graph is kept (no
+    # recompute); the router aux loss's per-microbatch sums ride on the boundary messages
+    schedule, recompute = "1f1b", False
     pipe = RankPipeline(DeviceStage(layers, local), prefix=prefix, postfix=postfix, rank=rank, world=world,
                         hidden_size=spec.hidden, router_sink=sink, router_aux_coef=spec.router_aux_coef,
                         n_experts=spec.experts, schedule=schedule, recompute=recompute)
@@ -989,7 +988,7 @@ def main():
     ap.add_argument("--workload", choices=("codec", "linear", "experts", "pipeline"), default="codec")
     ap.add_argument("--model", choices=("llama3-8b", "qwen3-0.6b", "qwen3-30b-a3b"), default="llama3-8b",
                     help="decoder config of the pipeline workload / section")
-    ap.add_argument("--microbatches", type=int, default=0, help="pipeline microbatches per step (default 4 x GPUs)")
+    ap.add_argument("--microbatches", type=int, default=0, help="pipeline microbatches per step (default 8 x GPUs)")
     ap.add_argument("--pipe-steps", type=int, default=3)
     ap.add_argument("--pipe-warmup", type=int, default=3)
     ap.add_argument("--no-pipeline", action="store_true", help="skip the pipeline section of the codec run")

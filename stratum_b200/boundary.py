@@ -111,10 +111,12 @@ class P2PChannel:
 
     ``send_forward`` / ``recv_forward`` carry the stage output to the next rank;
     ``send_backward`` / ``recv_backward`` carry the gradient of the stage input
-    to the previous rank.  Every call is issued in the same order on both ends
-    (the schedule guarantees it); NCCL runs the transfer on its own stream,
-    ordered after the caller's current stream, and the received tensor is
-    ordered before the caller's next work, so the host does not block.
+    to the previous rank.  Each takes or returns a list of tensors (the boundary
+    activation, plus any small side tensors that travel with it); every call is
+    one batched NCCL group.  Both ends issue their calls in the same order (the
+    schedule guarantees it); NCCL runs the transfers on its own stream, ordered
+    after the caller's current stream, and received tensors are ordered before
+    the caller's next work, so the host does not block.
     """
 
     def __init__(self, rank: int, world: int, group=None):
@@ -125,39 +127,46 @@ class P2PChannel:
     def _peer(self, r: int) -> int:
         return dist.get_global_rank(self.group, r) if self.group is not None else r
 
-    def send_forward(self, x: torch.Tensor) -> None:
-        dist.send(x.contiguous(), self._peer(self.next), group=self.group)
+    def exchange(self, sends=(), recvs=()) -> list:
+        """One NCCL group: ``sends`` = [(tensor, rank)], ``recvs`` = [(shape, dtype, device, rank)];
+        returns the received tensors in order."""
+        ops, out = [], []
+        for t, r in sends:
+            ops.append(dist.P2POp(dist.isend, t.contiguous(), self._peer(r), self.group))
+        for shape, dtype, device, r in recvs:
+            buf = torch.empty(shape, dtype=dtype, device=device)
+            out.append(buf)
+            ops.append(dist.P2POp(dist.irecv, buf, self._peer(r), self.group))
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        return out
 
-    def recv_forward(self, shape, dtype, device) -> torch.Tensor:
-        buf = torch.empty(shape, dtype=dtype, device=device)
-        dist.recv(buf, self._peer(self.prev), group=self.group)
-        return buf
+    def send_forward(self, xs) -> None:
+        self.exchange(sends=[(x, self.next) for x in _as_list(xs)])
 
-    def send_backward(self, g: torch.Tensor) -> None:
-        dist.send(g.contiguous(), self._peer(self.prev), group=self.group)
+    def recv_forward(self, specs) -> list:
+        return self.exchange(recvs=[(s, d, dev, self.prev) for s, d, dev in specs])
 
-    def recv_backward(self, shape, dtype, device) -> torch.Tensor:
-        buf = torch.empty(shape, dtype=dtype, device=device)
-        dist.recv(buf, self._peer(self.next), group=self.group)
-        return buf
+    def send_backward(self, gs) -> None:
+        self.exchange(sends=[(g, self.prev) for g in _as_list(gs)])
 
-    def _batched(self, ops) -> None:
-        for req in dist.batch_isend_irecv(ops):
-            req.wait()
+    def recv_backward(self, specs) -> list:
+        return self.exchange(recvs=[(s, d, dev, self.next) for s, d, dev in specs])
 
-    def send_forward_recv_backward(self, y: torch.Tensor, shape, dtype, device) -> torch.Tensor:
-        """Send this stage's output to the next rank and receive the gradient of an
+    def send_forward_recv_backward(self, ys, specs) -> list:
+        """Send this stage's outputs to the next rank and receive the gradients of an
         earlier output from it, as one NCCL group (the two ranks issue the mirror
         pair at the same time in a 1F1B schedule; separate blocking calls would
         wait on each other)."""
-        g = torch.empty(shape, dtype=dtype, device=device)
-        self._batched([dist.P2POp(dist.isend, y.contiguous(), self._peer(self.next), self.group),
-                       dist.P2POp(dist.irecv, g, self._peer(self.next), self.group)])
-        return g
+        return self.exchange(sends=[(y, self.next) for y in _as_list(ys)],
+                             recvs=[(s, d, dev, self.next) for s, d, dev in specs])
 
-    def send_backward_recv_forward(self, g: torch.Tensor, shape, dtype, device) -> torch.Tensor:
-        """Send an input gradient to the previous rank and receive its next output."""
-        x = torch.empty(shape, dtype=dtype, device=device)
-        self._batched([dist.P2POp(dist.isend, g.contiguous(), self._peer(self.prev), self.group),
-                       dist.P2POp(dist.irecv, x, self._peer(self.prev), self.group)])
-        return x
+    def send_backward_recv_forward(self, gs, specs) -> list:
+        """Send input gradients to the previous rank and receive its next outputs."""
+        return self.exchange(sends=[(g, self.prev) for g in _as_list(gs)],
+                             recvs=[(s, d, dev, self.prev) for s, d, dev in specs])
+
+
+def _as_list(xs):
+    return list(xs) if isinstance(xs, (list, tuple)) else [xs]

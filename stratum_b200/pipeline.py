@@ -395,9 +395,10 @@ class RankPipeline(nn.Module):
     alternates one forward and one backward, so at most ``world - rank``
     microbatches are in flight on it.  ``recompute=False`` keeps every layer's
     autograd graph instead of recomputing it in the backward (the 1F1B bound on
-    microbatches in flight is what makes that fit); it is not combined with the
-    router aux loss, whose gradient needs the global expert counts of each
-    microbatch before its backward.
+    microbatches in flight is what makes that fit).  The router aux loss needs
+    each microbatch's global per-expert sums before its backward: GPipe
+    all-reduces them after the forwards; 1F1B carries them on the boundary
+    messages (partial sums forward, global sums back).
     """
 
     def __init__(self, stage: DeviceStage, *, prefix: nn.Module, postfix: Optional[nn.Module], rank: int,
@@ -411,8 +412,6 @@ class RankPipeline(nn.Module):
             raise ValueError(f"RankPipeline: unknown schedule {schedule!r}")
         if not recompute and schedule != "1f1b":
             raise ValueError("RankPipeline: recompute=False needs the 1f1b schedule (bounded microbatches in flight)")
-        if not recompute and router_sink is not None and router_aux_coef:
-            raise ValueError("RankPipeline: the router aux loss needs recompute=True")
         self.schedule, self.recompute = schedule, recompute
         self.stage, self.prefix, self.postfix = stage, prefix, postfix
         self.rank, self.world, self.group = rank, world, group
@@ -441,8 +440,19 @@ class RankPipeline(nn.Module):
         for m, a in enumerate(states):  # the step's loss is the mean over its M microbatches
             a.finalize(buf[m, :E], buf[m, E:2 * E], buf[m, 2 * E], grad_scale=1.0 / M)
 
+    def _stats(self, aux: Optional[_AuxState]) -> torch.Tensor:
+        """This rank's router sums of one microbatch as [counts | psum | rows] (zeros if none)."""
+        E = self.n_experts
+        buf = torch.zeros(2 * E + 1, dtype=torch.float32, device=self.device)
+        if aux is not None and aux.counts is not None:
+            buf[:E] = aux.counts
+            buf[E:2 * E] = aux.psum
+            buf[2 * E] = aux.rows
+        return buf
+
     def _forward_mb(self, m: int, ids, labs, shape, x_recv: Optional[torch.Tensor], sink, aux):
-        """Forward of microbatch m on this stratum: (stage input, stage output, loss or None)."""
+        """Forward of microbatch m on this stratum: (stage input, stage output, loss or None, router
+        probabilities kept for the aux-loss backward when layers keep their graph)."""
         first, last = self.rank == 0, self.rank + 1 == self.world
         if first:
             tup = self.prefix(input_ids=ids[m])
@@ -451,68 +461,115 @@ class RankPipeline(nn.Module):
             h_in = x_recv.requires_grad_(True)
             tup = self.prefix.context(h_in)
         rest = tup[1:]
+        probs: list = []
         if self.recompute:
             out = _run_stage(self.stage, h_in, rest, self.streamer, "step", sink, aux, self.offload)
         else:
             t = (h_in,) + rest
             for i, layer in enumerate(self.stage.layers):
                 self.streamer.acquire(i)
-                t = layer(t)
+                if sink is not None:
+                    sink.clear()
+                    sink.active = True
+                try:
+                    t = layer(t)
+                finally:
+                    if sink is not None:
+                        sink.active = False
+                if sink is not None:
+                    for p, idx in zip(sink.probs, sink.indices):
+                        aux.add(p, idx)
+                        probs.append(p)
+                    sink.clear()
             out = t[0]
         loss = self.postfix((out,) + rest[:4] + (labs[m],) + rest[5:]) if last else None
-        return h_in, out, loss
+        return h_in, out, loss, probs
 
-    def _backward_mb(self, out, loss, g, M: int):
+    def _backward_mb(self, out, loss, g, M: int, aux: Optional[_AuxState] = None, probs=()):
+        outs, grads = [], []
         if loss is not None:
-            (loss / M).backward()
+            outs.append(loss / M)
+            grads.append(torch.ones((), dtype=loss.dtype, device=loss.device))
         else:
-            torch.autograd.backward(out, g)
+            outs.append(out)
+            grads.append(g)
+        if probs and aux is not None and aux.weight is not None:  # graph kept: the aux term's gradient here
+            term = sum((torch.softmax(p.float(), dim=-1) * aux.weight).sum() for p in probs)
+            if term.requires_grad:
+                outs.append(term)
+                grads.append(torch.ones((), dtype=term.dtype, device=term.device))
+        torch.autograd.backward(outs, grads)
 
-    def _train_1f1b(self, ids, labs, M: int, shape):
+    def _train_1f1b(self, ids, labs, M: int, shape, use_aux: bool):
+        """1F1B.  With the router aux loss, every boundary message carries the
+        microbatch's router sums: forward, the sums of the ranks so far; backward,
+        the global sums, from which each rank forms the aux gradient before
+        running that microbatch's backward."""
         first, last = self.rank == 0, self.rank + 1 == self.world
         dev, dt, ch = self.device, self.hidden_dtype, self.chan
+        sink = self.router_sink if use_aux else None
+        E = self.n_experts
+        act = [(shape, dt, dev)] + ([((2 * E + 1,), torch.float32, dev)] if use_aux else [])
         warm = min(self.world - self.rank - 1, M)
         rem = M - warm
         inflight = []
         losses = []
+        aux_values = []
         mf = 0
 
-        def fwd(x):
+        def fwd(msg):
             nonlocal mf
-            h_in, out, loss = self._forward_mb(mf, ids, labs, shape, x, None, None)
+            x = None if msg is None else msg[0]
+            aux = _AuxState(E, self.router_aux_coef) if use_aux else None
+            h_in, out, loss, probs = self._forward_mb(mf, ids, labs, shape, x, sink, aux)
             mf += 1
+            stats = None
+            if use_aux:
+                stats = self._stats(aux) + (msg[1] if msg is not None else 0.0)
+                if last:  # global sums of this microbatch: finalize here, send them back with the gradient
+                    aux.finalize(stats[:E], stats[E:2 * E], stats[2 * E], grad_scale=1.0 / M)
+                    aux_values.append(aux.value.detach())
             if loss is not None:
                 losses.append(loss.detach())
-            inflight.append((h_in, out, loss))
-            return out
+            inflight.append((h_in, out, loss, aux, probs, stats))
+            return [out.detach()] + ([stats] if use_aux else [])
 
-        def bwd(g):
-            h_in, out, loss = inflight.pop(0)
-            self._backward_mb(out, loss, g, M)
-            return None if first else h_in.grad
+        def bwd(msg):
+            h_in, out, loss, aux, probs, stats = inflight.pop(0)
+            g = None if msg is None else msg[0]
+            if use_aux and not last:
+                gs = msg[1]
+                aux.finalize(gs[:E], gs[E:2 * E], gs[2 * E], grad_scale=1.0 / M)
+                stats = gs
+            self._backward_mb(out, loss, g, M, aux, probs)
+            if first:
+                return None
+            return [h_in.grad] + ([stats] if use_aux else [])
 
         for _ in range(warm):
-            x = None if first else ch.recv_forward(shape, dt, dev)
-            out = fwd(x)
+            msg = None if first else ch.recv_forward(act)
+            y = fwd(msg)
             if not last:
-                ch.send_forward(out.detach())
-        x = None if (first or rem == 0) else ch.recv_forward(shape, dt, dev)
+                ch.send_forward(y)
+        msg = None if (first or rem == 0) else ch.recv_forward(act)
         for i in range(rem):
-            out = fwd(x)
-            g = None if last else ch.send_forward_recv_backward(out.detach(), shape, dt, dev)
-            gx = bwd(g)
+            y = fwd(msg)
+            gmsg = None if last else ch.send_forward_recv_backward(y, act)
+            gx = bwd(gmsg)
             if i == rem - 1:
                 if not first:
                     ch.send_backward(gx)
             elif first:
-                x = None
+                msg = None
             else:
-                x = ch.send_backward_recv_forward(gx, shape, dt, dev)
+                msg = ch.send_backward_recv_forward(gx, act)
         for _ in range(warm):
-            g = None if last else ch.recv_backward(shape, dt, dev)
-            gx = bwd(g)
+            gmsg = None if last else ch.recv_backward(act)
+            gx = bwd(gmsg)
             if not first:
                 ch.send_backward(gx)
+        if use_aux and last:
+            self.last_aux = torch.stack(aux_values).mean()
         return losses
 
     def train_step(self, input_ids: Optional[torch.Tensor] = None, labels: Optional[torch.Tensor] = None, *,
@@ -530,13 +587,16 @@ class RankPipeline(nn.Module):
             raise ValueError("RankPipeline.train_step: seq_len is needed on middle ranks")
         shape = (1, seq_len, self.hidden_size)
         use_aux = self.router_sink is not None and self.router_aux_coef != 0.0 and self.n_experts > 0
-        if self.schedule == "1f1b" and not use_aux:
+        if self.schedule == "1f1b":
             with _on(dev):
                 for i in range(len(self.stage.layers)):  # the stratum's upload, overlapped with microbatch 0
                     self.streamer.prefetch(i)
-                losses = self._train_1f1b(ids if first else None, labs if last else None, M, shape)
+                losses = self._train_1f1b(ids if first else None, labs if last else None, M, shape, use_aux)
                 self.streamer.release_all()
-            return torch.stack(losses).mean() if last else None
+            if not last:
+                return None
+            loss = torch.stack(losses).mean()
+            return loss + self.last_aux.to(loss.device) if use_aux else loss
         sink = self.router_sink if use_aux else None
         records = []
         losses = []
@@ -548,7 +608,7 @@ class RankPipeline(nn.Module):
                     tup = self.prefix(input_ids=ids[m])
                     h_in = tup[0]
                 else:
-                    h_in = self.chan.recv_forward(shape, self.hidden_dtype, dev).requires_grad_(True)
+                    h_in = self.chan.recv_forward([(shape, self.hidden_dtype, dev)])[0].requires_grad_(True)
                     tup = self.prefix.context(h_in)
                 aux = _AuxState(self.n_experts, self.router_aux_coef) if use_aux else None
                 rest = tup[1:]
@@ -566,7 +626,7 @@ class RankPipeline(nn.Module):
                 if last:
                     (losses[m] / M).backward()
                 else:
-                    g = self.chan.recv_backward(shape, self.hidden_dtype, dev)
+                    g = self.chan.recv_backward([(shape, self.hidden_dtype, dev)])[0]
                     torch.autograd.backward(out, g)
                 if not first:
                     self.chan.send_backward(h_in.grad)

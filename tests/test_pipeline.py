@@ -177,7 +177,9 @@ def _rank_main(rank, world, port, out_dir, moe, M, n_layers, schedule="gpipe", r
 @pytest.mark.parametrize("moe,world,schedule,recompute", [
     (False, 2, "gpipe", True), (True, 2, "gpipe", True),
     (False, 3, "1f1b", False), (False, 2, "1f1b", True),
-], ids=["gpipe", "gpipe-moe-aux", "1f1b-3rank-no-recompute", "1f1b-recompute"])
+    (True, 2, "1f1b", True), (True, 3, "1f1b", False),
+], ids=["gpipe", "gpipe-moe-aux", "1f1b-3rank-no-recompute", "1f1b-recompute", "1f1b-moe-aux-recompute",
+        "1f1b-3rank-moe-aux-no-recompute"])
 def test_rank_pipeline_matches_autograd(moe, world, schedule, recompute):
     M, n_layers = 4, 5
     ids, labels = _data(M)

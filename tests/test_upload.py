@@ -239,3 +239,20 @@ def test_device_stage_forward_range_order_and_bounds():
     for bad in ((-1, 2), (0, 4), (2, 2)):
         with pytest.raises(ValueError):
             stage.forward_range((torch.zeros(1),), local_start=bad[0], local_stop=bad[1])
+
+
+def test_balanced_strata_minimise_the_largest_load():
+    from stratum_b200.assign import balanced_strata
+
+    for L in (32, 48, 7):
+        for n in (1, 2, 3, 4, 8):
+            for tail in (0.0, 1.5, 2.0):
+                st = balanced_strata(L, n, tail_cost=tail)
+                assert len(st) == n
+                assert [i for s in st for i in s] == list(range(L))  # contiguous, every layer once
+                load = max(len(s) + (tail if i == n - 1 else 0.0) for i, s in enumerate(st))
+                # no contiguous split does better: the bound ceil-ish of (L + tail) / n over integer counts
+                best = min(max(max(-(-(L - c) // max(n - 1, 1)), 0) if n > 1 else L, c + tail) for c in range(L + 1)) \
+                    if n > 1 else L + tail
+                assert load <= best + 1e-9, (L, n, tail, [len(s) for s in st], load, best)
+    assert [len(s) for s in balanced_strata(32, 8, tail_cost=1.5)] == [4, 4, 4, 4, 4, 4, 5, 3]
