@@ -386,44 +386,48 @@ __device__ __forceinline__ void load_thresholds(const float *thresholds, float *
     if (threadIdx.x < 16) thr[threadIdx.x] = threadIdx.x < 15 ? thresholds[threadIdx.x] : __int_as_float(0x7f800000);
 }
 
-// One thread per 8 consecutive elements (one output word); BS/8 lanes share a
-// block and reduce its absmax with xor-shuffles.  Only whole blocks here.
+// 16 consecutive elements (two packed words) per thread; the BS/16 lanes of a
+// block reduce its absmax with xor-shuffles.  Only whole blocks here.
 template <typename InT, int BS>
 __global__ void __launch_bounds__(kThreads) k_quantize(const InT *__restrict__ src, int64_t nfull_words,
                                                         const float *__restrict__ thresholds,
                                                         uint32_t *__restrict__ packed, float *__restrict__ absmax) {
-    constexpr int L = BS / 8;  // lanes per block
+    constexpr int L = BS / 16;  // lanes per block
     __shared__ float thr[16];
     load_thresholds(thresholds, thr);
     __syncthreads();
     const float t7 = thr[7];
+    const int64_t npairs = nfull_words >> 1;
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-    for (int64_t w = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; w - threadIdx.x % 32 < nfull_words; w += stride) {
+    for (int64_t w = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; w - threadIdx.x % 32 < npairs; w += stride) {
         // whole warps iterate together (shuffles below); out-of-range lanes idle
-        const bool valid = w < nfull_words;
-        float v[8];
-        if (valid) In8<InT>::load(src, w << 3, v);
-        else {
+        const bool valid = w < npairs;
+        float v[16];
+        if (valid) {
+            In8<InT>::load(src, w << 4, v);
+            In8<InT>::load(src, (w << 4) + 8, v + 8);
+        } else {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) v[k] = 0.f;
+            for (int k = 0; k < 16; ++k) v[k] = 0.f;
         }
         float am = 0.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) am = fmaxf(am, fabsf(v[k]));
+        for (int k = 0; k < 16; ++k) am = fmaxf(am, fabsf(v[k]));
 #pragma unroll
         for (int off = L / 2; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
         const float inv = __frcp_rn(am);
-        uint32_t word = 0;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t hi = nf4_code(__fmul_rn(v[2 * k], inv), thr, t7);
-            const uint32_t lo = nf4_code(__fmul_rn(v[2 * k + 1], inv), thr, t7);
-            word |= ((hi << 4) | lo) << (8 * k);
+        for (int j = 0; j < 2; ++j) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t hi = nf4_code(__fmul_rn(v[8 * j + 2 * k], inv), thr, t7);
+                const uint32_t lo = nf4_code(__fmul_rn(v[8 * j + 2 * k + 1], inv), thr, t7);
+                word |= ((hi << 4) | lo) << (8 * k);
+            }
+            if (valid) __stcs(packed + 2 * w + j, word);
         }
-        if (valid) {
-            __stcs(packed + w, word);
-            if ((threadIdx.x % L) == 0) absmax[(w << 3) / BS] = am;
-        }
+        if (valid && (threadIdx.x % L) == 0) absmax[(w << 4) / BS] = am;
     }
 }
 
@@ -453,9 +457,9 @@ int launch_quantize_bs(const InT *src, int64_t n, const float *thr, uint8_t *pac
     const int64_t nfull_blocks = n / BS;
     const int64_t nfull_words = nfull_blocks * (BS / 8);
     if (nfull_words > 0) {
-        const int64_t want = (nfull_words + kThreads - 1) / kThreads;
-        const int64_t cap = int64_t(sm_count()) * 8;
-        const int grid = int(want > cap ? cap : want);
+        const int64_t want = (nfull_words / 2 + kThreads - 1) / kThreads;
+        const int64_t cap = int64_t(sm_count()) * 16;
+        const int grid = int(want < 1 ? 1 : (want > cap ? cap : want));
         k_quantize<InT, BS><<<grid, kThreads, 0, st>>>(src, nfull_words, thr, reinterpret_cast<uint32_t *>(packed), absmax);
         int rc = check_launch("nf4_quantize");
         if (rc) return rc;
