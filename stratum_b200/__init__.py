@@ -6,9 +6,12 @@ so it drops in for that path; the compute runs in libstratum_nf4.so (C ABI:
 include/stratum_nf4.h).
 """
 
-from .assign import assign_layers_to_devices
-from .functional import QuantState, dequantize_4bit, quantize_4bit
+from .assign import assign_layers_to_devices, balanced_strata, strata
+from .boundary import DeviceTransferPool, make_boundary_hook
+from .experts import NF4Experts
+from .functional import QuantState, dequantize_4bit, dequantize_4bit_many, quantize_4bit
 from .nf4_linear import NF4Linear
+from .pipeline import RankPipeline, StratumPipeline
 from .stage import DeviceStage
 from .upload import (
     FP16_ATTR,
@@ -26,6 +29,7 @@ from .upload import (
     prepare_fp16_staged,
     prepare_nf4,
     prepare_nf4_from_cache,
+    to_nf4_experts,
     to_nf4_linear,
     upload_stream,
 )
@@ -35,4 +39,6 @@ __all__ = [
     "NF4_ATTR", "FP16_ATTR", "NF4Payload", "FP16StagedPayload", "NF4Prefetch", "NF4Stats", "prepare_nf4",
     "prepare_nf4_from_cache", "prepare_fp16_staged", "ensure_weights", "free_weights", "prefetch_weights",
     "ensure_prefetched_weights", "upload_stream", "estimate_module_upload_gib", "build_layer_arena", "to_nf4_linear",
+    "to_nf4_experts", "NF4Experts", "dequantize_4bit_many", "StratumPipeline", "RankPipeline", "DeviceTransferPool",
+    "make_boundary_hook", "balanced_strata", "strata",
 ]

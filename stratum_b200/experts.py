@@ -84,6 +84,7 @@ class NF4Experts(nn.Module):
         self.gate_up_state = gate_up_state
         self.down = down
         self.down_state = down_state
+        self.streamed = False
         for qs, shape, what in ((gate_up_state, (self.num_experts * 2 * self.intermediate_dim, self.hidden_dim),
                                  "gate_up"),
                                 (down_state, (self.num_experts * self.hidden_dim, self.intermediate_dim), "down")):
@@ -107,6 +108,48 @@ class NF4Experts(nn.Module):
         dq, dqs = quantize_4bit(dn.reshape(-1, dn.shape[-1]).to(dev), blocksize=64,
                                 compress_statistics=compress_statistics, quant_type="nf4")
         return cls(E, H, I2 // 2, gq, gqs, dq, dqs)
+
+    @classmethod
+    def streamed_from(cls, gate_up_weight: nn.Parameter, gate_up_payload, down_weight: nn.Parameter,
+                      down_payload) -> "NF4Experts":
+        """Experts fed by the streaming contract: ``gate_up_weight`` / ``down_weight`` are
+        the frozen 3-D placeholder parameters carrying the NF4 payloads that
+        ``upload.prepare_nf4`` attached (the reference's [-1, last] staging);
+        ``ensure_weights`` uploads them into this module, ``free_weights`` drops them."""
+        E, I2, H = (int(d) for d in gate_up_payload.shape)
+        m = cls(E, H, I2 // 2)
+        m.gate_up_weight = gate_up_weight
+        m.down_weight = down_weight
+        gate_up_weight.requires_grad_(False)
+        down_weight.requires_grad_(False)
+        if tuple(down_payload.shape) != (E, H, I2 // 2):
+            raise ValueError(f"NF4Experts: down payload shape {tuple(down_payload.shape)} != {(E, H, I2 // 2)}")
+        m.streamed = True
+        return m
+
+    def load_device_state(self, which: str, quantized: torch.Tensor, quant_state: QuantState) -> None:
+        """Install one uploaded weight (``which`` = "gate_up_weight" or "down_weight"); the
+        quant state's shape becomes the flattened [E*N_e, K] the grouped kernels take."""
+        shape = tuple(int(d) for d in quant_state.shape)
+        if len(shape) == 3:
+            quant_state.shape = (shape[0] * shape[1], shape[2])
+        if which == "gate_up_weight":
+            self.gate_up, self.gate_up_state = quantized, quant_state
+        elif which == "down_weight":
+            self.down, self.down_state = quantized, quant_state
+        else:
+            raise ValueError(f"NF4Experts: unknown weight {which!r}")
+
+    def device_state_on(self, which: str, device: torch.device) -> bool:
+        t = self.gate_up if which == "gate_up_weight" else self.down
+        return t is not None and t.device == device
+
+    def drop_device_state(self, which: str) -> bool:
+        if which == "gate_up_weight":
+            had, self.gate_up, self.gate_up_state = self.gate_up is not None, None, None
+        else:
+            had, self.down, self.down_state = self.down is not None, None, None
+        return had
 
     @property
     def resident(self) -> bool:

@@ -170,12 +170,33 @@ def _build_param_owner_map(module: nn.Module) -> dict[int, tuple[nn.Module, str]
     return pmap
 
 
+class _ExpertsWeight:
+    """One of a streamed NF4Experts' two weights, seen as a fused owner."""
+
+    def __init__(self, owner, which: str):
+        self.owner, self.which = owner, which
+
+    def load_device_state(self, quantized, quant_state) -> None:
+        self.owner.load_device_state(self.which, quantized, quant_state)
+
+    def device_state_on(self, device) -> bool:
+        return self.owner.device_state_on(self.which, device)
+
+    def drop_device_state(self) -> bool:
+        return self.owner.drop_device_state(self.which)
+
+
 def _fused_owner(owner: Optional[nn.Module], pname: Optional[str]):
-    """The NF4Linear that consumes this parameter's payload directly, if any."""
+    """The fused module that consumes this parameter's payload directly, if any:
+    a streamed NF4Linear (its ``weight``) or a streamed NF4Experts (its
+    ``gate_up_weight`` / ``down_weight``)."""
+    from .experts import NF4Experts
     from .nf4_linear import NF4Linear
 
     if isinstance(owner, NF4Linear) and pname == "weight" and owner.streamed:
         return owner
+    if isinstance(owner, NF4Experts) and owner.streamed and pname in ("gate_up_weight", "down_weight"):
+        return _ExpertsWeight(owner, pname)
     return None
 
 
@@ -748,5 +769,32 @@ def to_nf4_linear(module: nn.Module, *, lora_r: int = 0, lora_alpha: float = 16.
                 new.attach_lora(lora_r, lora_alpha, dtype=lora_dtype,
                                 device=lora_device if lora_device is not None else torch.device("cpu"))
             setattr(parent, cname, new)
+            count += 1
+    return count
+
+
+@torch.no_grad()
+def to_nf4_experts(module: nn.Module) -> int:
+    """Replace every routed-experts module whose 3-D ``gate_up_proj`` / ``down_proj``
+    carry NF4 payloads (HF ``Qwen3MoeExperts`` after :func:`prepare_nf4`, staged as
+    ``[-1, last]`` like stratum/upload.py:361-366) by a streamed
+    :class:`~stratum_b200.experts.NF4Experts` fed by ``ensure_weights`` and consumed
+    by the grouped NF4 kernels.  Returns the number of modules converted."""
+    from .experts import NF4Experts
+
+    count = 0
+    for parent_name, parent in list(module.named_modules()):
+        for cname, child in list(parent.named_children()):
+            gu = getattr(child, "gate_up_proj", None)
+            dn = getattr(child, "down_proj", None)
+            if not isinstance(gu, nn.Parameter) or not isinstance(dn, nn.Parameter):
+                continue
+            gp, dp = getattr(gu, NF4_ATTR, None), getattr(dn, NF4_ATTR, None)
+            if gp is None or dp is None or len(gp.shape) != 3:
+                continue
+            act = getattr(child, "act_fn", None)
+            if act is not None and not isinstance(act, nn.SiLU) and type(act).__name__ not in ("SiLU", "SiLUActivation"):
+                continue
+            setattr(parent, cname, NF4Experts.streamed_from(gu, gp, dn, dp))
             count += 1
     return count

@@ -308,3 +308,34 @@ def test_nf4_experts_matches_transformers_module():
         out = mod(x, idx, w)
     # HF rounds gate|up, h and each of the k products to bf16; the fused path keeps fp32 until the output
     assert relative_error(out.float(), ref.float()) < TOL
+
+
+def test_streamed_experts_through_the_upload_contract():
+    """prepare_nf4 -> to_nf4_experts -> ensure_weights gives the same forward as quantizing
+    the experts directly; free_weights drops the device copies; a layer arena works too."""
+    from stratum_b200 import upload
+
+    E, H, I, T, k = 16, 256, 128, 300, 4
+    g0 = torch.Generator(device=DEV).manual_seed(21)
+    experts = torch.nn.Module()
+    experts.gate_up_proj = torch.nn.Parameter((torch.randn(E, 2 * I, H, generator=g0, device=DEV) * 0.02).half(),
+                                              requires_grad=False)
+    experts.down_proj = torch.nn.Parameter((torch.randn(E, H, I, generator=g0, device=DEV) * 0.02).half(),
+                                           requires_grad=False)
+    experts.act_fn = torch.nn.SiLU()
+    direct = NF4Experts.from_experts(experts)
+    block = torch.nn.Module()
+    block.experts = experts
+    upload.prepare_nf4(block, verbose=False, device=DEV)
+    assert upload.to_nf4_experts(block) == 1
+    x = torch.randn(T, H, generator=g0, device=DEV).to(torch.bfloat16)
+    wts, idx = torch.topk(torch.softmax(torch.randn(T, E, generator=g0, device=DEV), -1), k, -1)
+    for arena in (False, True):
+        if arena:
+            upload.build_layer_arena(block)
+        assert upload.ensure_weights(block, 0) == 2
+        assert block.experts.resident
+        with torch.no_grad():
+            assert torch.equal(block.experts(x, idx, wts), direct(x, idx, wts))
+        assert upload.free_weights(block) == 2
+        assert not block.experts.resident

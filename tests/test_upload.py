@@ -256,3 +256,30 @@ def test_balanced_strata_minimise_the_largest_load():
                     if n > 1 else L + tail
                 assert load <= best + 1e-9, (L, n, tail, [len(s) for s in st], load, best)
     assert [len(s) for s in balanced_strata(32, 8, tail_cost=1.5)] == [4, 4, 4, 4, 4, 4, 5, 3]
+
+
+def test_to_nf4_experts_converts_staged_3d_experts():
+    """HF-style experts with NF4-staged 3-D params become a streamed NF4Experts whose
+    two placeholder parameters keep their payloads (the upload contract feeds them)."""
+    from stratum_b200.experts import NF4Experts
+
+    E, H, I = 4, 64, 32
+    experts = nn.Module()
+    experts.gate_up_proj = nn.Parameter(torch.randn(E, 2 * I, H, dtype=torch.float16), requires_grad=False)
+    experts.down_proj = nn.Parameter(torch.randn(E, H, I, dtype=torch.float16), requires_grad=False)
+    experts.act_fn = nn.SiLU()
+    block = nn.Module()
+    block.experts = experts
+    _run_prepare(block, min_numel=8)
+    assert upload.to_nf4_experts(block) == 1
+    m = block.experts
+    assert isinstance(m, NF4Experts) and m.streamed and not m.resident
+    assert (m.num_experts, m.hidden_dim, m.intermediate_dim) == (E, H, I)
+    names = dict(m.named_parameters())
+    assert set(names) == {"gate_up_weight", "down_weight"}
+    assert getattr(names["gate_up_weight"], NF4_ATTR).shape == (E, 2 * I, H)
+    owner_map = upload._build_param_owner_map(block)
+    own, pname = owner_map[id(names["down_weight"])]
+    assert upload._fused_owner(own, pname) is not None
+    with pytest.raises(RuntimeError):
+        m(torch.zeros(2, H, dtype=torch.bfloat16), torch.zeros(2, 1, dtype=torch.long), torch.ones(2, 1))
