@@ -29,6 +29,7 @@ from .upload import (
     prepare_fp16_staged,
     prepare_nf4,
     prepare_nf4_from_cache,
+    stream_load_and_quantize_module,
     to_nf4_experts,
     to_nf4_linear,
     upload_stream,
@@ -40,5 +41,5 @@ __all__ = [
     "prepare_nf4_from_cache", "prepare_fp16_staged", "ensure_weights", "free_weights", "prefetch_weights",
     "ensure_prefetched_weights", "upload_stream", "estimate_module_upload_gib", "build_layer_arena", "to_nf4_linear",
     "to_nf4_experts", "NF4Experts", "dequantize_4bit_many", "StratumPipeline", "RankPipeline", "DeviceTransferPool",
-    "make_boundary_hook", "balanced_strata", "strata",
+    "make_boundary_hook", "balanced_strata", "strata", "stream_load_and_quantize_module",
 ]

@@ -798,3 +798,228 @@ def to_nf4_experts(module: nn.Module) -> int:
             setattr(parent, cname, NF4Experts.streamed_from(gu, gp, dn, dp))
             count += 1
     return count
+
+
+# --------------------------------------------------------------------------------
+# streaming load + quantize (checkpoint -> NF4 payloads, one tensor at a time)
+# --------------------------------------------------------------------------------
+
+def _ckpt_key_fn(module: nn.Module):
+    """``keys(param_name) -> [checkpoint key candidates]`` for a pipeline module:
+    the name itself, with PEFT's ``.base_layer.`` and wrappers' ``.inner.`` /
+    ``.layer.`` removed, with a ``model.`` prefix, and wrapped decoder layers
+    (modules with ``idx`` and ``layer``) mapped to ``model.layers.{idx}.``
+    (the reference's rule, stratum/upload.py:425-473)."""
+    import re
+
+    layer_prefixes = []
+    for mname, sub in module.named_modules():
+        idx = getattr(sub, "idx", None)
+        if isinstance(idx, int) and hasattr(sub, "layer"):
+            layer_prefixes.append((f"{mname}.layer." if mname else "layer.", f"model.layers.{idx}."))
+
+    def no_base(n: str) -> str:
+        return n.replace(".base_layer.", ".")
+
+    def keys(pname: str) -> list[str]:
+        out: list[str] = []
+        pname = _canonical_param_name(pname)
+
+        def add(name: str) -> None:
+            variants = [name]
+            if ".inner." in name:
+                variants.append(name.replace(".inner.", "."))
+            for v in variants:
+                stripped = re.sub(r"\.layer\.(?!layer)", ".", v)
+                for k in (v, no_base(v), stripped, no_base(stripped)):
+                    out.append(k)
+                for k in (v, no_base(v), stripped, no_base(stripped)):
+                    out.append(f"model.{k}")
+
+        add(pname)
+        if pname == "lm_head.weight":  # tied embeddings
+            add("model.embed_tokens.weight")
+            add("embed_tokens.weight")
+        for prefix, global_prefix in layer_prefixes:
+            if pname.startswith(prefix):
+                add(global_prefix + pname[len(prefix):])
+        return list(dict.fromkeys(out))
+
+    return keys
+
+
+def _load_stacked_experts(handle, keys: set, pname: str, param, key_fn):
+    """A 3-D expert parameter stacked from per-expert checkpoint tensors: the
+    reference's LFM2 layout (``...feed_forward.experts.{e}.w1/w3/w2.weight``,
+    stratum/upload.py:476-532) and, as an extension, HF Qwen3-MoE's
+    (``...mlp.experts.{e}.gate_proj/up_proj/down_proj.weight``)."""
+    if param.ndim != 3:
+        return None
+    E = int(param.shape[0])
+    layouts = (
+        (".feed_forward.experts.gate_up_proj", ".feed_forward.experts", ("w1", "w3")),
+        (".feed_forward.experts.down_proj", ".feed_forward.experts", ("w2",)),
+        (".mlp.experts.gate_up_proj", ".mlp.experts", ("gate_proj", "up_proj")),
+        (".mlp.experts.down_proj", ".mlp.experts", ("down_proj",)),
+    )
+    for cand in key_fn(pname):
+        for suffix, base_sfx, parts in layouts:
+            if not cand.endswith(suffix):
+                continue
+            base = cand[: -len(suffix)] + base_sfx
+            need = [f"{base}.{e}.{p}.weight" for e in range(E) for p in parts]
+            if not all(k in keys for k in need):
+                continue
+            rows = []
+            for e in range(E):
+                ts = [handle.get_tensor(f"{base}.{e}.{p}.weight") for p in parts]
+                rows.append(torch.cat(ts, dim=0) if len(ts) > 1 else ts[0])
+            return torch.stack(rows, dim=0)
+    return None
+
+
+@torch.no_grad()
+def stream_load_and_quantize_module(
+    module: nn.Module,
+    hf_model_name: str,
+    *,
+    min_numel: int = 4096,
+    cache_dir: Optional[Path | str] = None,
+    blocksize: int = 64,
+    quant_type: str = "nf4",
+    verbose: bool = False,
+    compress_statistics: bool = False,
+    device=None,
+) -> Optional[NF4Stats]:
+    """Load and NF4-quantize a meta-device module in one streaming pass
+    (reference: stratum/upload.py:670-904).  For each frozen parameter still on
+    the meta device (or empty): an NF4-eligible one is served from the payload
+    cache if present, else its checkpoint tensor is read, quantized on the GPU
+    and dropped before the next one; other parameters get their checkpoint
+    tensor.  Peak host memory is the payloads so far plus one tensor.
+
+    ``hf_model_name`` is a local checkpoint directory or a cached hub id
+    (``model.safetensors`` or a sharded ``model.safetensors.index.json``).
+    Returns ``NF4Stats``, or ``None`` when a parameter has no checkpoint key or
+    a shard is missing (the reference's contract).
+    """
+    from safetensors import safe_open
+
+    def locate(fname: str) -> Optional[Path]:
+        local = Path(hf_model_name) / fname
+        if local.exists():
+            return local
+        try:
+            from transformers.utils.hub import cached_file
+
+            p = cached_file(hf_model_name, fname, cache_dir=None)
+            return Path(p) if p and Path(p).exists() else None
+        except Exception:
+            return None
+
+    cache_root = Path(cache_dir) if cache_dir else None
+    owner_map = _build_param_owner_map(module)
+    key_fn = _ckpt_key_fn(module)
+
+    def eligible(p) -> bool:
+        return p.ndim >= 2 and p.numel() >= min_numel and p.dtype in (torch.float16, torch.bfloat16, torch.float32)
+
+    stats = NF4Stats()
+    needed = []
+    for n, p in module.named_parameters():
+        if hasattr(p, NF4_ATTR):
+            pl = cast(NF4Payload, getattr(p, NF4_ATTR))
+            stats.tensors += 1
+            stats.source_bytes += pl.source_bytes
+            stats.payload_bytes += pl.payload_bytes
+            continue
+        if p.requires_grad or (p.device.type != "meta" and p.data.numel() != 0):
+            continue
+        needed.append((n, p))
+
+    def attach(name, param, payload) -> None:
+        setattr(param, NF4_ATTR, payload)
+        owner, pname = owner_map.get(id(param), (None, None))
+        _replace_param_data(param, torch.empty(0, dtype=payload.dtype, device="cpu"), owner=owner, pname=pname)
+        stats.tensors += 1
+        stats.source_bytes += payload.source_bytes
+        stats.payload_bytes += payload.payload_bytes
+
+    def from_cache(name, param) -> bool:
+        if cache_root is None:
+            return False
+        payload = _load_payload_from_cache(_cache_path(cache_root, name), param, blocksize=blocksize,
+                                           quant_type=quant_type, compress_statistics=compress_statistics)
+        if payload is None:
+            return False
+        attach(name, param, payload)
+        stats.cache_hits += 1
+        return True
+
+    def consume(name, param, t) -> bool:
+        t = t.to(device="cpu", dtype=param.dtype)
+        if eligible(param):
+            payload = _quantize_param(t, blocksize, quant_type, compress_statistics, tuple(param.shape),
+                                      param.numel() * param.element_size(), device)
+            if cache_root is not None:
+                _save_payload_to_cache(_cache_path(cache_root, name), payload)
+                stats.cache_writes += 1
+                stats.cache_misses += 1
+            attach(name, param, payload)
+            return True
+        owner, pname = owner_map.get(id(param), (None, None))
+        try:
+            _replace_param_data(param, t, owner=owner, pname=pname)
+        except (RuntimeError, TypeError):
+            return False
+        return True
+
+    if needed:
+        index = locate("model.safetensors.index.json")
+        if index is not None:
+            import json
+
+            weight_map = json.loads(index.read_text())["weight_map"]
+            todo = []
+            for n, p in needed:
+                if eligible(p) and from_cache(n, p):
+                    continue
+                ck = next((k for k in key_fn(n) if k in weight_map), None)
+                if ck is None:
+                    if verbose:
+                        print(f"  stream_nf4: no checkpoint key for {n}", flush=True)
+                    return None
+                todo.append((n, p, ck))
+            by_shard: dict = {}
+            for n, p, ck in todo:
+                by_shard.setdefault(weight_map[ck], []).append((n, p, ck))
+            for shard, items in by_shard.items():
+                sp = index.parent / shard
+                if not sp.exists():
+                    return None
+                with safe_open(str(sp), framework="pt") as f:
+                    for n, p, ck in items:
+                        if not consume(n, p, f.get_tensor(ck)):
+                            return None
+        else:
+            single = locate("model.safetensors")
+            if single is None:
+                return None
+            with safe_open(str(single), framework="pt") as f:
+                all_keys = set(f.keys())
+                for n, p in needed:
+                    if eligible(p) and from_cache(n, p):
+                        continue
+                    ck = next((k for k in key_fn(n) if k in all_keys), None)
+                    t = f.get_tensor(ck) if ck is not None else _load_stacked_experts(f, all_keys, n, p, key_fn)
+                    if t is None:
+                        if verbose:
+                            print(f"  stream_nf4: no checkpoint key for {n}", flush=True)
+                        return None
+                    if not consume(n, p, t):
+                        return None
+    if verbose:
+        print(f"  nf4 total: {stats.tensors} tensors, {stats.source_bytes / 1024**3:.2f} GiB -> "
+              f"{stats.payload_bytes / 1024**3:.2f} GiB payload (cache hits={stats.cache_hits} "
+              f"misses={stats.cache_misses} writes={stats.cache_writes})", flush=True)
+    return stats

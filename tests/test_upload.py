@@ -283,3 +283,88 @@ def test_to_nf4_experts_converts_staged_3d_experts():
     assert upload._fused_owner(own, pname) is not None
     with pytest.raises(RuntimeError):
         m(torch.zeros(2, H, dtype=torch.bfloat16), torch.zeros(2, 1, dtype=torch.long), torch.ones(2, 1))
+
+
+def _stream_module():
+    """A meta-device wrapped layer (idx 3) with a frozen linear, a 1-D norm and 3-D experts."""
+
+    class Wrapped(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.idx = 3
+            self.layer = nn.Module()
+            with torch.device("meta"):
+                self.layer.q_proj = nn.Linear(64, 128, bias=False, dtype=torch.float16)
+                self.layer.norm = nn.Module()
+                self.layer.norm.weight = nn.Parameter(torch.empty(64, dtype=torch.float16))
+                self.layer.mlp = nn.Module()
+                self.layer.mlp.experts = nn.Module()
+                self.layer.mlp.experts.gate_up_proj = nn.Parameter(torch.empty(2, 32, 64, dtype=torch.float16))
+                self.layer.mlp.experts.down_proj = nn.Parameter(torch.empty(2, 64, 16, dtype=torch.float16))
+
+    root = nn.Module()
+    root.w = Wrapped()
+    root.requires_grad_(False)
+    return root
+
+
+def _stream_ckpt(tmp_path, sharded: bool):
+    from safetensors.torch import save_file
+
+    g = torch.Generator().manual_seed(0)
+    t = {"model.layers.3.q_proj.weight": torch.randn(128, 64, generator=g).half(),
+         "model.layers.3.norm.weight": torch.randn(64, generator=g).half()}
+    for e in range(2):
+        t[f"model.layers.3.mlp.experts.{e}.gate_proj.weight"] = torch.randn(16, 64, generator=g).half()
+        t[f"model.layers.3.mlp.experts.{e}.up_proj.weight"] = torch.randn(16, 64, generator=g).half()
+        t[f"model.layers.3.mlp.experts.{e}.down_proj.weight"] = torch.randn(64, 16, generator=g).half()
+    if sharded:
+        import json
+
+        names = sorted(t)
+        a, b = names[: len(names) // 2], names[len(names) // 2:]
+        save_file({k: t[k] for k in a}, str(tmp_path / "s1.safetensors"))
+        save_file({k: t[k] for k in b}, str(tmp_path / "s2.safetensors"))
+        wm = {k: "s1.safetensors" for k in a} | {k: "s2.safetensors" for k in b}
+        # stacked experts are addressed by their fused name in a sharded index
+        (tmp_path / "model.safetensors.index.json").write_text(json.dumps({"weight_map": wm}))
+    else:
+        save_file(t, str(tmp_path / "model.safetensors"))
+    return t
+
+
+def test_stream_load_and_quantize_single_file(tmp_path):
+    ckpt = _stream_ckpt(tmp_path, sharded=False)
+    m = _stream_module()
+    fake, calls = _fake_quantizer()
+    cache = tmp_path / "cache"
+    with mock.patch.object(upload, "_quantize_param", side_effect=fake):
+        stats = upload.stream_load_and_quantize_module(m, str(tmp_path), min_numel=512, cache_dir=cache)
+    assert stats is not None and stats.tensors == 3 and stats.cache_writes == 3
+    q = m.w.layer.q_proj.weight
+    assert getattr(q, NF4_ATTR).shape == (128, 64) and q.data.numel() == 0
+    gu = m.w.layer.mlp.experts.gate_up_proj
+    assert getattr(gu, NF4_ATTR).shape == (2, 32, 64)
+    assert (2, 32, 64) in calls  # the stacked per-expert tensor went through the quantizer
+    norm = m.w.layer.norm.weight
+    assert norm.device.type == "cpu" and torch.equal(norm.data, ckpt["model.layers.3.norm.weight"])
+    # a second pass over a fresh module is served from the payload cache
+    m2 = _stream_module()
+    with mock.patch.object(upload, "_quantize_param", side_effect=AssertionError("should hit the cache")):
+        stats2 = upload.stream_load_and_quantize_module(m2, str(tmp_path), min_numel=512, cache_dir=cache)
+    assert stats2.cache_hits == 3
+
+
+def test_stream_load_sharded_and_missing_key(tmp_path):
+    _stream_ckpt(tmp_path, sharded=True)
+    m = _stream_module()
+    del m.w.layer.mlp  # per-expert keys are stacked only for single-file checkpoints (as the reference)
+    fake, _ = _fake_quantizer()
+    with mock.patch.object(upload, "_quantize_param", side_effect=fake):
+        stats = upload.stream_load_and_quantize_module(m, str(tmp_path), min_numel=512)
+    assert stats is not None and stats.tensors == 1
+    m3 = _stream_module()
+    with torch.device("meta"):
+        m3.w.layer.extra = nn.Parameter(torch.empty(8, 8), requires_grad=False)
+    with mock.patch.object(upload, "_quantize_param", side_effect=fake):
+        assert upload.stream_load_and_quantize_module(m3, str(tmp_path), min_numel=512) is None
