@@ -139,3 +139,26 @@ def test_device_stage_streams_layers_with_overlap():
     assert relative_error(out.float(), eager.float()) < 1e-2
     upload.free_weights(stage)
     assert all(layer.lin.quantized is None for layer in stage.layers)
+
+
+def test_stream_load_matches_prepare_nf4(tmp_path):
+    """Checkpoint -> stream_load_and_quantize_module gives the same payload bytes as
+    loading the tensor and running prepare_nf4 on it (both quantize on the GPU)."""
+    from safetensors.torch import save_file
+
+    g = torch.Generator().manual_seed(5)
+    w = (torch.randn(512, 256, generator=g) * 0.02).half()
+    save_file({"model.proj.weight": w}, str(tmp_path / "model.safetensors"))
+    with torch.device("meta"):
+        m = torch.nn.Module()
+        m.proj = torch.nn.Linear(256, 512, bias=False, dtype=torch.float16)
+    m.requires_grad_(False)
+    stats = upload.stream_load_and_quantize_module(m, str(tmp_path))
+    assert stats is not None and stats.tensors == 1
+    ref = torch.nn.Module()
+    ref.proj = torch.nn.Linear(256, 512, bias=False, dtype=torch.float16)
+    ref.requires_grad_(False)
+    ref.proj.weight.data.copy_(w)
+    upload.prepare_nf4(ref, verbose=False)
+    a, b = getattr(m.proj.weight, upload.NF4_ATTR), getattr(ref.proj.weight, upload.NF4_ATTR)
+    assert torch.equal(a.quantized, b.quantized) and torch.equal(a.absmax, b.absmax)
