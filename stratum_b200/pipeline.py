@@ -325,6 +325,14 @@ class StratumPipeline(nn.Module):
                                                                for l in s.layers))
             for s in stages]
         self.last_aux: Optional[torch.Tensor] = None
+        self.timing_recorder = None
+        self._layer_timer = None
+        self._plan_adapt_after_n = 0
+        # the reference's bookkeeping names, kept for callers and tests that inspect them:
+        # one module per recompute group (here: per layer), the backward look-ahead fences
+        # of the current step (streamed layers carry their own events here, so it stays empty)
+        self._fwd_group_modules: list[nn.Module] = [layer for s in stages for layer in s.layers]
+        self._pending_bwd_fences: dict = {}
 
     @property
     def n_devices(self) -> int:
@@ -333,6 +341,9 @@ class StratumPipeline(nn.Module):
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
                 labels: Optional[torch.Tensor] = None, **kwargs):
         """Run forward through all stages; returns the loss when labels are given."""
+        self._pending_bwd_fences = {}
+        if self._layer_timer is not None and hasattr(self._layer_timer, "update_times"):
+            self._layer_timer.update_times()
         dev0 = _dev(self.stages[0].device_id)
         if input_ids.device != dev0:
             input_ids = input_ids.to(dev0, non_blocking=True)
@@ -362,6 +373,28 @@ class StratumPipeline(nn.Module):
             if loss is not None:
                 loss = loss + aux.value.detach().to(loss.device)
         return loss
+
+    def set_timing_recorder(self, recorder) -> None:
+        """Attach a timing recorder to every stage's layer spans (stratum/pipeline.py:231-245)."""
+        self.timing_recorder = recorder
+        start = 0
+        for stage in self.stages:
+            stage.set_timing_recorder(recorder, layer_start=start)
+            start += len(stage.layers)
+
+    def set_layer_timer(self, timer, *, adapt_every_n: int = 0) -> None:
+        """Attach a per-layer timer (stratum/pipeline.py:247-268); there is no execute plan
+        to adapt here (every layer is its own recompute group), so ``adapt_every_n`` is kept
+        for the call's shape only."""
+        self._layer_timer = timer
+        self._plan_adapt_after_n = adapt_every_n
+
+    def _param_upload_stream(self, device_id: int) -> Optional["torch.cuda.Stream"]:
+        """The side stream streamed layers of ``device_id`` upload on (None when nothing streams)."""
+        for stage, st in zip(self.stages, self._streamers):
+            if _dev(stage.device_id) == _dev(device_id) and st.enabled:
+                return st.stream
+        return None
 
     def free_all_weights(self) -> None:
         """Drop every streamed layer's device copy (reference: call after backward)."""

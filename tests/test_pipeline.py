@@ -196,3 +196,27 @@ def test_rank_pipeline_matches_autograd(moe, world, schedule, recompute):
     assert set(got) == set(ref_grads)
     for k, g in ref_grads.items():
         torch.testing.assert_close(got[k], g, rtol=1e-4, atol=1e-6, msg=k)
+
+
+def test_stratum_pipeline_keeps_the_reference_hooks():
+    """The reference's recorder / timer setters and the bookkeeping names its tests inspect."""
+    layers = _model(4, False)
+    stages = [DeviceStage(layers[:2], "cpu"), DeviceStage(layers[2:], "cpu")]
+    pipe = StratumPipeline(ToyPrefix(), stages, ToyPostfix())
+
+    class Rec:
+        def span(self, name, **kw):
+            import contextlib
+
+            return contextlib.nullcontext()
+
+    rec = Rec()
+    pipe.set_timing_recorder(rec)
+    assert stages[1].timing_recorder is rec and stages[1].layer_start == 2
+    pipe.set_layer_timer(None, adapt_every_n=0)
+    assert [id(m) for m in pipe._fwd_group_modules] == [id(l) for l in layers]
+    pipe._pending_bwd_fences[99] = object()
+    ids, labels = _data(1)
+    pipe(ids, labels=labels).backward()
+    assert 99 not in pipe._pending_bwd_fences
+    assert pipe._param_upload_stream(0) is None
