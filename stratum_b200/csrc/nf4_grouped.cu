@@ -20,9 +20,13 @@
 //            h[t, j] = silu(gate) * up is formed in the epilogue (from the 16-bit
 //            gate and up, as HF's bf16 forward forms it) and only h -- half the
 //            width of gate_up -- is written, plus gate|up when the backward needs it.
-// A tile whose expert has fewer than 256 tokens left issues MMAs only as wide as
-// those tokens (rounded up to 16), so the tail tiles of skewed routing cost
-// tensor-core time in proportion to their tokens.
+// An expert's tokens are split into equal token tiles (multiples of 16, at most
+// 320 in the forward, 256 in the input gradient), and a tile's MMAs are only as
+// wide as its tokens, so skewed routing costs tensor-core time in proportion to
+// the tokens and no tile re-dequantizes a weight tile for a handful of them.
+// The forward covers up to 320 tokens with two MMAs per K slice (N <= 256 into
+// accumulator columns [0, 256), the rest into [256, 320)): at 4096 x top-8
+// tokens over 128 experts (~256 per expert) every expert is one token tile.
 #include "common.cuh"
 #include "nf4_decode.cuh"
 #include "sm100.cuh"
@@ -52,14 +56,16 @@ struct Tile {
 };
 
 // offsets[E+1] (device) -> tiles[]; order: expert, token tile, then weight-row
-// tile innermost, so CTAs running at the same time share a token tile.  One
-// block: each thread counts one expert's tiles, a block scan places them.
-// Offsets that are not non-decreasing within [0, Ttot] set the status word
-// and leave the table empty, so no kernel can store outside y.
+// tile innermost, so CTAs running at the same time share a token tile.  An
+// expert's n tokens become ceil(n / cap) tiles of equal size rounded up to 16
+// (the last one shorter).  One block: each thread counts one expert's tiles, a
+// block scan places them.  Offsets that are not non-decreasing within
+// [0, Ttot] set the status word and leave the table empty, so no kernel can
+// store outside y.
 constexpr int kTileThreads = 256;
 
 __global__ void __launch_bounds__(kTileThreads)
-k_build_tiles(const int *__restrict__ offsets, int E, int m_tiles, int64_t Ttot, Tile *__restrict__ tiles,
+k_build_tiles(const int *__restrict__ offsets, int E, int m_tiles, int cap, int64_t Ttot, Tile *__restrict__ tiles,
               int *__restrict__ ntiles, int max_tiles, int *__restrict__ status) {
     __shared__ int warp_sums[kTileThreads / 32];
     __shared__ int base_s;
@@ -79,11 +85,15 @@ k_build_tiles(const int *__restrict__ offsets, int E, int m_tiles, int64_t Ttot,
     }
     for (int e0 = 0; e0 < E; e0 += kTileThreads) {
         const int e = e0 + threadIdx.x;
-        int a = 0, b = 0, cnt = 0;
+        int a = 0, b = 0, cnt = 0, sz = cap;
         if (e < E) {
             a = offsets[e];
             b = offsets[e + 1];
-            cnt = (b - a + BN - 1) / BN * m_tiles;
+            if (b > a) {
+                const int n = b - a, parts = (n + cap - 1) / cap;
+                sz = ((n + parts - 1) / parts + 15) & ~15;  // <= cap (a multiple of 16)
+                cnt = (n + sz - 1) / sz * m_tiles;
+            }
         }
         int v = cnt;  // inclusive scan within the warp
 #pragma unroll
@@ -105,9 +115,9 @@ k_build_tiles(const int *__restrict__ offsets, int E, int m_tiles, int64_t Ttot,
         __syncthreads();
         const int start = base_s + (wid ? warp_sums[wid - 1] : 0) + v - cnt;
         int n = start;
-        for (int t0 = a; t0 < b; t0 += BN)
+        for (int t0 = a; t0 < b; t0 += sz)
             for (int m = 0; m < m_tiles; ++m, ++n)
-                if (n < max_tiles) tiles[n] = Tile{e, m, t0, b};
+                if (n < max_tiles) tiles[n] = Tile{e, m, t0, t0 + sz < b ? t0 + sz : b};
         __syncthreads();
         if (threadIdx.x == kTileThreads - 1) base_s = start + cnt;
         __syncthreads();
@@ -122,10 +132,10 @@ k_build_tiles(const int *__restrict__ offsets, int E, int m_tiles, int64_t Ttot,
     }
 }
 
-// Tokens of a tile that belong to its expert, and the MMA width that covers
-// them (a multiple of 16, at most BN): a tail tile of a few tokens issues a
-// narrow MMA instead of a full 256-column one.
-__device__ __forceinline__ int tile_cols(const Tile &t) { return t.t_end - t.t0 < BN ? t.t_end - t.t0 : BN; }
+// Tokens of a tile (all of its expert; at most the table's cap), and the MMA
+// width that covers them (a multiple of 16): a tile of a few tokens issues a
+// narrow MMA instead of a full-width one.
+__device__ __forceinline__ int tile_cols(const Tile &t) { return t.t_end - t.t0; }
 __device__ __forceinline__ int tile_mma_n(const Tile &t) { return (tile_cols(t) + 15) & ~15; }
 
 template <bool BF16>
@@ -154,11 +164,20 @@ __device__ __forceinline__ uint4 pack8(const float f[8]) {
 
 // ------------------------------------------------------------- forward --
 
-constexpr int F_XS = 4, F_WS = 6, F_AS = 8;
+// Token tiles of up to F_TMAX tokens: accumulator columns [0, F_TMAX) (an N <= 256
+// MMA into [0, 256) plus an N <= 64 one into [256, 320)), the dequantized A ring
+// in the remaining TMEM columns [F_TMAX, 512).  x arrives in 64-token boxes, only
+// as many as the tile's MMA width needs.
+constexpr int F_TMAX = 320;
+constexpr int F_XBOX = 64;
+constexpr int F_XBOX_BYTES = F_XBOX * BK * 2;
+constexpr int F_X_BYTES = F_TMAX * BK * 2;
+constexpr int F_XS = 3, F_WS = 6, F_AS = (512 - F_TMAX) / 32;
 constexpr int F_W_BYTES = BM * BK / 2;
-constexpr int F_STAGE_BYTES = BN * BM * 2;  // [256 tokens][128 rows] 16-bit, 2 swizzled halves
-constexpr int F_SMEM = 1024 + F_XS * X_BYTES + F_STAGE_BYTES + F_WS * F_W_BYTES + 512 + 1088;
+constexpr int F_STAGE_BYTES = F_TMAX * BM * 2;  // [320 tokens][128 rows] 16-bit, 2 swizzled halves
+constexpr int F_SMEM = 1024 + F_XS * F_X_BYTES + F_STAGE_BYTES + F_WS * F_W_BYTES + 512 + 1088;
 static_assert(F_SMEM <= 232448, "smem");
+static_assert(F_TMAX % F_XBOX == 0 && F_TMAX > BN && F_TMAX - BN <= BN && F_AS >= 4, "forward tile shape");
 
 struct FwdParams {
     const Tile *tiles;
@@ -184,7 +203,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *x0 = base;
-    uint8_t *y0 = x0 + F_XS * X_BYTES;
+    uint8_t *y0 = x0 + F_XS * F_X_BYTES;
     uint8_t *w0 = y0 + F_STAGE_BYTES;
     uint64_t *bars = reinterpret_cast<uint64_t *>(w0 + F_WS * F_W_BYTES);
     uint64_t *xfull = bars, *xempty = xfull + F_XS, *wfull = xempty + F_XS, *wempty = wfull + F_WS;
@@ -228,11 +247,14 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
                 const Tile t = tile_at(tl);
+                const int nbox = (tile_mma_n(t) + F_XBOX - 1) / F_XBOX;  // 64-token boxes the MMAs read
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % F_XS;
                     if (!mbar_wait(&xempty[s], ((it / F_XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&xfull[s], X_BYTES);
-                    tma_load_2d(x0 + s * X_BYTES, &tm_x, ks * BK, t.t0, &xfull[s]);
+                    mbar_arrive_expect_tx(&xfull[s], uint32_t(nbox * F_XBOX_BYTES));
+                    for (int bx = 0; bx < nbox; ++bx)
+                        tma_load_2d(x0 + s * F_X_BYTES + bx * F_XBOX_BYTES, &tm_x, ks * BK, t.t0 + bx * F_XBOX,
+                                    &xfull[s]);
                 }
             }
             for (uint32_t j = (it > F_XS ? it - F_XS : 0); j < it; ++j)
@@ -262,7 +284,11 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
             uint32_t it = 0;
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
-                const uint32_t idesc = idesc_f16(BF16, BM, tile_mma_n(tile_at(tl)));
+                // tokens [0, n0) into accumulator columns [0, n0), tokens [BN, BN + n1) into [BN, BN + n1)
+                const int ntot = tile_mma_n(tile_at(tl));
+                const int n0 = ntot < BN ? ntot : BN, n1 = ntot - n0;
+                const uint32_t idesc0 = idesc_f16(BF16, BM, n0);
+                const uint32_t idesc1 = n1 ? idesc_f16(BF16, BM, n1) : 0u;
                 if (!mbar_wait(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
@@ -270,11 +296,14 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                     if (!mbar_wait(&afull[sa], (it / F_AS) & 1, p.status, kErrTimeoutMma) ||
                         !mbar_wait(&xfull[s], (it / F_XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                     tc_fence_after();
-                    const uint64_t bdesc = smem_desc_k_sw128(x0 + s * X_BYTES);
-                    const uint32_t a0 = tmem + 256 + sa * 32;
+                    const uint64_t bdesc0 = smem_desc_k_sw128(x0 + s * F_X_BYTES);
+                    const uint64_t bdesc1 = smem_desc_k_sw128(x0 + s * F_X_BYTES + BN * BK * 2);
+                    const uint32_t a0 = tmem + F_TMAX + sa * 32;
 #pragma unroll
-                    for (int j = 0; j < BK / 16; ++j)
-                        mma_ts_f16(tmem, a0 + j * 8, bdesc + uint64_t(j * 2), idesc, (ks | j) != 0);
+                    for (int j = 0; j < BK / 16; ++j) {
+                        mma_ts_f16(tmem, a0 + j * 8, bdesc0 + uint64_t(j * 2), idesc0, (ks | j) != 0);
+                        if (n1) mma_ts_f16(tmem + BN, a0 + j * 8, bdesc1 + uint64_t(j * 2), idesc1, (ks | j) != 0);
+                    }
                     mma_commit(&xempty[s]);
                     mma_commit(&aempty[sa]);
                 }
@@ -325,7 +354,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
             if (!__all_sync(0xffffffffu, mbar_wait(&aempty[sa], ((it / F_AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
                 break;
             tc_fence_after();
-            tmem_st_32x32b_x32(tmem + lane_addr + 256 + sa * 32, vals);
+            tmem_st_32x32b_x32(tmem + lane_addr + F_TMAX + sa * 32, vals);
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&afull[sa]);
@@ -746,16 +775,19 @@ size_t stratum_nf4_grouped_table_bytes(int64_t total_tokens, int n_experts, int6
 }
 
 // Shared argument checks and tile-table build for the two grouped kernels.
-static int build_table(const int *offsets, int E, int m_tiles, int64_t Ttot, void *table, size_t table_bytes,
-                       int *status, cudaStream_t st, grouped::Tile **tiles, int **ntiles, int *grid) {
+// `cap`: most tokens in a token tile (a multiple of 16, at least 256, so the
+// table size of stratum_nf4_grouped_table_bytes bounds the tile count).
+static int build_table(const int *offsets, int E, int m_tiles, int cap, int64_t Ttot, void *table,
+                       size_t table_bytes, int *status, cudaStream_t st, grouped::Tile **tiles, int **ntiles,
+                       int *grid) {
     const size_t need = table_bytes_for(Ttot, E, m_tiles);
     if (table_bytes < need) return fail(STRATUM_ERR_INVALID, "grouped: tile table needs %zu bytes, got %zu", need, table_bytes);
     STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(table) % 16 == 0, "grouped: tile table must be 16-byte aligned");
     *ntiles = static_cast<int *>(table);
     *tiles = reinterpret_cast<grouped::Tile *>(static_cast<uint8_t *>(table) + 256);
     const int max_tiles = int((table_bytes - 256) / sizeof(grouped::Tile));
-    grouped::k_build_tiles<<<1, grouped::kTileThreads, 0, st>>>(offsets, E, m_tiles, Ttot, *tiles, *ntiles, max_tiles,
-                                                                 status);
+    grouped::k_build_tiles<<<1, grouped::kTileThreads, 0, st>>>(offsets, E, m_tiles, cap, Ttot, *tiles, *ntiles,
+                                                                 max_tiles, status);
     int rc = check_launch("nf4_grouped_tiles");
     if (rc) return rc;
     *grid = sm_count();
@@ -789,11 +821,12 @@ int stratum_nf4_grouped_fwd(const void *x_sorted, int dtype, int64_t Ttot, int K
     const int m_tiles = N_e / 128;
     grouped::Tile *tiles;
     int *ntiles, grid;
-    int rc = build_table(offsets, E, m_tiles, Ttot, table, table_bytes, status, st, &tiles, &ntiles, &grid);
+    int rc = build_table(offsets, E, m_tiles, grouped::F_TMAX, Ttot, table, table_bytes, status, st, &tiles, &ntiles,
+                         &grid);
     if (rc) return rc;
     const CUtensorMapDataType xdt = dtype == STRATUM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUtensorMap mx, mw;
-    rc = grouped::make_map(&mx, xdt, x_sorted, uint64_t(K), uint64_t(Ttot), uint64_t(K) * 2, 64, grouped::BN,
+    rc = grouped::make_map(&mx, xdt, x_sorted, uint64_t(K), uint64_t(Ttot), uint64_t(K) * 2, 64, grouped::F_XBOX,
                            CU_TENSOR_MAP_SWIZZLE_128B, "nf4_grouped_fwd x");
     if (rc) return rc;
     rc = grouped::make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(K / 2), uint64_t(E) * uint64_t(N_e),
@@ -835,7 +868,8 @@ int stratum_nf4_grouped_dx(const void *dy_sorted, int dtype, int64_t Ttot, int N
     const int m_tiles = (K + grouped::BM - 1) / grouped::BM;
     grouped::Tile *tiles;
     int *ntiles, grid;
-    int rc = build_table(offsets, E, m_tiles, Ttot, table, table_bytes, status, st, &tiles, &ntiles, &grid);
+    int rc = build_table(offsets, E, m_tiles, grouped::BN, Ttot, table, table_bytes, status, st, &tiles, &ntiles,
+                         &grid);
     if (rc) return rc;
     const CUtensorMapDataType xdt = dtype == STRATUM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUtensorMap mdy, mw;

@@ -84,7 +84,9 @@ def test_route_skewed_and_empty_experts():
 
 # ----------------------------------------------------------- grouped GEMMs --
 
-SKEWED = [0, 1, 255, 256, 257, 700, 0, 3, 1024, 64]  # empty, single, tile edges, multi-tile
+# empty, single, tile edges (256: one MMA; 257-320: a second, narrower MMA in the
+# forward; 321: two balanced tiles), multi-tile (641, 700, 1024)
+SKEWED = [0, 1, 255, 256, 257, 700, 0, 3, 1024, 64, 300, 320, 321, 641]
 
 
 def _sorted_inputs(counts, K, dtype, seed):
@@ -167,6 +169,50 @@ def test_grouped_dx(dtype, N_e, K):
             ref = dy[a:b].float() @ w_deq[e].to(dtype).float()
             err = relative_error(dx[a:b].float(), ref)
             assert err < TOL, f"expert {e}: rel err {err}"
+
+
+def _tiles_ref(offs, m_tiles, cap):
+    """The tile table's rule: an expert's n tokens in ceil(n / cap) equal tiles
+    rounded up to 16 tokens (the last one shorter), weight-row tiles innermost."""
+    out = []
+    for e in range(len(offs) - 1):
+        a, b = offs[e], offs[e + 1]
+        if b <= a:
+            continue
+        n = b - a
+        parts = -(-n // cap)
+        sz = (-(-n // parts) + 15) // 16 * 16
+        for t0 in range(a, b, sz):
+            out += [(e, m, t0, min(t0 + sz, b)) for m in range(m_tiles)]
+    return out
+
+
+@pytest.mark.parametrize("kind", ["fwd", "dx"])
+def test_grouped_tile_table(kind, monkeypatch):
+    E, N_e, K = len(SKEWED), 256, 384
+    packed, qs, _ = _expert_weight(E, N_e, K, seed=9)
+    r, x = _sorted_inputs(SKEWED, N_e if kind == "dx" else K, torch.bfloat16, seed=10)
+    seen = []
+    real = ops._table
+
+    def spy(*a):
+        t = real(*a)
+        seen.append(t[0])
+        return t
+
+    monkeypatch.setattr(ops, "_table", spy)
+    if kind == "fwd":
+        ops.nf4_grouped_fwd(x, r, packed, qs)
+        m_tiles, cap = N_e // 128, 320
+    else:
+        ops.nf4_grouped_dx(x, r, packed, qs)
+        m_tiles, cap = -(-K // 128), 256
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    raw = seen[0].cpu()
+    n = int(raw[:4].view(torch.int32)[0])
+    got = [tuple(t) for t in raw[256:256 + 16 * n].view(torch.int32).view(-1, 4).tolist()]
+    assert got == _tiles_ref(r.offsets.cpu().tolist(), m_tiles, cap)
 
 
 def test_grouped_rejects_bad_offsets():
