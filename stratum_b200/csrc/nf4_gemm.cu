@@ -337,16 +337,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const int k = lane >> 3, j = lane & 7;
                 const int tok_in = j + 8 * (k >> 1);         // token offset within a 16-column block
                 const int nrow = q * 32 + 8 * (k & 1);        // + 16h: first weight row of the 8x8 matrix
-#pragma unroll 1
-                for (int cb = 0; cb < BN / 16; ++cb) {
-                    uint32_t v[2][8];
-                    tmem_ld_16x256b_x2(tmem + lane_addr + ACC_COL + cb * 16, v[0]);
-                    tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + ACC_COL + cb * 16, v[1]);
-                    tmem_ld_wait();
-                    if (cb == BN / 16 - 1) {  // accumulator fully read: the next tile's MMAs may start
-                        tc_fence_before();
-                        mbar_arrive(sm.accempty);
-                    }
+                auto stage_block = [&](int cb, const uint32_t (&v)[2][8]) {
                     const int tok = cb * 16 + tok_in;
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
@@ -364,6 +355,23 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                         const uint8_t *dst = sm.y0 + half * Y_HALF_BYTES + tok * 128 + ((chunk ^ (tok & 7)) << 4);
                         stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
                     }
+                };
+                // two 16-token column blocks per TMEM load wait: half the round trips
+                // on the path that holds the accumulator
+#pragma unroll 1
+                for (int cb = 0; cb < BN / 16; cb += 2) {
+                    uint32_t v0[2][8], v1[2][8];
+                    tmem_ld_16x256b_x2(tmem + lane_addr + ACC_COL + cb * 16, v0[0]);
+                    tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + ACC_COL + cb * 16, v0[1]);
+                    tmem_ld_16x256b_x2(tmem + lane_addr + ACC_COL + (cb + 1) * 16, v1[0]);
+                    tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + ACC_COL + (cb + 1) * 16, v1[1]);
+                    tmem_ld_wait();
+                    if (cb + 2 == BN / 16) {  // accumulator fully read: the next tile's MMAs may start
+                        tc_fence_before();
+                        mbar_arrive(sm.accempty);
+                    }
+                    stage_block(cb, v0);
+                    stage_block(cb + 1, v1);
                 }
                 fence_proxy_async_smem();
                 named_bar_sync(1, 128);

@@ -51,8 +51,30 @@ constexpr int X_BYTES = BN * BK * 2;
 
 // ------------------------------------------------------------- tile table --
 
-struct Tile {
+struct __align__(16) Tile {
     int e, m, t0, t_end;
+};
+
+// A CTA's tiles (first, first + stride, ...), read in increasing order by every
+// warp role; each record is fetched one tile ahead, so a role's first use of a
+// tile never waits on the table load (and the absmax address computed from it
+// is ready one step later, as the dequant warps' prefetch expects).
+struct TileCursor {
+    const Tile *tiles;
+    int first, stride, n, tl;
+    Tile cur, next;
+    __device__ __forceinline__ TileCursor(const Tile *t, int f, int s, int count)
+        : tiles(t), first(f), stride(s), n(count), tl(-1), cur{0, 0, 0, 0}, next{0, 0, 0, 0} {
+        if (count > 0) next = tiles[f];
+    }
+    __device__ __forceinline__ Tile at(int want) {
+        if (want != tl) {
+            cur = want == tl + 1 ? next : tiles[first + want * stride];
+            tl = want;
+            if (want + 1 < n) next = tiles[first + (want + 1) * stride];
+        }
+        return cur;
+    }
 };
 
 // offsets[E+1] (device) -> tiles[]; order: expert, token tile, then weight-row
@@ -235,7 +257,8 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    auto tile_at = [&](int tl) { return p.tiles[int(blockIdx.x) + tl * int(gridDim.x)]; };
+    TileCursor cursor(p.tiles, int(blockIdx.x), int(gridDim.x), my_tiles);
+    auto tile_at = [&](int tl) { return cursor.at(tl); };
     // first global weight row of the tile's rows r < 64 (and, in SWIGLU mode, r >= 64)
     auto row_lo = [&](const Tile &t) { return t.e * p.N_e + (SWIGLU ? t.m * 64 : t.m * BM); };
     auto row_hi = [&](const Tile &t) { return t.e * p.N_e + (SWIGLU ? half_rows + t.m * 64 : t.m * BM + 64); };
@@ -378,16 +401,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
             const int kq = lane >> 3, jr = lane & 7;
             const int tok_in = jr + 8 * (kq >> 1);
             const int nrow = q * 32 + 8 * (kq & 1);
-#pragma unroll 1
-            for (int cb = 0; cb < nb; ++cb) {
-                uint32_t v[2][8];
-                tmem_ld_16x256b_x2(tmem + lane_addr + cb * 16, v[0]);
-                tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + cb * 16, v[1]);
-                tmem_ld_wait();
-                if (cb == nb - 1) {
-                    tc_fence_before();
-                    mbar_arrive(accempty);
-                }
+            auto stage_block = [&](int cb, const uint32_t (&v)[2][8]) {
                 float s0 = 1.f, s1 = 1.f, s2 = 1.f, s3 = 1.f;  // routing weights of this thread's 4 tokens
                 if (!SWIGLU && p.rw) {
                     const int tk = cb * 16 + 2 * (lane & 3);
@@ -412,6 +426,26 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                     const uint8_t *dst = y0 + half * (F_STAGE_BYTES / 2) + tok * 128 + ((chunk ^ (tok & 7)) << 4);
                     stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
                 }
+            };
+            // two 16-token column blocks per TMEM load wait: half the round trips on
+            // the path that holds the accumulator
+#pragma unroll 1
+            for (int cb = 0; cb < nb; cb += 2) {
+                const bool pair = cb + 1 < nb;  // warp-uniform
+                uint32_t v0[2][8], v1[2][8];
+                tmem_ld_16x256b_x2(tmem + lane_addr + cb * 16, v0[0]);
+                tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + cb * 16, v0[1]);
+                if (pair) {
+                    tmem_ld_16x256b_x2(tmem + lane_addr + (cb + 1) * 16, v1[0]);
+                    tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + (cb + 1) * 16, v1[1]);
+                }
+                tmem_ld_wait();
+                if (cb + 2 >= nb) {
+                    tc_fence_before();
+                    mbar_arrive(accempty);
+                }
+                stage_block(cb, v0);
+                if (pair) stage_block(cb + 1, v1);
             }
             named_bar_sync(1, 128);
             if constexpr (SWIGLU) {
@@ -521,7 +555,8 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    auto tile_at = [&](int tl) { return p.tiles[int(blockIdx.x) + tl * int(gridDim.x)]; };
+    TileCursor cursor(p.tiles, int(blockIdx.x), int(gridDim.x), my_tiles);
+    auto tile_at = [&](int tl) { return cursor.at(tl); };
 
     if (warp == 0) {
         if (lane == 0) {
