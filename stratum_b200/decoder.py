@@ -300,49 +300,77 @@ class WrappedLayer(nn.Module):
 class _LMHeadCE(torch.autograd.Function):
     """Mean next-token cross entropy of ``h . W_lm^T`` with the gradient formed in
     the forward: the NF4 GEMM writes bf16 logits, one kernel turns each row into
-    its loss and (softmax - onehot) in place, and the backward is one fused NF4
-    input-gradient GEMM over those rows.  The 1/N mean is applied as a tensor, so
-    nothing waits on the host."""
+    its loss and (softmax - onehot) in place, and one fused NF4 input-gradient
+    GEMM takes those rows to dh.  The 1/N mean is applied as a tensor, so nothing
+    waits on the host.
+
+    ``chunk`` rows at a time (0: all rows in one pass): a chunk's logits are
+    freed as soon as its dh rows are formed, so at most ``chunk x vocab`` 16-bit
+    logits are live, and what the backward keeps is dh ([rows, H]).  Every row
+    is computed independently, so the loss and dh do not depend on ``chunk``.
+    Unchunked, the logits themselves are kept and dh is formed in the backward."""
 
     @staticmethod
-    def forward(ctx, h, labels, lm_head):
+    def forward(ctx, h, labels, lm_head, chunk):
         from . import _lib, ops
 
         qs = lm_head.quant_state
-        logits = ops.nf4_gemm_fwd(h, lm_head.quantized, qs)
-        rows, vocab = logits.shape
-        loss_rows = torch.empty(rows, dtype=torch.float32, device=h.device)
+        rows = h.shape[0]
         lab = labels.to(torch.int64).contiguous()
-        with torch.cuda.device(h.device):
-            _lib.check(_lib.lib().stratum_ce_fwd_grad(_lib.ptr(logits), _lib.DTYPE_CODE[logits.dtype], _lib.ptr(lab),
-                                                      rows, vocab, -100, 1.0, _lib.ptr(loss_rows),
-                                                      _lib.stream_of(h.device)), "ce_fwd_grad")
+        loss_rows = torch.empty(rows, dtype=torch.float32, device=h.device)
         n = (lab != -100).sum().clamp_min(1).to(torch.float32)
-        ctx.save_for_backward(logits, n)
+        chunk = rows if chunk <= 0 else min(chunk, rows)
+        need_grad = ctx.needs_input_grad[0]
+        dh = torch.empty_like(h) if (need_grad and chunk < rows) else None
+        logits = None
+        for r0 in range(0, rows, chunk):
+            r1 = min(r0 + chunk, rows)
+            logits = ops.nf4_gemm_fwd(h[r0:r1], lm_head.quantized, qs)
+            vocab = logits.shape[1]
+            with torch.cuda.device(h.device):
+                _lib.check(_lib.lib().stratum_ce_fwd_grad(_lib.ptr(logits), _lib.DTYPE_CODE[logits.dtype],
+                                                          _lib.ptr(lab[r0:r1]), r1 - r0, vocab, -100, 1.0,
+                                                          _lib.ptr(loss_rows[r0:r1]), _lib.stream_of(h.device)),
+                           "ce_fwd_grad")
+            if dh is not None:
+                ops.nf4_gemm_dx(logits, lm_head.quantized, qs, out=dh[r0:r1])
+                logits = None
         ctx.lm_head = lm_head
+        if dh is not None:
+            ctx.save_for_backward(dh, n)
+            ctx.formed = True
+        else:
+            ctx.save_for_backward(logits if need_grad else None, n)
+            ctx.formed = False
         return loss_rows.sum() / n
 
     @staticmethod
     def backward(ctx, g):
         from . import ops
 
-        dlogits, n = ctx.saved_tensors
-        m = ctx.lm_head
-        dh = ops.nf4_gemm_dx(dlogits, m.quantized, m.quant_state)
-        return dh * (g / n).to(dh.dtype), None, None
+        saved, n = ctx.saved_tensors
+        if ctx.formed:
+            dh = saved
+        else:
+            m = ctx.lm_head
+            dh = ops.nf4_gemm_dx(saved, m.quantized, m.quant_state)
+        return dh * (g / n).to(dh.dtype), None, None, None
 
 
 class Postfix(nn.Module):
     """Final norm + lm_head + next-token cross entropy (stratum/model/llama.py:334-399).
 
     The lm_head is a frozen NF4Linear.  The reference chunks the loss over tokens
-    and recomputes each chunk's logits in the backward; here the bf16 logits of
-    the microbatch are formed once and overwritten with their own gradient by
-    the cross-entropy kernel, so the backward is a single NF4 input-gradient GEMM
-    (the 16-bit [tokens, vocab] buffer lives until the backward).  Returns the
-    mean loss over non-ignored tokens."""
+    and recomputes each chunk's logits in the backward
+    (stratum/model/chunked_loss.py:66-192); here each chunk's bf16 logits are
+    formed once, overwritten with their own gradient by the cross-entropy kernel
+    and taken to dh by one NF4 input-gradient GEMM, with no recompute and no
+    dequantized lm_head.  ``token_chunk`` bounds the live logits to
+    ``token_chunk x vocab``; 0 (the default) forms a microbatch's logits in one
+    pass and keeps them until its backward, which fills the GPU best when that
+    memory is available.  Returns the mean loss over non-ignored tokens."""
 
-    def __init__(self, spec: DecoderSpec, device, *, seed: int = 0, token_chunk: int = 4096):
+    def __init__(self, spec: DecoderSpec, device, *, seed: int = 0, token_chunk: int = 0):
         super().__init__()
         _, _, norm_cls = _layer_classes(spec)
         dev = _device(device)
@@ -366,7 +394,7 @@ class Postfix(nn.Module):
     def loss(self, hidden: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         h = self.norm(hidden)[:, :-1, :].reshape(-1, self.spec.hidden)
         y = labels[:, 1:].reshape(-1)
-        return _LMHeadCE.apply(h, y, self.lm_head)
+        return _LMHeadCE.apply(h, y, self.lm_head, int(self.token_chunk))
 
     def forward(self, input_data):
         hidden, _, _, _, _, labels, _ = input_data

@@ -111,11 +111,13 @@ def nf4_gemm_dx(
     lora_B: Optional[torch.Tensor] = None,
     scaling: float = 1.0,
     dyb: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """dx = dy . W + scaling * (dy . lora_B) . lora_A with W in NF4 (fused kernel).
 
     ``dyb`` may be passed precomputed (= scaling * dy . lora_B, padded to a
-    multiple of 64 columns), e.g. when dA needs it too.
+    multiple of 64 columns), e.g. when dA needs it too.  ``out``: a contiguous,
+    16-byte aligned [rows, K] tensor of dy's dtype and device to write dx into.
     """
     _lib.require_cuda(dy, "nf4_gemm_dx")
     if dy.dtype not in (torch.bfloat16, torch.float16):
@@ -130,7 +132,14 @@ def nf4_gemm_dx(
     if not dy2.is_contiguous() or dy2.data_ptr() % 16:
         dy2 = dy2.contiguous()
     T = dy2.shape[0]
-    dx = torch.empty((T, K), dtype=dy.dtype, device=dev)
+    if out is None:
+        dx = torch.empty((T, K), dtype=dy.dtype, device=dev)
+    else:
+        if (out.dtype != dy.dtype or out.device != dev or out.numel() != T * K or not out.is_contiguous()
+                or out.data_ptr() % 16):
+            raise ValueError(f"nf4_gemm_dx: out must be a contiguous, 16-byte aligned {dy.dtype} tensor of "
+                             f"{T}x{K} elements on {dev}")
+        dx = out
     r = 0
     la = None
     if lora_A is not None:
@@ -149,7 +158,7 @@ def nf4_gemm_dx(
             ),
             "nf4_gemm_dx",
         )
-    return dx.reshape(*dy.shape[:-1], K)
+    return dx if out is not None else dx.reshape(*dy.shape[:-1], K)
 
 
 # --------------------------------------------------------------------------------

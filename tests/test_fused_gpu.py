@@ -143,3 +143,33 @@ def test_lm_head_cross_entropy_matches_torch():
     ref.backward()
     assert abs(float(loss.detach()) - float(ref.detach())) < 1e-2 * abs(float(ref.detach()))
     assert relative_error(gh.float(), hidden.grad.float()) < 1e-2
+
+
+def test_lm_head_chunked_equals_unchunked_and_bounds_logits_memory():
+    """token_chunk changes only how many logits are live: loss and dh are the same
+    bits (every row is computed alone), and 256-row chunks hold a fraction of the
+    full [rows, vocab] logits."""
+    spec = D.DecoderSpec("t", "llama", 1, 256, 512, 4, 2, 64, 32000, 5e5)
+    post = D.Postfix(spec, DEV, seed=2)
+    g0 = torch.Generator(device=DEV).manual_seed(5)
+    hidden = torch.randn(1, 2048, 256, generator=g0, device=DEV).to(torch.bfloat16).requires_grad_()
+    labels = torch.randint(0, 32000, (1, 2048), generator=g0, device=DEV)
+    labels[0, 100:400] = -100
+    out = {}
+    for chunk in (0, 256, 700):
+        post.token_chunk = chunk
+        hidden.grad = None
+        torch.cuda.synchronize()
+        base = torch.cuda.memory_allocated()
+        torch.cuda.reset_peak_memory_stats()
+        loss = post.loss(hidden, labels)
+        torch.cuda.synchronize()
+        peak = torch.cuda.max_memory_allocated() - base
+        loss.backward()
+        out[chunk] = (loss.detach().clone(), hidden.grad.clone(), peak)
+    for chunk in (256, 700):
+        assert torch.equal(out[chunk][0], out[0][0]), chunk
+        assert torch.equal(out[chunk][1], out[0][1]), chunk
+    logits_bytes = 2047 * 32000 * 2
+    assert out[0][2] >= logits_bytes
+    assert out[256][2] < logits_bytes // 4
