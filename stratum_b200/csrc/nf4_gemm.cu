@@ -43,9 +43,9 @@ using namespace sm100;
 constexpr int BM = 128;       // weight rows per tile (TMEM lanes, MMA M)
 constexpr int BN = 256;       // tokens per tile (MMA N)
 constexpr int BK = 64;        // K per step: one NF4 block per weight row
-constexpr int XS = 4;         // ring of token tiles (32 KiB each), released by MMA completion
+constexpr int XS = 4;         // stages: token tile (32 KiB) + dequantized weight tile (TMEM), released by MMA completion
 constexpr int WS = 6;         // ring of packed weight tiles (4 KiB each), released by the dequant warps
-constexpr int AS = 8;         // TMEM ring of dequantized weight tiles (32 columns each)
+constexpr int AS = XS;        // TMEM weight tiles (32 columns each), one per stage
 constexpr int DQG = 3;        // dequant warpgroups; group g owns the steps with it % DQG == g
 constexpr int X_BYTES = BN * BK * 2;  // 32 KiB
 constexpr int W_BYTES = BM * BK / 2;  // 4 KiB
@@ -83,7 +83,9 @@ struct Smem {
     uint8_t *x0;    // token tile i at x0 + i * X_BYTES (1024-byte aligned)
     uint8_t *w0;    // packed weight tile i at w0 + i * W_BYTES
     uint8_t *y0;    // y staging: two halves of Y_HALF_BYTES (1024-byte aligned)
-    uint64_t *xfull, *xempty, *wfull, *wempty, *afull, *aempty, *accfull, *accempty, *drain;
+    // full[s]: stage s's token tile landed (TMA bytes) and its weight tile is in TMEM
+    // (128 dequant arrivals); empty[s]: the stage's MMAs completed (one commit)
+    uint64_t *full, *empty, *wfull, *wempty, *accfull, *accempty, *drain;
     uint32_t *tmem_slot;
     float *lv, *c2;
 };
@@ -99,12 +101,10 @@ __device__ __forceinline__ Smem carve(uint8_t *raw) {
     s.w0 = p;
     p += WS * W_BYTES;
     uint64_t *b = reinterpret_cast<uint64_t *>(p);
-    s.xfull = b; b += XS;
-    s.xempty = b; b += XS;
+    s.full = b; b += XS;
+    s.empty = b; b += XS;
     s.wfull = b; b += WS;
     s.wempty = b; b += WS;
-    s.afull = b; b += AS;
-    s.aempty = b; b += AS;
     s.accfull = b; b += 1;
     s.accempty = b; b += 1;
     s.drain = b; b += 1;
@@ -142,16 +142,12 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < XS; ++i) {
-            mbar_init(&sm.xfull[i], 1);
-            mbar_init(&sm.xempty[i], 1);
+            mbar_init(&sm.full[i], 1 + 128);  // the token producer's expect-tx + the owning dequant warpgroup
+            mbar_init(&sm.empty[i], 1);
         }
         for (int i = 0; i < WS; ++i) {
             mbar_init(&sm.wfull[i], 1);
             mbar_init(&sm.wempty[i], 128);  // the dequant warpgroup that owns the step
-        }
-        for (int i = 0; i < AS; ++i) {
-            mbar_init(&sm.afull[i], 128);
-            mbar_init(&sm.aempty[i], 1);
         }
         mbar_init(sm.accfull, 1);
         mbar_init(sm.accempty, 128);
@@ -179,17 +175,17 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const int t0 = ((int(blockIdx.x) + tl * int(gridDim.x)) / p.n_tiles) * BN;
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % XS;
-                    if (!mbar_wait(&sm.xempty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                    if (!mbar_wait(&sm.empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&sm.xfull[s], X_BYTES);
-                    if (ks < nkw) tma_load_2d(sm.x0 + s * X_BYTES, &tm_x, ks * BK, t0, &sm.xfull[s]);
-                    else tma_load_2d(sm.x0 + s * X_BYTES, &tm_xa, (ks - nkw) * BK, t0, &sm.xfull[s]);
+                    mbar_arrive_expect_tx(&sm.full[s], X_BYTES);
+                    if (ks < nkw) tma_load_2d(sm.x0 + s * X_BYTES, &tm_x, ks * BK, t0, &sm.full[s]);
+                    else tma_load_2d(sm.x0 + s * X_BYTES, &tm_xa, (ks - nkw) * BK, t0, &sm.full[s]);
                 }
             }
             for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)  // every copy lands before exit
-                mbar_wait(&sm.xfull[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait(&sm.full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         // ---------------------------------- producer: packed weight tiles
@@ -222,21 +218,20 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 if (!mbar_wait(sm.accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
+                    // one wait and one commit per stage: each costs the issuing thread
+                    // ~100 cycles that the tensor pipe spends idle
                     const int s = it % XS;
-                    const int sa = it % AS;
-                    if (!mbar_wait(&sm.afull[sa], (it / AS) & 1, p.status, kErrTimeoutMma) ||
-                        !mbar_wait(&sm.xfull[s], (it / XS) & 1, p.status, kErrTimeoutMma)) {
+                    if (!mbar_wait(&sm.full[s], (it / XS) & 1, p.status, kErrTimeoutMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint64_t bdesc = smem_desc_k_sw128(sm.x0 + s * X_BYTES);
-                    const uint32_t a0 = tmem + A_COL0 + sa * 32;
+                    const uint32_t a0 = tmem + A_COL0 + s * 32;
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j)
                         mma_ts_f16(tmem + ACC_COL, a0 + j * 8, bdesc + uint64_t(j * 2), idesc, (ks | j) != 0);
-                    mma_commit(&sm.xempty[s]);
-                    mma_commit(&sm.aempty[sa]);
+                    mma_commit(&sm.empty[s]);
                 }
                 if (ok) mma_commit(sm.accfull);
             }
@@ -300,13 +295,13 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 }
             }
             const int sa = it % AS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&sm.aempty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.empty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
                 break;
             tc_fence_after();
             tmem_st_32x32b_x32(tmem + lane_addr + A_COL0 + sa * 32, vals);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&sm.afull[sa]);
+            mbar_arrive(&sm.full[sa]);
         }
     } else if (warp >= EPI_WARP0) {
         // --------------------------------------------------------- epilogue
@@ -430,9 +425,9 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 namespace dx {
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int XS = 3;               // dY tiles (32 KiB)
+constexpr int XS = 3;               // stages: dY tile (32 KiB) + dequantized W^T tile (16 KiB)
 constexpr int WS = 4;               // packed weight tiles: 64 rows x 64 bytes (4 KiB)
-constexpr int AS = 3;               // dequantized W^T tiles in shared memory (16 KiB)
+constexpr int AS = XS;              // dequantized W^T tiles in shared memory, one per stage
 constexpr int DQG = 3;
 constexpr int X_BYTES = BN * BK * 2;
 constexpr int W_BYTES = BK * BM / 2;
@@ -472,8 +467,10 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
     uint8_t *y0 = a0 + AS * A_BYTES;                 // 2 x 32 KiB (1024-aligned)
     uint8_t *w0 = y0 + 2 * Y_HALF_BYTES;             // WS x 4 KiB
     uint64_t *bars = reinterpret_cast<uint64_t *>(w0 + WS * W_BYTES);
-    uint64_t *xfull = bars, *xempty = xfull + XS, *wfull = xempty + XS, *wempty = wfull + WS;
-    uint64_t *afull = wempty + WS, *aempty = afull + AS, *accfull = aempty + AS, *accempty = accfull + 2;
+    // full[s]: stage s's dY tile landed (TMA bytes) and its W^T tile is in shared memory
+    // (128 dequant arrivals); empty[s]: the stage's MMAs completed (one commit)
+    uint64_t *full = bars, *empty = full + XS, *wfull = empty + XS, *wempty = wfull + WS;
+    uint64_t *accfull = wempty + WS, *accempty = accfull + 2;
     uint64_t *drain = accempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     float *lv_s = reinterpret_cast<float *>(bars + 64);
@@ -487,9 +484,8 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
     const int my_tiles = ntiles > int(blockIdx.x) ? (ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < XS; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xempty[i], 1); }
+        for (int i = 0; i < XS; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
         for (int i = 0; i < WS; ++i) { mbar_init(&wfull[i], 1); mbar_init(&wempty[i], 128); }
-        for (int i = 0; i < AS; ++i) { mbar_init(&afull[i], 128); mbar_init(&aempty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&accfull[i], 1); mbar_init(&accempty[i], 128); }
         mbar_init(drain, 1);
         fence_barrier_init();
@@ -515,14 +511,14 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 const int t0 = ((int(blockIdx.x) + tl * int(gridDim.x)) / p.k_tiles) * BN;
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % XS;
-                    if (!mbar_wait(&xempty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&xfull[s], X_BYTES);
-                    if (ks < nkw) tma_load_2d(x0 + s * X_BYTES, &tm_dy, ks * BK, t0, &xfull[s]);
-                    else tma_load_2d(x0 + s * X_BYTES, &tm_dyb, (ks - nkw) * BK, t0, &xfull[s]);
+                    if (!mbar_wait(&empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], X_BYTES);
+                    if (ks < nkw) tma_load_2d(x0 + s * X_BYTES, &tm_dy, ks * BK, t0, &full[s]);
+                    else tma_load_2d(x0 + s * X_BYTES, &tm_dyb, (ks - nkw) * BK, t0, &full[s]);
                 }
             }
             for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
-                mbar_wait(&xfull[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         // ------------------------------- producer: packed weight tiles (64 x 128)
@@ -554,17 +550,15 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 tc_fence_after();
                 const uint32_t acc = tmem + uint32_t(ab * 256);
                 for (int ks = 0; ks < nk; ++ks, ++it) {
-                    const int s = it % XS, sa = it % AS;
-                    if (!mbar_wait(&afull[sa], (it / AS) & 1, p.status, kErrTimeoutMma) ||
-                        !mbar_wait(&xfull[s], (it / XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                    const int s = it % XS, sa = s;
+                    if (!mbar_wait(&full[s], (it / XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t bdesc = smem_desc_k_sw128(x0 + s * X_BYTES);
                     const uint64_t adesc = smem_desc_mn_sw128(a0 + sa * A_BYTES, A_ATOM, 1024);
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j)  // 16 K-rows = two 8-row groups = 2 KiB further
                         mma_ss_f16(acc, adesc + uint64_t(j * (2048 >> 4)), bdesc + uint64_t(j * 2), idesc, (ks | j) != 0);
-                    mma_commit(&xempty[s]);
-                    mma_commit(&aempty[sa]);
+                    mma_commit(&empty[s]);
                 }
                 if (ok) mma_commit(&accfull[ab]);
             }
@@ -636,7 +630,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 }
             }
             const int sa = it % AS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&aempty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant))) break;
             // MN-major atom kb, K-row rl: 8 chunks of 16 B, XOR-swizzled by rl % 8
             uint8_t *dst = a0 + sa * A_BYTES + kb * A_ATOM + (rl >> 3) * 1024 + (rl & 7) * 128;
 #pragma unroll
@@ -644,7 +638,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 *reinterpret_cast<uint4 *>(dst + ((c ^ (rl & 7)) << 4)) =
                     make_uint4(vals[4 * c], vals[4 * c + 1], vals[4 * c + 2], vals[4 * c + 3]);
             fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
-            mbar_arrive(&afull[sa]);
+            mbar_arrive(&full[sa]);
         }
     } else if (warp >= EPI_WARP0) {
         // --------------------------------------------------------- epilogue

@@ -194,12 +194,15 @@ constexpr int F_TMAX = 320;
 constexpr int F_XBOX = 64;
 constexpr int F_XBOX_BYTES = F_XBOX * BK * 2;
 constexpr int F_X_BYTES = F_TMAX * BK * 2;
-constexpr int F_XS = 3, F_WS = 6, F_AS = (512 - F_TMAX) / 32;
+// stages: a token tile (40 KiB) and its dequantized weight tile (TMEM) share one
+// full/empty barrier pair, so the MMA issuer waits and commits once per K step
+constexpr int F_XS = 3, F_WS = 6, F_AS = F_XS;
 constexpr int F_W_BYTES = BM * BK / 2;
 constexpr int F_STAGE_BYTES = F_TMAX * BM * 2;  // [320 tokens][128 rows] 16-bit, 2 swizzled halves
 constexpr int F_SMEM = 1024 + F_XS * F_X_BYTES + F_STAGE_BYTES + F_WS * F_W_BYTES + 512 + 1088;
 static_assert(F_SMEM <= 232448, "smem");
-static_assert(F_TMAX % F_XBOX == 0 && F_TMAX > BN && F_TMAX - BN <= BN && F_AS >= 4, "forward tile shape");
+static_assert(F_TMAX % F_XBOX == 0 && F_TMAX > BN && F_TMAX - BN <= BN && F_TMAX + 32 * F_AS <= 512,
+              "forward tile shape");
 
 struct FwdParams {
     const Tile *tiles;
@@ -228,8 +231,10 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     uint8_t *y0 = x0 + F_XS * F_X_BYTES;
     uint8_t *w0 = y0 + F_STAGE_BYTES;
     uint64_t *bars = reinterpret_cast<uint64_t *>(w0 + F_WS * F_W_BYTES);
-    uint64_t *xfull = bars, *xempty = xfull + F_XS, *wfull = xempty + F_XS, *wempty = wfull + F_WS;
-    uint64_t *afull = wempty + F_WS, *aempty = afull + F_AS, *accfull = aempty + F_AS, *accempty = accfull + 1;
+    // full[s]: stage s's token boxes landed (TMA bytes) and its weight tile is in TMEM
+    // (128 dequant arrivals); empty[s]: the stage's MMAs completed (one commit)
+    uint64_t *full = bars, *empty = full + F_XS, *wfull = empty + F_XS, *wempty = wfull + F_WS;
+    uint64_t *accfull = wempty + F_WS, *accempty = accfull + 1;
     uint64_t *drain = accempty + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     float *lv_s = reinterpret_cast<float *>(bars + 64);
@@ -242,9 +247,8 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     const int half_rows = p.N_e / 2;  // SWIGLU: I
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < F_XS; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xempty[i], 1); }
+        for (int i = 0; i < F_XS; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
         for (int i = 0; i < F_WS; ++i) { mbar_init(&wfull[i], 1); mbar_init(&wempty[i], 128); }
-        for (int i = 0; i < F_AS; ++i) { mbar_init(&afull[i], 128); mbar_init(&aempty[i], 1); }
         mbar_init(accfull, 1);
         mbar_init(accempty, 128);
         mbar_init(drain, 1);
@@ -273,15 +277,15 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 const int nbox = (tile_mma_n(t) + F_XBOX - 1) / F_XBOX;  // 64-token boxes the MMAs read
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % F_XS;
-                    if (!mbar_wait(&xempty[s], ((it / F_XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&xfull[s], uint32_t(nbox * F_XBOX_BYTES));
+                    if (!mbar_wait(&empty[s], ((it / F_XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], uint32_t(nbox * F_XBOX_BYTES));
                     for (int bx = 0; bx < nbox; ++bx)
                         tma_load_2d(x0 + s * F_X_BYTES + bx * F_XBOX_BYTES, &tm_x, ks * BK, t.t0 + bx * F_XBOX,
-                                    &xfull[s]);
+                                    &full[s]);
                 }
             }
             for (uint32_t j = (it > F_XS ? it - F_XS : 0); j < it; ++j)
-                mbar_wait(&xfull[j % F_XS], (j / F_XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait(&full[j % F_XS], (j / F_XS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         if (lane == 0) {
@@ -315,9 +319,8 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 if (!mbar_wait(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
-                    const int s = it % F_XS, sa = it % F_AS;
-                    if (!mbar_wait(&afull[sa], (it / F_AS) & 1, p.status, kErrTimeoutMma) ||
-                        !mbar_wait(&xfull[s], (it / F_XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                    const int s = it % F_XS, sa = s;
+                    if (!mbar_wait(&full[s], (it / F_XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t bdesc0 = smem_desc_k_sw128(x0 + s * F_X_BYTES);
                     const uint64_t bdesc1 = smem_desc_k_sw128(x0 + s * F_X_BYTES + BN * BK * 2);
@@ -327,8 +330,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                         mma_ts_f16(tmem, a0 + j * 8, bdesc0 + uint64_t(j * 2), idesc0, (ks | j) != 0);
                         if (n1) mma_ts_f16(tmem + BN, a0 + j * 8, bdesc1 + uint64_t(j * 2), idesc1, (ks | j) != 0);
                     }
-                    mma_commit(&xempty[s]);
-                    mma_commit(&aempty[sa]);
+                    mma_commit(&empty[s]);
                 }
                 if (ok) mma_commit(accfull);
             }
@@ -374,13 +376,13 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
             fence_proxy_async_smem();  // generic reads before the stage's TMA refill
             mbar_arrive(&wempty[s]);
             const int sa = it % F_AS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&aempty[sa], ((it / F_AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / F_AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
                 break;
             tc_fence_after();
             tmem_st_32x32b_x32(tmem + lane_addr + F_TMAX + sa * 32, vals);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&afull[sa]);
+            mbar_arrive(&full[sa]);
         }
     } else if (warp >= EPI_WARP0) {  // warp 3 is idle: it must not join the epilogue's barriers
         // --------------------------------------------------------- epilogue
@@ -495,7 +497,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
 
 // -------------------------------------------------------- input gradient --
 
-constexpr int D_XS = 3, D_WS = 4, D_AS = 3;
+constexpr int D_XS = 3, D_WS = 4, D_AS = D_XS;  // stages: dY tile + W^T tile, one barrier pair
 constexpr int D_W_BYTES = BK * BM / 2;
 constexpr int D_A_BYTES = BM * BK * 2;
 constexpr int D_A_ATOM = BK * 128;
@@ -528,8 +530,10 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
     uint8_t *y0 = a0 + D_AS * D_A_BYTES;
     uint8_t *w0 = y0 + D_STAGE_BYTES;
     uint64_t *bars = reinterpret_cast<uint64_t *>(w0 + D_WS * D_W_BYTES);
-    uint64_t *xfull = bars, *xempty = xfull + D_XS, *wfull = xempty + D_XS, *wempty = wfull + D_WS;
-    uint64_t *afull = wempty + D_WS, *aempty = afull + D_AS, *accfull = aempty + D_AS, *accempty = accfull + 2;
+    // full[s]: stage s's dY tile landed and its W^T tile is in shared memory (TMA bytes +
+    // 128 dequant arrivals); empty[s]: the stage's MMAs completed (one commit)
+    uint64_t *full = bars, *empty = full + D_XS, *wfull = empty + D_XS, *wempty = wfull + D_WS;
+    uint64_t *accfull = wempty + D_WS, *accempty = accfull + 2;
     uint64_t *drain = accempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     float *lv_s = reinterpret_cast<float *>(bars + 64);
@@ -541,9 +545,8 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
     const int my_tiles = ntiles > int(blockIdx.x) ? (ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < D_XS; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xempty[i], 1); }
+        for (int i = 0; i < D_XS; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
         for (int i = 0; i < D_WS; ++i) { mbar_init(&wfull[i], 1); mbar_init(&wempty[i], 128); }
-        for (int i = 0; i < D_AS; ++i) { mbar_init(&afull[i], 128); mbar_init(&aempty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&accfull[i], 1); mbar_init(&accempty[i], 128); }
         mbar_init(drain, 1);
         fence_barrier_init();
@@ -567,13 +570,13 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                 const Tile t = tile_at(tl);
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % D_XS;
-                    if (!mbar_wait(&xempty[s], ((it / D_XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&xfull[s], X_BYTES);
-                    tma_load_2d(x0 + s * X_BYTES, &tm_dy, ks * BK, t.t0, &xfull[s]);
+                    if (!mbar_wait(&empty[s], ((it / D_XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], X_BYTES);
+                    tma_load_2d(x0 + s * X_BYTES, &tm_dy, ks * BK, t.t0, &full[s]);
                 }
             }
             for (uint32_t j = (it > D_XS ? it - D_XS : 0); j < it; ++j)
-                mbar_wait(&xfull[j % D_XS], (j / D_XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait(&full[j % D_XS], (j / D_XS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         if (lane == 0) {
@@ -603,17 +606,15 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                 tc_fence_after();
                 const uint32_t acc = tmem + uint32_t(ab * 256);
                 for (int ks = 0; ks < nk; ++ks, ++it) {
-                    const int s = it % D_XS, sa = it % D_AS;
-                    if (!mbar_wait(&afull[sa], (it / D_AS) & 1, p.status, kErrTimeoutMma) ||
-                        !mbar_wait(&xfull[s], (it / D_XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                    const int s = it % D_XS, sa = s;
+                    if (!mbar_wait(&full[s], (it / D_XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t bdesc = smem_desc_k_sw128(x0 + s * X_BYTES);
                     const uint64_t adesc = smem_desc_mn_sw128(a0 + sa * D_A_BYTES, D_A_ATOM, 1024);
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j)
                         mma_ss_f16(acc, adesc + uint64_t(j * (2048 >> 4)), bdesc + uint64_t(j * 2), idesc, (ks | j) != 0);
-                    mma_commit(&xempty[s]);
-                    mma_commit(&aempty[sa]);
+                    mma_commit(&empty[s]);
                 }
                 if (ok) mma_commit(&accfull[ab]);
             }
@@ -658,7 +659,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
             fence_proxy_async_smem();
             mbar_arrive(&wempty[s]);
             const int sa = it % D_AS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&aempty[sa], ((it / D_AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / D_AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
                 break;
             uint8_t *dst = a0 + sa * D_A_BYTES + kb * D_A_ATOM + (rl >> 3) * 1024 + (rl & 7) * 128;
 #pragma unroll
@@ -666,7 +667,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                 *reinterpret_cast<uint4 *>(dst + ((c ^ (rl & 7)) << 4)) =
                     make_uint4(vals[4 * c], vals[4 * c + 1], vals[4 * c + 2], vals[4 * c + 3]);
             fence_proxy_async_smem();
-            mbar_arrive(&afull[sa]);
+            mbar_arrive(&full[sa]);
         }
     } else if (warp >= EPI_WARP0) {  // warp 3 is idle
         const int q = warp & 3;
