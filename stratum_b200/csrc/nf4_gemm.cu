@@ -52,7 +52,7 @@ constexpr int W_BYTES = BM * BK / 2;  // 4 KiB
 constexpr int Y_HALF_BYTES = BN * 64 * 2;  // staging of y: two [256 tokens][64 rows] halves, 128B-swizzled
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;    // accumulator: columns [0, 256)
-constexpr int A_COL0 = 256;   // A ring: columns [256, 512)
+constexpr int A_COL0 = 256;   // A ring: columns [256, 256 + 32 * AS)
 constexpr int EPI_WARP0 = 4 + 4 * DQG;
 constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_BYTES + WS * W_BYTES + 2 * Y_HALF_BYTES +
