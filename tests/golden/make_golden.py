@@ -1,6 +1,6 @@
 """Generate the golden NF4 fixtures in this directory (run here, where the reference is mounted).
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 The reference's own ``stratum.upload.prepare_nf4`` (stratum/upload.py:305-398)
 is imported and run on small seeded modules, with ``bitsandbytes.functional``
@@ -88,7 +88,10 @@ def build_modules():
     return m
 
 
-def main(ref_root: str = "/root/reference") -> None:
+def main(ref_root: str) -> None:
+    """``ref_root``: the checkout of the reference project (the directory that holds ``stratum/``)."""
+    if not (Path(ref_root) / "stratum" / "upload.py").is_file():
+        raise SystemExit(f"{ref_root}: not a checkout of the reference (no stratum/upload.py)")
     sys.path.insert(0, ref_root)
     pkg, functional = _fake_bnb()
     sys.modules["bitsandbytes"] = pkg
@@ -118,4 +121,6 @@ def main(ref_root: str = "/root/reference") -> None:
 
 
 if __name__ == "__main__":
-    main(*sys.argv[1:])
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py /path/to/reference")
+    main(sys.argv[1])
