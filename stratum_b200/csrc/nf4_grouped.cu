@@ -187,9 +187,9 @@ __device__ __forceinline__ uint4 pack8(const float f[8]) {
 // ------------------------------------------------------------- forward --
 
 // Token tiles of up to F_TMAX tokens: accumulator columns [0, F_TMAX) (an N <= 256
-// MMA into [0, 256) plus an N <= 64 one into [256, 320)), the dequantized A ring
-// in the remaining TMEM columns [F_TMAX, 512).  x arrives in 64-token boxes, only
-// as many as the tile's MMA width needs.
+// MMA into [0, 256) plus an N <= 64 one into [256, 320)), the dequantized A tiles
+// from TMEM column F_TMAX on (32 columns per stage).  x arrives in 64-token boxes,
+// only as many as the tile's MMA width needs.
 constexpr int F_TMAX = 320;
 constexpr int F_XBOX = 64;
 constexpr int F_XBOX_BYTES = F_XBOX * BK * 2;
