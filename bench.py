@@ -751,9 +751,11 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
     # 1F1B keeps at most world - rank microbatches in flight, so every layer's graph is kept (no
     # recompute); the router aux loss's per-microbatch sums ride on the boundary messages
     schedule, recompute = "1f1b", False
+    # one GPU with resident weights and no router aux loss: microbatches replay a CUDA graph
+    graphed = world == 1 and not stream and not (spec.experts and spec.router_aux_coef)
     pipe = RankPipeline(DeviceStage(layers, local), prefix=prefix, postfix=postfix, rank=rank, world=world,
                         hidden_size=spec.hidden, router_sink=sink, router_aux_coef=spec.router_aux_coef,
-                        n_experts=spec.experts, schedule=schedule, recompute=recompute)
+                        n_experts=spec.experts, schedule=schedule, recompute=recompute, cuda_graph=graphed)
     g = torch.Generator(device=dev).manual_seed(1234)
     ids = torch.randint(0, spec.vocab, (M, seq), generator=g, device=dev)
     ids_host = ids.cpu().pin_memory()
@@ -769,7 +771,7 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        n0 = _lib.launch_count()
+        n0, g0 = _lib.launch_count(), pipe.graph_launches
         e0.record()
         for _ in range(n):
             loss = step(mb, host)
@@ -777,12 +779,14 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
                 float(loss)  # the step's result read back to the host
         e1.record()
         torch.cuda.synchronize()
-        launches = _lib.launch_count() - n0
+        launches = _lib.launch_count() - n0 + pipe.graph_launches - g0
         barrier(world)
         return max_over_ranks(e0.elapsed_time(e1) / n, world), launches
 
     for _ in range(warmup):
         step(M)
+    if graphed:
+        step(1)  # the sequential schedule's graph, built outside its timing
     torch.cuda.synchronize()
     with ClockSampler(dev.index) as clocks:
         ms, launches = timed(M, steps)
@@ -807,13 +811,14 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
                     f"rank, last rank lighter by the postfix), {M} microbatches x [1, {seq}] tokens per step ({schedule}, "
                     f"{'per-layer recompute' if recompute else 'no recompute'}), NF4 bs64"
                     f"{' + double quant, streamed per step from pinned host' if stream else ' resident'}, "
-                    f"LoRA r={spec.lora_r}, NCCL send/recv boundaries",
+                    f"LoRA r={spec.lora_r}, NCCL send/recv boundaries"
+                    f"{'; microbatches replayed from a CUDA graph of one forward + backward' if graphed else ''}",
         "microbatches": M,
         "seq_len": seq,
         "sequential": {"what": "one sequence per step (the reference's sequential execution)",
                        "value": round(seq / (ms_seq * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms_seq, 3)},
         "e2e": {"value": round(tok / (ms_e2e * 1e-3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(ids_host[:M].numel() * 8 * (2 if world > 1 else 1)),
+                "h2d_bytes_per_step": int(ids_host[:M].numel() * 8 * 2),  # token ids and labels
                 "d2h_bytes_per_step": 4, "path": "RankPipeline.train_step with pinned host token ids, loss read back"},
         "roofline": {"bound": "tensor", "what": "algorithmic FLOPs of the step (fwd + dX + LoRA grads + attention "
                      "+ lm_head; recompute not counted) per second over all GPUs",

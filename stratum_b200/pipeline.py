@@ -432,12 +432,22 @@ class RankPipeline(nn.Module):
     each microbatch's global per-expert sums before its backward: GPipe
     all-reduces them after the forwards; 1F1B carries them on the boundary
     messages (partial sums forward, global sums back).
+
+    ``cuda_graph=True`` (one rank, weights resident on the device, no router aux
+    loss): one microbatch's forward and backward are captured once into a CUDA
+    graph -- together with adding its LoRA gradients and loss into static
+    accumulators -- and every microbatch is a replay of it, so a model whose
+    kernels are small no longer waits on the host's per-op dispatch.  The graph
+    is built once per (microbatch count, sequence length); gradients are added
+    into the parameters' ``.grad`` as the eager path does.  ``graph_launches``
+    counts the library kernels the replays ran (they bypass the host-side launch
+    counter).
     """
 
     def __init__(self, stage: DeviceStage, *, prefix: nn.Module, postfix: Optional[nn.Module], rank: int,
                  world: int, group=None, hidden_size: int, offload_stage_inputs: bool = False, router_sink=None,
                  router_aux_coef: float = 0.0, n_experts: int = 0, hidden_dtype=torch.bfloat16,
-                 schedule: str = "gpipe", recompute: bool = True):
+                 schedule: str = "gpipe", recompute: bool = True, cuda_graph: bool = False):
         super().__init__()
         if (postfix is None) != (rank + 1 < world):
             raise ValueError("RankPipeline: the postfix lives on the last rank only")
@@ -458,6 +468,16 @@ class RankPipeline(nn.Module):
         self.streamer = _Streamer(_stage_layers(stage), self.device,
                                   any(_needs_streaming(l, self.device) for l in stage.layers))
         self.last_aux: Optional[torch.Tensor] = None
+        self.cuda_graph = bool(cuda_graph)
+        if self.cuda_graph:
+            if world != 1:
+                raise ValueError("RankPipeline: cuda_graph needs a single rank (boundaries are NCCL calls)")
+            if self.streamer.enabled:
+                raise ValueError("RankPipeline: cuda_graph needs the stratum's weights resident on the device")
+            if router_sink is not None and self.router_aux_coef != 0.0 and self.n_experts > 0:
+                raise ValueError("RankPipeline: cuda_graph does not cover the router aux loss")
+        self._graphs: dict = {}
+        self.graph_launches = 0
 
     def _aux_reduce(self, states: list[_AuxState]) -> None:
         E = self.n_experts
@@ -605,9 +625,77 @@ class RankPipeline(nn.Module):
             self.last_aux = torch.stack(aux_values).mean()
         return losses
 
+    # ------------------------------------------------------------ CUDA graph
+
+    def _one_microbatch(self, ids, labs, M: int) -> torch.Tensor:
+        """Forward and backward of the microbatch in ``ids`` / ``labs`` ([1, 1, S]), loss scaled by 1/M."""
+        _, out, loss, _ = self._forward_mb(0, ids, labs, None, None, None, None)
+        self._backward_mb(out, loss, None, M)
+        return loss.detach()
+
+    def _graph_build(self, M: int, S: int):
+        from . import _lib
+
+        dev = self.device
+        trainable = [p for p in self.parameters() if p.requires_grad]
+        saved = [p.grad for p in trainable]
+        ids = torch.zeros((1, 1, S), dtype=torch.int64, device=dev)
+        labs = torch.zeros((1, 1, S), dtype=torch.int64, device=dev)
+        # warm-up off the capture (library handles, workspaces, kernel attributes), on a
+        # side stream as capture requires; its gradients are discarded
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                for p in trainable:
+                    p.grad = None
+                self._one_microbatch(ids, labs, M)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        params = [p for p in trainable if p.grad is not None]  # the ones this stratum's loss reaches
+        accs = [torch.zeros_like(p) for p in params]
+        loss_acc = torch.zeros((), dtype=torch.float32, device=dev)
+        for p in trainable:
+            p.grad = None  # the captured backward creates them in the graph's pool; every replay rewrites them
+        graph = torch.cuda.CUDAGraph()
+        n0 = _lib.launch_count()
+        with torch.cuda.graph(graph):
+            loss = self._one_microbatch(ids, labs, M)
+            loss_acc.add_(loss.float())
+            torch._foreach_add_(accs, [p.grad for p in params])
+        launches = _lib.launch_count() - n0
+        pool_grads = [p.grad for p in params]  # owned by the graph's pool: kept alive with the graph
+        for p, g in zip(trainable, saved):
+            p.grad = g
+        return graph, ids, labs, params, accs, loss_acc, pool_grads, launches
+
+    def _graph_train(self, ids, labs, M: int) -> torch.Tensor:
+        key = (M, int(ids.shape[-1]))
+        if key not in self._graphs:
+            self._graphs[key] = self._graph_build(*key)
+        graph, sids, slabs, params, accs, loss_acc, _, launches = self._graphs[key]
+        torch._foreach_zero_(accs)
+        loss_acc.zero_()
+        for m in range(M):
+            sids.copy_(ids[m:m + 1])
+            slabs.copy_(labs[m:m + 1])
+            graph.replay()
+        self.graph_launches += M * launches
+        for p, a in zip(params, accs):
+            if p.grad is None:
+                p.grad = a.clone()
+            else:
+                p.grad.add_(a)
+        return loss_acc / M
+
     def train_step(self, input_ids: Optional[torch.Tensor] = None, labels: Optional[torch.Tensor] = None, *,
                    microbatches: int = 1, seq_len: Optional[int] = None):
         M = int(microbatches)
+        if self.cuda_graph:
+            dev = self.device
+            with _on(dev):
+                ids = input_ids.reshape(M, 1, -1).to(dev, non_blocking=True)
+                labs = labels.reshape(M, 1, -1).to(dev, non_blocking=True)
+                return self._graph_train(ids, labs, M)
         first, last = self.rank == 0, self.rank + 1 == self.world
         dev = self.device
         if first:

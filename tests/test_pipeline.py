@@ -220,3 +220,17 @@ def test_stratum_pipeline_keeps_the_reference_hooks():
     pipe(ids, labels=labels).backward()
     assert 99 not in pipe._pending_bwd_fences
     assert pipe._param_upload_stream(0) is None
+
+
+def test_rank_pipeline_cuda_graph_is_refused_where_it_cannot_apply():
+    """CUDA-graph microbatches need one rank and no router aux loss (host-side checks only)."""
+    sink = RouterLogitsSink()
+    layers = _model(2, True, sink)
+    stage = DeviceStage(layers, "cpu")
+    with pytest.raises(ValueError, match="single rank"):
+        RankPipeline(stage, prefix=ToyPrefix(), postfix=None, rank=0, world=2, hidden_size=H,
+                     hidden_dtype=torch.float32, schedule="1f1b", recompute=False, cuda_graph=True)
+    with pytest.raises(ValueError, match="aux loss"):
+        RankPipeline(stage, prefix=ToyPrefix(), postfix=ToyPostfix(), rank=0, world=1, hidden_size=H,
+                     hidden_dtype=torch.float32, router_sink=sink, router_aux_coef=COEF, n_experts=E,
+                     schedule="1f1b", recompute=False, cuda_graph=True)

@@ -247,3 +247,40 @@ def test_stratum_pipeline_across_two_devices_matches_one_device():
     torch.cuda.synchronize(1)
     got = {k: v.to(DEV) for k, v in _lora_grads(l0 + l1).items()}
     _compare(loss2.detach().to(DEV), got, loss1.detach(), ref)
+
+
+def test_rank_pipeline_cuda_graph_matches_eager():
+    """One rank, resident weights: microbatches replayed from a captured CUDA graph give the
+    eager path's loss and LoRA gradients (twice, so the second step reuses the graph), and
+    a new microbatch count rebuilds it."""
+    spec = TINY_LLAMA
+    prefix, layers, postfix, _ = _build(spec)
+    ids, labels = _data(spec, m=3)
+
+    def run(graph, m=3, steps=1):
+        _zero(layers)
+        pipe = RankPipeline(DeviceStage(layers, 0), prefix=prefix, postfix=postfix, rank=0, world=1,
+                            hidden_size=spec.hidden, schedule="1f1b", recompute=False, cuda_graph=graph)
+        loss = None
+        for _ in range(steps):
+            _zero(layers)
+            loss = pipe.train_step(ids[:m], labels[:m], microbatches=m)
+        torch.cuda.synchronize()
+        return pipe, loss, _lora_grads(layers)
+
+    _, loss_e, grads_e = run(False)
+    pipe, loss_g, grads_g = run(True, steps=2)
+    _compare(loss_g, grads_g, loss_e, grads_e)
+    # a different microbatch count rebuilds the graph
+    _, loss_e2, grads_e2 = run(False, m=2)
+    _zero(layers)
+    loss_g2 = pipe.train_step(ids[:2], labels[:2], microbatches=2)
+    torch.cuda.synchronize()
+    _compare(loss_g2, _lora_grads(layers), loss_e2, grads_e2)
+    # gradients accumulate into existing .grad as the eager path's do
+    before = _lora_grads(layers)
+    pipe.train_step(ids[:2], labels[:2], microbatches=2)
+    torch.cuda.synchronize()
+    after = _lora_grads(layers)
+    for k in before:
+        assert relative_error(after[k].float(), 2 * before[k].float()) < TOL, k
