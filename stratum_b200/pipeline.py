@@ -439,9 +439,12 @@ class RankPipeline(nn.Module):
     accumulators -- and every microbatch is a replay of it, so a model whose
     kernels are small no longer waits on the host's per-op dispatch.  The graph
     is built once per (microbatch count, sequence length); gradients are added
-    into the parameters' ``.grad`` as the eager path does.  ``graph_launches``
-    counts the library kernels the replays ran (they bypass the host-side launch
-    counter).
+    into the parameters' ``.grad`` as the eager path does.  Replays read the
+    parameters and NF4 weights at the addresses they had when the graph was
+    captured: update parameters in place (as torch optimizers do), and keep the
+    stratum's weights resident (no ``free_weights`` / re-upload between steps).
+    ``graph_launches`` counts the library kernels the replays ran (they bypass
+    the host-side launch counter).
     """
 
     def __init__(self, stage: DeviceStage, *, prefix: nn.Module, postfix: Optional[nn.Module], rank: int,
