@@ -84,6 +84,24 @@ def _device_tensors(module: nn.Module) -> list[torch.Tensor]:
     return out
 
 
+def _address_signature(module: nn.Module) -> tuple:
+    """Data addresses of everything the module's forward reads from device memory:
+    parameters, buffers, NF4Linear payloads and uploaded NF4Experts weights -- the
+    addresses a captured CUDA graph has baked in."""
+    ptrs = [t.data_ptr() for t in module.parameters()] + [t.data_ptr() for t in module.buffers()]
+    ptrs += [t.data_ptr() for t in _device_tensors(module)]
+    for m in module.modules():
+        for w, qs in ((getattr(m, "gate_up", None), getattr(m, "gate_up_state", None)),
+                      (getattr(m, "down", None), getattr(m, "down_state", None))):
+            if qs is None or not torch.is_tensor(w):
+                continue
+            ptrs.append(w.data_ptr())
+            ptrs += [t.data_ptr() for t in (qs.absmax, qs.code, qs.offset) if torch.is_tensor(t)]
+            if qs.state2 is not None:
+                ptrs += [t.data_ptr() for t in (qs.state2.absmax, qs.state2.code) if torch.is_tensor(t)]
+    return tuple(ptrs)
+
+
 def _needs_streaming(module: nn.Module, device: torch.device) -> bool:
     return any(isinstance(m, NF4Linear) and m.streamed and not m.device_state_on(device) for m in module.modules())
 
@@ -441,8 +459,9 @@ class RankPipeline(nn.Module):
     is built once per (microbatch count, sequence length); gradients are added
     into the parameters' ``.grad`` as the eager path does.  Replays read the
     parameters and NF4 weights at the addresses they had when the graph was
-    captured: update parameters in place (as torch optimizers do), and keep the
-    stratum's weights resident (no ``free_weights`` / re-upload between steps).
+    captured; each step compares those addresses with the current ones and
+    captures again if any moved (a replaced ``param.data``, a re-upload), so
+    in-place updates (as torch optimizers make) keep the graph.
     ``graph_launches`` counts the library kernels the replays ran (they bypass
     the host-side launch counter).
     """
@@ -669,13 +688,15 @@ class RankPipeline(nn.Module):
         pool_grads = [p.grad for p in params]  # owned by the graph's pool: kept alive with the graph
         for p, g in zip(trainable, saved):
             p.grad = g
-        return graph, ids, labs, params, accs, loss_acc, pool_grads, launches
+        return graph, ids, labs, params, accs, loss_acc, pool_grads, launches, _address_signature(self)
 
     def _graph_train(self, ids, labs, M: int) -> torch.Tensor:
         key = (M, int(ids.shape[-1]))
+        if key in self._graphs and self._graphs[key][-1] != _address_signature(self):
+            self._graphs.clear()  # a parameter or weight moved: every graph reads stale addresses
         if key not in self._graphs:
             self._graphs[key] = self._graph_build(*key)
-        graph, sids, slabs, params, accs, loss_acc, _, launches = self._graphs[key]
+        graph, sids, slabs, params, accs, loss_acc, _, launches, _ = self._graphs[key]
         torch._foreach_zero_(accs)
         loss_acc.zero_()
         for m in range(M):

@@ -277,6 +277,15 @@ def test_rank_pipeline_cuda_graph_matches_eager():
     loss_g2 = pipe.train_step(ids[:2], labels[:2], microbatches=2)
     torch.cuda.synchronize()
     _compare(loss_g2, _lora_grads(layers), loss_e2, grads_e2)
+    # a parameter replaced (not updated in place) is seen: the graph is captured again
+    with torch.no_grad():
+        lb = next(p for n, p in layers[0].named_parameters() if n.endswith("lora_B"))
+        lb.data = lb.data * 1.5
+    _, loss_e3, grads_e3 = run(False, m=2)
+    _zero(layers)
+    loss_g3 = pipe.train_step(ids[:2], labels[:2], microbatches=2)
+    torch.cuda.synchronize()
+    _compare(loss_g3, _lora_grads(layers), loss_e3, grads_e3)
     # gradients accumulate into existing .grad as the eager path's do
     before = _lora_grads(layers)
     pipe.train_step(ids[:2], labels[:2], microbatches=2)
