@@ -234,3 +234,32 @@ def test_rank_pipeline_cuda_graph_is_refused_where_it_cannot_apply():
         RankPipeline(stage, prefix=ToyPrefix(), postfix=ToyPostfix(), rank=0, world=1, hidden_size=H,
                      hidden_dtype=torch.float32, router_sink=sink, router_aux_coef=COEF, n_experts=E,
                      schedule="1f1b", recompute=False, cuda_graph=True)
+
+
+def test_cuda_graph_address_signature_tracks_storage_not_values():
+    """What a captured graph has baked in: in-place updates keep the signature,
+    replaced storage (a new ``param.data``, a re-uploaded NF4 payload) changes it."""
+    from stratum_b200.pipeline import _address_signature
+
+    layers = _model(2, False, None)
+    model = nn.ModuleList(layers)
+    sig = _address_signature(model)
+    assert sig == _address_signature(model)
+    p = next(q for q in model.parameters() if q.requires_grad)
+    with torch.no_grad():
+        p.mul_(1.5)  # an optimizer step: same storage
+    assert _address_signature(model) == sig
+    p.data = p.data.clone()  # new storage
+    assert _address_signature(model) != sig
+
+    holder = nn.Module()  # uploaded NF4Experts-style weights are covered too
+
+    class _QS:
+        def __init__(self):
+            self.absmax, self.code, self.offset, self.state2 = torch.ones(4), torch.ones(16), None, None
+
+    holder.gate_up, holder.gate_up_state = torch.zeros(8, dtype=torch.uint8), _QS()
+    holder.down, holder.down_state = None, None
+    s1 = _address_signature(holder)
+    holder.gate_up = torch.zeros(8, dtype=torch.uint8)
+    assert _address_signature(holder) != s1
