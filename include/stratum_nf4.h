@@ -97,7 +97,8 @@ int stratum_nf4_quantize_absmax_dq(const float *absmax, int64_t nb, int blocksiz
  * stratum_nf4_quantize_absmax_dq.  Its scratch (the float32 absmax and the
  * mean's chunk sums) is one fixed array inside the library: at most 2^20
  * blocks (67,108,864 elements) per call, larger sizes return
- * STRATUM_ERR_INVALID; the array takes 4 MiB + 8 KiB on every GPU that loads
+ * STRATUM_ERR_INVALID; n == 0 returns STRATUM_OK and writes nothing (as
+ * stratum_nf4_quantize); the array takes 4 MiB + 8 KiB on every GPU that loads
  * the library until the process exits.  A device's first call looks the array
  * up, so make it before any stream capture.  All calls share the array:
  * calls that overlap on the GPU (other streams, other threads) race. */

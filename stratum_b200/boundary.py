@@ -123,23 +123,66 @@ class P2PChannel:
         self.rank, self.world, self.group = rank, world, group
         self.prev = rank - 1 if rank > 0 else None
         self.next = rank + 1 if rank + 1 < world else None
+        # send-only groups in flight: (works, tensors kept alive until the sends complete)
+        self._pending: list = []
+        # when a list: (start, end) CUDA event pairs around every wait of the caller's
+        # stream for received tensors (the time this rank's compute sat idle on a neighbour)
+        self.wait_events: Optional[list] = None
 
     def _peer(self, r: int) -> int:
         return dist.get_global_rank(self.group, r) if self.group is not None else r
 
+    def _retire(self) -> None:
+        self._pending = [(ws, ts) for ws, ts in self._pending if not all(w.is_completed() for w in ws)]
+
+    def flush(self) -> None:
+        """Order the caller's stream after every send still in flight and drop the
+        references that kept their tensors alive (end of a step)."""
+        for ws, _ in self._pending:
+            for w in ws:
+                w.wait()
+        self._pending.clear()
+
+    @property
+    def sends_in_flight(self) -> int:
+        return len(self._pending)
+
     def exchange(self, sends=(), recvs=()) -> list:
         """One NCCL group: ``sends`` = [(tensor, rank)], ``recvs`` = [(shape, dtype, device, rank)];
-        returns the received tensors in order."""
-        ops, out = [], []
+        returns the received tensors in order.
+
+        A group that receives is waited on by the caller's stream (NCCL completes a
+        group as a whole, so its sends are waited on with the receives they are paired
+        with -- in 1F1B those pairs mirror the neighbour's and finish together).  A
+        send-only group is not waited on: the caller's stream runs on while NCCL's
+        stream transfers, and the sent tensors stay referenced until the host sees the
+        group complete (or ``flush``), so the allocator cannot recycle them early."""
+        self._retire()
+        ops, out, held = [], [], []
         for t, r in sends:
-            ops.append(dist.P2POp(dist.isend, t.contiguous(), self._peer(r), self.group))
+            t = t.contiguous()
+            held.append(t)
+            ops.append(dist.P2POp(dist.isend, t, self._peer(r), self.group))
         for shape, dtype, device, r in recvs:
             buf = torch.empty(shape, dtype=dtype, device=device)
             out.append(buf)
             ops.append(dist.P2POp(dist.irecv, buf, self._peer(r), self.group))
-        if ops:
-            for req in dist.batch_isend_irecv(ops):
-                req.wait()
+        if not ops:
+            return out
+        works = dist.batch_isend_irecv(ops)
+        if not recvs:
+            self._pending.append((works, held))
+            return out
+        timed = self.wait_events is not None and out and out[0].is_cuda
+        if timed:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+        for w in works:
+            w.wait()
+        if timed:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            self.wait_events.append((e0, e1))
         return out
 
     def send_forward(self, xs) -> None:

@@ -244,23 +244,40 @@ __global__ void __launch_bounds__(kThreads, 3) k_dequant_many(const __grid_const
     const int64_t total = m.tile0[m.count];
     const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t gt = warp; gt < total; gt += nwarps) {
-        int lo = 0, hi = m.count - 1;  // the last tensor whose first tile is <= gt
+    // the tensor of warp tile gt: the last one whose first tile is <= gt
+    auto tensor_of = [&](int64_t gt) {
+        int lo = 0, hi = m.count - 1;
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
             if (m.tile0[mid] <= gt) lo = mid;
             else hi = mid - 1;
         }
-        const int t = lo;
+        return lo;
+    };
+    // loads of warp tile gt for this lane (zeros past the tensor's end); issued one tile
+    // ahead, so each warp has the next tile's packed bytes in flight while it decodes
+    auto load = [&](int64_t gt, uint4 &p0, uint4 &p1) {
+        p0 = make_uint4(0, 0, 0, 0);
+        p1 = p0;
+        if (gt >= total) return;
+        const int t = tensor_of(gt);
+        const int64_t g = ((gt - m.tile0[t]) << 5) + lane;
+        if (g < m.nseg[t]) {
+            const uint4 *pk = reinterpret_cast<const uint4 *>(m.packed[t]);
+            p0 = __ldcs(pk + 2 * g);
+            p1 = __ldcs(pk + 2 * g + 1);
+        }
+    };
+    uint4 n0, n1;
+    load(warp, n0, n1);
+    for (int64_t gt = warp; gt < total; gt += nwarps) {
+        const int t = tensor_of(gt);
         const int64_t wt = gt - m.tile0[t];
         const int64_t nseg = m.nseg[t];
         const int64_t g = (wt << 5) + lane;
-        const uint4 *pk = reinterpret_cast<const uint4 *>(m.packed[t]);
-        uint4 p0 = make_uint4(0, 0, 0, 0), p1 = p0;
+        const uint4 p0 = n0, p1 = n1;
         float am = 0.f;
         if (g < nseg) {
-            p0 = __ldcs(pk + 2 * g);
-            p1 = __ldcs(pk + 2 * g + 1);
             const int64_t blk = (g << 6) >> m.log2bs;
             if constexpr (DQ) {
                 am = __fadd_rn(__fmul_rn(__ldg(m.code2[t] + m.absmax_q[t][blk]),
@@ -270,6 +287,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_dequant_many(const __grid_const
                 am = __ldg(m.absmax[t] + blk);
             }
         }
+        load(gt + nwarps, n0, n1);
         const Nf4Tables tb = nf4_build_tables<BF16>(lv, am);
         const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
@@ -644,29 +662,35 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocAbsmaxB
 
 // Device address of g_noalloc_scratch on the current device.  The name is
 // only a host-side stand-in; the address comes from cudaGetSymbolAddress,
-// looked up once per device (on that device's first call) and cached.
+// looked up once per device (on that device's first call) and cached.  The
+// cache entries are atomics: threads that race on a device's first call all
+// store the same address.  The cache assumes the device's primary context
+// lives as long as the process (a cudaDeviceReset would leave a stale entry).
 static int noalloc_scratch(unsigned char **out) {
-    static unsigned char *ptrs[64] = {nullptr};
+    static std::atomic<unsigned char *> ptrs[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= 64)
         return fail(STRATUM_ERR_CUDA, "quantize_dq_noalloc: no current device (%s)", cudaGetErrorString(e));
-    if (ptrs[dev] == nullptr) {
+    unsigned char *cached = ptrs[dev].load(std::memory_order_acquire);
+    if (cached == nullptr) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || p == nullptr)
             return fail(STRATUM_ERR_CUDA, "quantize_dq_noalloc: cannot resolve the scratch array on device %d: %s", dev,
                         cudaGetErrorString(e));
-        ptrs[dev] = static_cast<unsigned char *>(p);
+        cached = static_cast<unsigned char *>(p);
+        ptrs[dev].store(cached, std::memory_order_release);
     }
-    *out = ptrs[dev];
+    *out = cached;
     return STRATUM_OK;
 }
 
 int stratum_nf4_quantize_dq_noalloc(const void *src, int src_dtype, int64_t n, const float *thresholds,
                                     const float *thresholds2, uint8_t *packed, uint8_t *absmax_q, float *absmax2,
                                     float *offset, void *stream) {
-    STRATUM_REQUIRE(n > 0, "quantize_dq_noalloc: n must be > 0");
+    STRATUM_REQUIRE(n >= 0, "quantize_dq_noalloc: n < 0");
+    if (n == 0) return STRATUM_OK;  // as stratum_nf4_quantize: nothing to do, nothing written
     const int64_t nb = (n + 63) / 64;
     if (nb > kNoAllocMaxBlocks)
         return fail(STRATUM_ERR_INVALID,

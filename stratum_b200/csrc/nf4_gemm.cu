@@ -752,17 +752,21 @@ int make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64
     return STRATUM_OK;
 }
 
+// Device address of g_gemm_status on the current device, resolved on the
+// device's first call and cached (atomics: racing first calls store the same value).
 int *status_ptr() {
-    static int *ptrs[64] = {nullptr};
+    static std::atomic<int *> ptrs[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return nullptr;
-    if (!ptrs[dev]) {
+    int *cached = ptrs[dev].load(std::memory_order_acquire);
+    if (!cached) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_gemm_status) != cudaSuccess) return nullptr;
-        ptrs[dev] = static_cast<int *>(p);
+        cached = static_cast<int *>(p);
+        ptrs[dev].store(cached, std::memory_order_release);
     }
-    return ptrs[dev];
+    return cached;
 }
 
 template <bool BF16, bool DQ>

@@ -53,11 +53,13 @@ def nf4_gemm_fwd(
     lora_B: Optional[torch.Tensor] = None,
     scaling: float = 1.0,
     xa: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """y = x . W^T + bias + scaling * (x . lora_A^T) . lora_B^T with W in NF4 (fused kernel).
 
     ``xa`` may be passed precomputed (scaling already applied, padded to a
-    multiple of 64 columns), e.g. when the backward needs it too.
+    multiple of 64 columns), e.g. when the backward needs it too.  ``out``: a
+    contiguous, 16-byte aligned [rows, N] tensor of x's dtype and device to write y into.
     """
     _lib.require_cuda(x, "nf4_gemm_fwd")
     if x.dtype not in (torch.bfloat16, torch.float16):
@@ -74,7 +76,14 @@ def nf4_gemm_fwd(
     if not x2.is_contiguous() or x2.data_ptr() % 16:
         x2 = x2.contiguous()
     T = x2.shape[0]
-    y = torch.empty((T, N), dtype=x.dtype, device=dev)
+    if out is None:
+        y = torch.empty((T, N), dtype=x.dtype, device=dev)
+    else:
+        if (out.dtype != x.dtype or out.device != dev or out.numel() != T * N or not out.is_contiguous()
+                or out.data_ptr() % 16):
+            raise ValueError(f"nf4_gemm_fwd: out must be a contiguous, 16-byte aligned {x.dtype} tensor of "
+                             f"{T * N} elements on {dev}")
+        y = out.view(T, N)
     r = 0
     lb = None
     if lora_B is not None:

@@ -87,8 +87,12 @@ def _device_tensors(module: nn.Module) -> list[torch.Tensor]:
 def _address_signature(module: nn.Module) -> tuple:
     """Data addresses of everything the module's forward reads from device memory:
     parameters, buffers, NF4Linear payloads and uploaded NF4Experts weights -- the
-    addresses a captured CUDA graph has baked in."""
-    ptrs = [t.data_ptr() for t in module.parameters()] + [t.data_ptr() for t in module.buffers()]
+    addresses a captured CUDA graph has baked in -- plus which parameters are
+    trainable (a captured backward writes the gradients of the set it was captured
+    with, so freezing or unfreezing a parameter needs a new graph)."""
+    params = list(module.parameters())
+    ptrs = [t.data_ptr() for t in params] + [t.data_ptr() for t in module.buffers()]
+    ptrs += [bool(p.requires_grad) for p in params]
     ptrs += [t.data_ptr() for t in _device_tensors(module)]
     for m in module.modules():
         for w, qs in ((getattr(m, "gate_up", None), getattr(m, "gate_up_state", None)),
@@ -100,6 +104,20 @@ def _address_signature(module: nn.Module) -> tuple:
             if qs.state2 is not None:
                 ptrs += [t.data_ptr() for t in (qs.state2.absmax, qs.state2.code) if torch.is_tensor(t)]
     return tuple(ptrs)
+
+
+def _check_status(devices, what: str) -> None:
+    """Raise if a GEMM kernel on any of ``devices`` gave up a bounded wait since the last
+    check.  Reading the status word clears it, so a caller that catches the error can
+    retry.  One host synchronisation per device; skipped for CPU devices (gloo tests)
+    and while a stream captures a CUDA graph."""
+    devs = {d for d in devices if d.type == "cuda"}
+    if not devs or torch.cuda.is_current_stream_capturing():
+        return
+    from . import _lib
+
+    for d in sorted(devs, key=lambda x: x.index or 0):
+        _lib.check_device_status(what, d)
 
 
 def _needs_streaming(module: nn.Module, device: torch.device) -> bool:
@@ -360,6 +378,8 @@ class StratumPipeline(nn.Module):
                 labels: Optional[torch.Tensor] = None, **kwargs):
         """Run forward through all stages; returns the loss when labels are given."""
         self._pending_bwd_fences = {}
+        # the previous step's backward ran after the last check: report a kernel that gave up
+        _check_status([_dev(s.device_id) for s in self.stages], "StratumPipeline.forward")
         if self._layer_timer is not None and hasattr(self._layer_timer, "update_times"):
             self._layer_timer.update_times()
         dev0 = _dev(self.stages[0].device_id)
@@ -420,6 +440,7 @@ class StratumPipeline(nn.Module):
             s.release_all()
         for stage in self.stages:
             free_weights(stage)
+        _check_status([_dev(s.device_id) for s in self.stages], "StratumPipeline.free_all_weights")
 
     def forward_batch(self, batch: Any, *, ignore_index: int = -100):
         """Forward on a dict-like batch with ``input_ids`` / ``attention_mask`` / ``labels``."""
@@ -709,6 +730,7 @@ class RankPipeline(nn.Module):
                 p.grad = a.clone()
             else:
                 p.grad.add_(a)
+        _check_status([self.device], "RankPipeline.train_step")
         return loss_acc / M
 
     def train_step(self, input_ids: Optional[torch.Tensor] = None, labels: Optional[torch.Tensor] = None, *,
@@ -737,7 +759,9 @@ class RankPipeline(nn.Module):
                 for i in range(len(self.stage.layers)):  # the stratum's upload, overlapped with microbatch 0
                     self.streamer.prefetch(i)
                 losses = self._train_1f1b(ids if first else None, labs if last else None, M, shape, use_aux)
+                self.chan.flush()
                 self.streamer.release_all()
+            _check_status([dev], "RankPipeline.train_step")
             if not last:
                 return None
             loss = torch.stack(losses).mean()
@@ -776,7 +800,9 @@ class RankPipeline(nn.Module):
                 if not first:
                     self.chan.send_backward(h_in.grad)
                 records[m] = None
+            self.chan.flush()
             self.streamer.release_all()
+        _check_status([dev], "RankPipeline.train_step")
         if use_aux:
             self.last_aux = torch.stack([r.value for r in aux_states]).mean()
         if not last:

@@ -726,17 +726,31 @@ def upload_stream(module: nn.Module, device_id: int, *, verbose: bool = True) ->
 
 @torch.no_grad()
 def snapshot_module_buffers(module: nn.Module) -> dict[str, torch.Tensor]:
-    """Copies of every buffer, for restoring after a recompute (stratum/upload.py:1162-1180)."""
-    return {name: b.detach().clone() for name, b in module.named_buffers()}
+    """Host copies of every non-empty buffer, taken before a group's forward so its
+    recompute can start from the same buffer state (stratum/upload.py:1162-1180).
+    Empty buffers (released weights, placeholders) are left out; the copies live in
+    host memory whatever the buffer's device, so a snapshot costs no device memory."""
+    snap: dict[str, torch.Tensor] = {}
+    for name, b in module.named_buffers():
+        if b.numel() > 0:
+            snap[name] = b.detach().to("cpu").clone()
+    return snap
 
 
 @torch.no_grad()
 def restore_module_buffers(module: nn.Module, snapshot: dict[str, torch.Tensor]) -> int:
+    """Copy a snapshot back into the module's buffers on their current devices
+    (stratum/upload.py:1183-1203); returns the number restored."""
+    if not snapshot:
+        return 0
+    bufs = dict(module.named_buffers())
     n = 0
-    for name, b in module.named_buffers():
-        if name in snapshot:
-            b.copy_(snapshot[name].to(b.device))
-            n += 1
+    for name, saved in snapshot.items():
+        b = bufs.get(name)
+        if b is None:
+            continue
+        b.data.copy_(saved.to(b.device))
+        n += 1
     return n
 
 

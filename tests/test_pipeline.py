@@ -251,6 +251,11 @@ def test_cuda_graph_address_signature_tracks_storage_not_values():
     assert _address_signature(model) == sig
     p.data = p.data.clone()  # new storage
     assert _address_signature(model) != sig
+    sig = _address_signature(model)
+    p.requires_grad_(False)  # a frozen adapter: the captured backward's gradient set changed
+    assert _address_signature(model) != sig
+    p.requires_grad_(True)
+    assert _address_signature(model) == sig
 
     holder = nn.Module()  # uploaded NF4Experts-style weights are covered too
 
@@ -263,3 +268,45 @@ def test_cuda_graph_address_signature_tracks_storage_not_values():
     s1 = _address_signature(holder)
     holder.gate_up = torch.zeros(8, dtype=torch.uint8)
     assert _address_signature(holder) != s1
+
+
+def _channel_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    from stratum_b200.boundary import P2PChannel
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ch = P2PChannel(rank, world)
+        got = []
+        if rank == 0:
+            for i in range(3):  # send-only groups: not waited on, kept alive until they complete
+                ch.send_forward([torch.full((5,), float(i))])
+            in_flight = ch.sends_in_flight
+            g = ch.recv_backward([((5,), torch.float32, "cpu")])[0]  # a receiving group is waited on
+            got.append(g)
+            ch.flush()
+            torch.save({"in_flight": in_flight, "after_flush": ch.sends_in_flight, "got": got},
+                       os.path.join(out_dir, "rank0.pt"))
+        else:
+            for _ in range(3):
+                got.append(ch.recv_forward([((5,), torch.float32, "cpu")])[0])
+            ch.send_backward([torch.full((5,), 7.0)])
+            ch.flush()
+            torch.save({"got": got, "after_flush": ch.sends_in_flight}, os.path.join(out_dir, "rank1.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_p2p_channel_send_only_groups_do_not_block_and_flush_retires_them():
+    """Send-only boundary groups return without waiting (the sender's stream runs on),
+    arrive in order, and ``flush`` retires every send still held."""
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_channel_main, args=(2, _free_port(), d), nprocs=2, start_method="spawn", join=True)
+        r0 = torch.load(os.path.join(d, "rank0.pt"))
+        r1 = torch.load(os.path.join(d, "rank1.pt"))
+    assert 0 <= r0["in_flight"] <= 3
+    assert r0["after_flush"] == 0 and r1["after_flush"] == 0
+    assert [float(t[0]) for t in r1["got"]] == [0.0, 1.0, 2.0]
+    assert torch.equal(r0["got"][0], torch.full((5,), 7.0))

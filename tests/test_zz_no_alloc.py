@@ -3,11 +3,12 @@
 It exists for callers of the C ABI that cannot hand the library a device
 workspace: an FFI host that only owns the buffers it passes in, or code that
 must not allocate at that point.  Its scratch is a fixed array inside the
-library, shared by every call.  This test calls it through the C ABI twice in
-a row (a large input, then a smaller one, so the second call runs over scratch
-the first left behind) and checks each result bit for bit against the regular
-entry points given a caller-allocated workspace -- the codec's tolerance is
-exact.  It also checks the size limit.
+library, shared by every call.  This test calls it through the C ABI three
+times in a row (a large input, then a smaller one, so the second call runs over
+scratch the first left behind, then one whose last NF4 block is partial) and
+checks each result bit for bit against the regular entry points given a
+caller-allocated workspace -- the codec's tolerance is exact.  It also checks
+the size limit and that an empty input is a no-op.
 
 Named so pytest collects it last; it passes alone and after the other tests.
 """
@@ -66,7 +67,9 @@ def _no_alloc(w):
 def test_no_alloc_matches_regular_entry_points_on_two_calls_in_a_row():
     big = workloads.codec_weight((14336, 4096), seed=21)  # 58.7 M elements, close to the limit
     small = workloads.codec_weight((1000, 4096 + 192), seed=22).to(torch.bfloat16)  # ragged block count
-    for w in (big, small):
+    # a partial final NF4 block (n % 64 == 37) and an odd element count (half-filled last byte)
+    tail = workloads.codec_weight((64 * 1000 + 37,), seed=23)
+    for w in (big, small, tail):
         got = _no_alloc(w)
         ref = _regular(w)
         torch.cuda.synchronize()
@@ -82,3 +85,14 @@ def test_no_alloc_rejects_sizes_above_its_scratch():
                                            _lib.stream_of(dummy.device))
     assert rc == _lib.STRATUM_ERR_INVALID
     assert b"fixed scratch" in L.stratum_last_error()
+
+
+def test_no_alloc_empty_input_is_a_no_op():
+    L = _lib.lib()
+    dummy = torch.full((16,), 0xEE, dtype=torch.uint8, device=DEV)
+    rc = L.stratum_nf4_quantize_dq_noalloc(_lib.ptr(dummy), 1, 0, _lib.ptr(dummy), _lib.ptr(dummy), _lib.ptr(dummy),
+                                           _lib.ptr(dummy), _lib.ptr(dummy), _lib.ptr(dummy),
+                                           _lib.stream_of(dummy.device))
+    assert rc == _lib.STRATUM_OK
+    torch.cuda.synchronize()
+    assert bool((dummy == 0xEE).all())
