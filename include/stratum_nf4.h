@@ -190,6 +190,63 @@ int stratum_nf4_gemm_dx(const void *dy, int dtype, int64_t T, int64_t N,
                         int64_t K, const void *lora_dyb, const void *lora_a, int r,
                         void *dx, void *stream);
 
+/* One NF4 weight for the fused MLP entry points below: packed bytes and either
+ * absmax (plain) or, with absmax == NULL, the double-quant set. */
+typedef struct stratum_nf4_weight {
+    const uint8_t *packed;
+    const float *absmax;
+    const uint8_t *absmax_q;
+    const float *absmax2;
+    const float *code2;
+    const float *offset;
+} stratum_nf4_weight;
+
+/* Fused SwiGLU up-projection of a dense MLP (LlamaMLP / Qwen3MLP with two
+ * NF4Linear + PEFT LoRA projections and SiLU): one GEMM pass over x computes
+ *   gate = x . Wg^T + lora_xa[:, 0:r] . lora_b_gate^T
+ *   up   = x . Wu^T + lora_xa[:, rp:rp+r] . lora_b_up^T     (rp = ceil(r/64)*64)
+ *   h    = r16(r16(silu(r16(gate))) * r16(up))              (HF's bf16 forward)
+ * Replaces act_fn(gate_proj(x)) * up_proj(x) of the reference's MLP, whose
+ * fused-memory variant is stratum/model/mlp_opt.py:154-245 (MemoryFlatFrozenMLP).
+ *   x          : T x K (K % 64 == 0), BF16 or F16, 16-byte aligned
+ *   gate, up   : NF4 weights I x K (I % 64 == 0), both plain or both double quant
+ *   lora_xa    : T x 2*rp in x's dtype = [scaling_g * x . A_g^T | 0 | scaling_u * x . A_u^T | 0]
+ *                (NULL when r == 0)
+ *   lora_b_*   : I x r (r even, <= 256), NULL when r == 0
+ *   h          : T x I;  gate_out / up_out: T x I (the 16-bit gate and up, for the
+ *                backward), or NULL */
+int stratum_nf4_gemm_swiglu_fwd(const void *x, int x_dtype, int64_t T, int64_t K,
+                                const stratum_nf4_weight *gate, const stratum_nf4_weight *up,
+                                const float *code16, int64_t I, const void *lora_xa,
+                                const void *lora_b_gate, const void *lora_b_up, int r,
+                                void *h, void *gate_out, void *up_out, void *stream);
+
+/* Input gradient through two NF4 weights stacked along N (the gate and up
+ * projections of a SwiGLU MLP), one pass:
+ *   dx[T,K] = dy[T, N0+N1] . [W0; W1] + lora_dyb[T, r] . lora_a[r, K]
+ * Replaces the two F.linear backwards (and PEFT LoRA's) of gate_proj and
+ * up_proj, summed by autograd.  N0, N1 multiples of 64; both weights plain or
+ * both double quantized; lora_dyb / lora_a as in stratum_nf4_gemm_dx, e.g. the
+ * two adapters' terms side by side. */
+int stratum_nf4_gemm_dx_pair(const void *dy, int dtype, int64_t T,
+                             const stratum_nf4_weight *w0, int64_t N0,
+                             const stratum_nf4_weight *w1, int64_t N1,
+                             const float *code16, int64_t K, const void *lora_dyb,
+                             const void *lora_a, int r, void *dx, void *stream);
+
+/* Input gradient of a SwiGLU MLP's down projection with the SwiGLU backward in
+ * the epilogue: dh = dy . Wd + lora_dyb . lora_a (as stratum_nf4_gemm_dx, rounded
+ * to 16 bits), then with the forward's 16-bit gate and up
+ *   dup   = r16(dh * r16(silu(gate)))
+ *   dgate = r16(r16(dh * up) * s * (1 + gate * (1 - s))),  s = sigmoid(gate)
+ * written as dgate_up[T, 2I] = [dgate | dup] (dh itself is never stored).
+ * Replaces the down_proj backward and the SiLU / multiply backward of the
+ * reference's MLP (stratum/model/mlp_opt.py:154-245).  I % 64 == 0. */
+int stratum_nf4_gemm_dx_swiglu(const void *dy, int dtype, int64_t T, int64_t N,
+                               const stratum_nf4_weight *w, const float *code16, int64_t I,
+                               const void *lora_dyb, const void *lora_a, int r,
+                               const void *gate, const void *up, void *dgate_up, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

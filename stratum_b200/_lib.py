@@ -48,6 +48,10 @@ SIGNATURES: dict[str, tuple] = {
                                     _vp, _int, _vp, _vp]),
     "stratum_nf4_gemm_dx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _int,
                                    _vp, _vp]),
+    "stratum_nf4_gemm_swiglu_fwd": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _int, _vp, _vp,
+                                           _vp, _vp]),
+    "stratum_nf4_gemm_dx_pair": (_int, [_vp, _int, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _int, _vp, _vp]),
+    "stratum_nf4_gemm_dx_swiglu": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     # include/stratum_moe.h
     "stratum_moe_route_workspace_bytes": (_sz, [_i64, _int]),
     "stratum_moe_route": (_int, [_vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
@@ -138,6 +142,13 @@ def stream_of(device: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(handle)
 
 
+class NF4Weight(ctypes.Structure):
+    """``stratum_nf4_weight`` of include/stratum_nf4.h."""
+
+    _fields_ = [("packed", _vp), ("absmax", _vp), ("absmax_q", _vp), ("absmax2", _vp), ("code2", _vp),
+                ("offset", _vp)]
+
+
 def require_cuda(t: torch.Tensor, what: str) -> None:
     if t.device.type != "cuda":
         raise RuntimeError(f"{what}: tensor on {t.device}; the NF4 kernels run on CUDA only (no CPU fallback)")
@@ -153,9 +164,13 @@ def device_status(device=None, reset: bool = True) -> int:
 
 
 def check_device_status(what: str, device=None) -> None:
+    """Raise :class:`StratumError` if a GEMM kernel on ``device`` gave up a bounded wait
+    (or rejected its tile table) since the last read.  The read clears the word, so
+    after the error the caller may retry; the results of the failed step are invalid."""
     st = device_status(device)
     if st != 0:
-        raise StratumError(f"{what}: a device-side wait timed out (status 0x{st:x}); the kernel unwound")
+        raise StratumError(f"{what}: a device-side wait timed out or a tile table was rejected (status 0x{st:x}); "
+                           "the kernel unwound and its outputs are invalid (the status word is now cleared)")
 
 
 def launch_count() -> int:

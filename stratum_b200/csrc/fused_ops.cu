@@ -13,42 +13,17 @@
 // and the matching backward passes.  All are HBM-bound: 16-byte vector
 // accesses, one warp per row for the reductions, grids sized to the SM count.
 #include "common.cuh"
+#include "half8.cuh"
 
 namespace stratum {
 namespace fused {
 
-template <bool BF16>
-__device__ __forceinline__ float ld1(const uint16_t v) {
-    if constexpr (BF16) return __uint_as_float(uint32_t(v) << 16);
-    else return __half2float(__ushort_as_half(v));
-}
-
-template <bool BF16>
-__device__ __forceinline__ uint16_t st1(float f) {
-    if constexpr (BF16) return __bfloat16_as_ushort(__float2bfloat16_rn(f));
-    else return __half_as_ushort(__float2half_rn(f));
-}
-
-template <bool BF16>
-__device__ __forceinline__ float rnd(float f) {  // round to the 16-bit type and back
-    return ld1<BF16>(st1<BF16>(f));
-}
-
-template <bool BF16>
-__device__ __forceinline__ void unpack8(const uint4 v, float f[8]) {
-    const uint16_t *h = reinterpret_cast<const uint16_t *>(&v);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = ld1<BF16>(h[i]);
-}
-
-template <bool BF16>
-__device__ __forceinline__ uint4 pack8(const float f[8]) {
-    uint4 v;
-    uint16_t *h = reinterpret_cast<uint16_t *>(&v);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] = st1<BF16>(f[i]);
-    return v;
-}
+using h16::ld1;
+using h16::st1;
+using h16::rnd;
+using h16::unpack8;
+using h16::pack8;
+using h16::sigmoid_f;
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -189,8 +164,6 @@ __global__ void k_rope_from_heads(const uint4 *__restrict__ dy, const uint4 *__r
 
 // ------------------------------------------------------------------- SwiGLU --
 
-__device__ __forceinline__ float sigmoid_f(float g) { return 1.f / (1.f + expf(-g)); }
-
 template <bool BF16>
 __global__ void k_swiglu_fwd(const uint4 *__restrict__ g, const uint4 *__restrict__ u, int64_t n,
                              uint4 *__restrict__ h) {
@@ -199,7 +172,7 @@ __global__ void k_swiglu_fwd(const uint4 *__restrict__ g, const uint4 *__restric
         unpack8<BF16>(g[i], a);
         unpack8<BF16>(u[i], b);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) a[k] = rnd<BF16>(a[k] / (1.f + expf(-a[k]))) * b[k];
+        for (int k = 0; k < 8; ++k) a[k] = h16::swiglu_fwd1<BF16>(a[k], b[k]);
         h[i] = pack8<BF16>(a);
     }
 }
@@ -214,12 +187,7 @@ __global__ void k_swiglu_bwd(const uint4 *__restrict__ g, const uint4 *__restric
         unpack8<BF16>(u[i], b);
         unpack8<BF16>(dh[i], d);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float s = sigmoid_f(a[k]);
-            ob[k] = d[k] * rnd<BF16>(a[k] / (1.f + expf(-a[k])));
-            const float dact = rnd<BF16>(d[k] * b[k]);
-            oa[k] = dact * s * (1.f + a[k] * (1.f - s));  // torch's silu_backward order
-        }
+        for (int k = 0; k < 8; ++k) h16::swiglu_bwd1<BF16>(a[k], b[k], d[k], oa[k], ob[k]);
         dg[i] = pack8<BF16>(oa);
         du[i] = pack8<BF16>(ob);
     }

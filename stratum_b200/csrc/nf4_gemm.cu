@@ -26,6 +26,7 @@
 // turns by K-step; w%4 selects the TMEM lane quarter), w16-19 epilogue.
 // Every wait is bounded; a timeout records a status word and unwinds.
 #include "common.cuh"
+#include "half8.cuh"
 #include "nf4_decode.cuh"
 #include "sm100.cuh"
 
@@ -56,28 +57,48 @@ constexpr int A_COL0 = 256;   // A ring: columns [256, 256 + 32 * AS)
 constexpr int EPI_WARP0 = 4 + 4 * DQG;
 constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_BYTES + WS * W_BYTES + 2 * Y_HALF_BYTES +
-                           1024 /*barriers*/ + 1088 /*tables*/;
+                           1024 /*barriers*/ + 2112 /*tables*/;
 static_assert(A_COL0 + AS * 32 <= TMEM_COLS, "TMEM budget");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
-struct FwdParams {
+// One NF4 weight's absmax (plain, or the double-quant set).
+struct WeightScales {
     const float *absmax;      // [N, K/64] (plain)
     const uint8_t *absmax_q;  // [N, K/64] (double quant)
     const float *absmax2;     // [ceil(N*K/64 / 256)]
     const float *code2;       // [256]
     const float *offset;      // [1]
+};
+
+struct FwdParams {
+    WeightScales w;           // the weight (SWIGLU: the gate projection's)
+    WeightScales wu;          // SWIGLU: the up projection's
     const float *code16;      // [16]
     const void *bias;         // [N] or null
     int bias_dtype;
-    const uint16_t *lora_b;   // [N, r] (bf16/fp16 bits) or null
+    const uint16_t *lora_b;   // [N, r] (bf16/fp16 bits) or null (SWIGLU: the gate projection's)
+    const uint16_t *lora_bu;  // SWIGLU: the up projection's [N, r]
     int r;
+    int lora_rp;              // SWIGLU: columns of xa per projection (r rounded up to 64)
     int lora_chunks;
-    uint16_t *y;              // [T, N]
+    uint16_t *y;              // [T, N] (SWIGLU: h [T, N], N = the projections' width)
+    uint16_t *gate, *up;      // SWIGLU, optional: the 16-bit gate and up [T, N] for the backward
     int64_t T, N, K;
     int n_tiles, t_tiles;
     int tma_store;            // y stored through the staging tile + TMA (N % 8 == 0, 16-byte aligned)
     int *status;
 };
+
+// absmax of NF4 block b of a weight (plain, or rebuilt from the double-quant set
+// with its code2 table in shared memory)
+template <bool DQ>
+__device__ __forceinline__ float block_scale(const WeightScales &w, const float *c2, int64_t b) {
+    if constexpr (DQ) {
+        return __fadd_rn(__fmul_rn(c2[__ldg(w.absmax_q + b)], __ldg(w.absmax2 + (b >> 8))), *w.offset);
+    } else {
+        return __ldg(w.absmax + b);
+    }
+}
 
 struct Smem {
     uint8_t *x0;    // token tile i at x0 + i * X_BYTES (1024-byte aligned)
@@ -87,7 +108,7 @@ struct Smem {
     // (128 dequant arrivals); empty[s]: the stage's MMAs completed (one commit)
     uint64_t *full, *empty, *wfull, *wempty, *accfull, *accempty, *drain;
     uint32_t *tmem_slot;
-    float *lv, *c2;
+    float *lv, *c2, *c2u;
 };
 
 __device__ __forceinline__ Smem carve(uint8_t *raw) {
@@ -111,6 +132,7 @@ __device__ __forceinline__ Smem carve(uint8_t *raw) {
     s.tmem_slot = reinterpret_cast<uint32_t *>(b);
     s.lv = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(b) + 64);
     s.c2 = s.lv + 16;
+    s.c2u = s.c2 + 256;
     return s;
 }
 
@@ -126,10 +148,16 @@ __device__ __forceinline__ uint16_t to16(float v) {
     else return __half_as_ushort(__float2half_rn(v));
 }
 
-template <bool BF16, bool DQ>
+// SWIGLU: the tile's 128 weight rows are 64 rows of the gate projection (TMEM
+// lanes 0-63, packed tiles from tm_w) and the same 64 rows of the up projection
+// (lanes 64-127, from tm_w2); the epilogue forms h = silu(gate) * up from the
+// 16-bit gate and up and writes h (and gate / up for the backward) -- the dense
+// LlamaMLP up-projection in one pass over x.
+template <bool BF16, bool DQ, bool SWIGLU>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-               const __grid_constant__ CUtensorMap tm_xa, const __grid_constant__ CUtensorMap tm_y, const FwdParams p) {
+               const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_xa,
+               const __grid_constant__ CUtensorMap tm_y, const FwdParams p) {
     extern __shared__ uint8_t smem_raw[];
     Smem sm = carve(smem_raw);
     const int warp = threadIdx.x >> 5;
@@ -156,7 +184,9 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     }
     if (threadIdx.x < 16) sm.lv[threadIdx.x] = p.code16[threadIdx.x];
     if (DQ) {
-        for (int i = threadIdx.x; i < 256; i += NUM_THREADS) sm.c2[i] = p.code2[i];
+        for (int i = threadIdx.x; i < 256; i += NUM_THREADS) sm.c2[i] = p.w.code2[i];
+        if (SWIGLU)
+            for (int i = threadIdx.x; i < 256; i += NUM_THREADS) sm.c2u[i] = p.wu.code2[i];
     }
     if (warp == 1) tmem_alloc(sm.tmem_slot, TMEM_COLS);
     tc_fence_before();
@@ -191,10 +221,11 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         // ---------------------------------- producer: packed weight tiles
         if (lane == 0) {
             prefetch_tensormap(&tm_w);
+            if (SWIGLU) prefetch_tensormap(&tm_w2);
             uint32_t wt = 0;
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
-                const int n0 = ((int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles) * BM;
+                const int m = (int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles;
                 for (int ks = 0; ks < nkw; ++ks, ++wt) {
                     const int s = wt % WS;
                     if (!mbar_wait(&sm.wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
@@ -202,7 +233,12 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                         break;
                     }
                     mbar_arrive_expect_tx(&sm.wfull[s], W_BYTES);
-                    tma_load_2d(sm.w0 + s * W_BYTES, &tm_w, ks * (BK / 2), n0, &sm.wfull[s]);
+                    if constexpr (SWIGLU) {  // 64 gate rows, then the same 64 up rows
+                        tma_load_2d(sm.w0 + s * W_BYTES, &tm_w, ks * (BK / 2), m * 64, &sm.wfull[s]);
+                        tma_load_2d(sm.w0 + s * W_BYTES + W_BYTES / 2, &tm_w2, ks * (BK / 2), m * 64, &sm.wfull[s]);
+                    } else {
+                        tma_load_2d(sm.w0 + s * W_BYTES, &tm_w, ks * (BK / 2), m * BM, &sm.wfull[s]);
+                    }
                 }
             }
             for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
@@ -244,21 +280,25 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
+        // SWIGLU: lanes 64-127 hold up-projection rows (warp-uniform: q >= 2)
+        const bool upper = SWIGLU && q >= 2;
+        const WeightScales &ws = upper ? p.wu : p.w;
+        const float *c2 = upper ? sm.c2u : sm.c2;
         float lv[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) lv[i] = sm.lv[i];
         const int64_t kb = p.K / BK;
+        // weight row of this lane in tile tl (SWIGLU: row of its projection)
+        auto row_of = [&](int tl) -> int64_t {
+            const int m = (int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles;
+            return SWIGLU ? int64_t(m) * 64 + (row & 63) : int64_t(m) * BM + row;
+        };
         auto absmax_of = [&](uint32_t it) -> float {
             const int tl = int(it / nk), ks = int(it % nk);
             if (tl >= my_tiles || ks >= nkw) return 0.f;
-            const int64_t n = int64_t((int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles) * BM + row;
+            const int64_t n = row_of(tl);
             if (n >= p.N) return 0.f;
-            const int64_t b = n * kb + ks;
-            if constexpr (DQ) {
-                return __fadd_rn(__fmul_rn(sm.c2[__ldg(p.absmax_q + b)], __ldg(p.absmax2 + (b >> 8))), *p.offset);
-            } else {
-                return __ldg(p.absmax + b);
-            }
+            return block_scale<DQ>(ws, c2, n * kb + ks);
         };
         const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
         float am_next = absmax_of(uint32_t(grp));
@@ -266,7 +306,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             const float am = am_next;
             am_next = absmax_of(it + DQG);  // one owned step ahead
             const int tl = int(it / nk), ks = int(it % nk);
-            const int64_t n = int64_t((int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles) * BM + row;
+            const int64_t n = row_of(tl);
             uint32_t vals[32];
             if (ks < nkw) {
                 const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
@@ -288,10 +328,24 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             } else {
                 const int j0 = (ks - nkw) * BK;
                 const bool valid = n < p.N;
+                if constexpr (SWIGLU) {
+                    // xa = [gate's xa | 0-pad | up's xa | 0-pad], lora_rp columns each: the gate
+                    // rows take lora_b over columns [0, r), the up rows lora_bu over [rp, rp + r)
+                    const uint16_t *lb = upper ? p.lora_bu : p.lora_b;
+                    const int c0 = upper ? p.lora_rp : 0;
 #pragma unroll
-                for (int m = 0; m < 32; ++m) {
-                    const int j = j0 + 2 * m;
-                    vals[m] = (valid && j < p.r) ? __ldg(reinterpret_cast<const uint32_t *>(p.lora_b + n * p.r + j)) : 0u;
+                    for (int m = 0; m < 32; ++m) {
+                        const int j = j0 + 2 * m - c0;
+                        vals[m] = (valid && j >= 0 && j < p.r)
+                                      ? __ldg(reinterpret_cast<const uint32_t *>(lb + n * p.r + j)) : 0u;
+                    }
+                } else {
+#pragma unroll
+                    for (int m = 0; m < 32; ++m) {
+                        const int j = j0 + 2 * m;
+                        vals[m] = (valid && j < p.r) ? __ldg(reinterpret_cast<const uint32_t *>(p.lora_b + n * p.r + j))
+                                                     : 0u;
+                    }
                 }
             }
             const int sa = it % AS;
@@ -314,7 +368,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             const int tile = int(blockIdx.x) + tl * int(gridDim.x);
             const int64_t n0 = int64_t(tile % p.n_tiles) * BM;
             const int64_t t0 = int64_t(tile / p.n_tiles) * BN;
-            if (p.tma_store) {
+            if (SWIGLU || p.tma_store) {
                 // TMEM -> registers as 16x256b fragments (row = weight row, pairs of
                 // tokens), + bias, -> 16-bit -> stmatrix.trans into the [token][row]
                 // staging tile, then one TMA store per 64-row half.
@@ -368,12 +422,39 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                     stage_block(cb, v0);
                     stage_block(cb + 1, v1);
                 }
-                fence_proxy_async_smem();
-                named_bar_sync(1, 128);
-                if (leader) {
-                    tma_store_2d(&tm_y, int32_t(n0), int32_t(t0), sm.y0);
-                    if (n0 + 64 < p.N) tma_store_2d(&tm_y, int32_t(n0 + 64), int32_t(t0), sm.y0 + Y_HALF_BYTES);
-                    bulk_commit();
+                if constexpr (SWIGLU) {
+                    // staging half 0 holds the tile's 64 gate rows, half 1 the same 64 up rows
+                    // (16-bit, as HF's bf16 projections round them): h = silu(gate) * up,
+                    // 8 columns per 16-byte chunk, stored row by row with the gate and up
+                    named_bar_sync(1, 128);
+                    const int etid = int(threadIdx.x) - EPI_WARP0 * 32;
+                    const int64_t col0 = int64_t(tile % p.n_tiles) * 64;
+                    const int ntok = int(p.T - t0 < BN ? p.T - t0 : BN);
+                    for (int idx = etid; idx < ntok * 8; idx += 128) {
+                        const int tok = idx >> 3, chunk = idx & 7;
+                        const int64_t col = col0 + chunk * 8;
+                        if (col >= p.N) continue;
+                        const int off = tok * 128 + ((chunk ^ (tok & 7)) << 4);
+                        const uint4 gv = *reinterpret_cast<const uint4 *>(sm.y0 + off);
+                        const uint4 uv = *reinterpret_cast<const uint4 *>(sm.y0 + Y_HALF_BYTES + off);
+                        float g[8], u[8], h[8];
+                        h16::unpack8<BF16>(gv, g);
+                        h16::unpack8<BF16>(uv, u);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) h[i] = h16::swiglu_fwd1<BF16>(g[i], u[i]);
+                        const int64_t at = (t0 + tok) * p.N + col;
+                        *reinterpret_cast<uint4 *>(p.y + at) = h16::pack8<BF16>(h);
+                        if (p.gate) *reinterpret_cast<uint4 *>(p.gate + at) = gv;
+                        if (p.up) *reinterpret_cast<uint4 *>(p.up + at) = uv;
+                    }
+                } else {
+                    fence_proxy_async_smem();
+                    named_bar_sync(1, 128);
+                    if (leader) {
+                        tma_store_2d(&tm_y, int32_t(n0), int32_t(t0), sm.y0);
+                        if (n0 + 64 < p.N) tma_store_2d(&tm_y, int32_t(n0 + 64), int32_t(t0), sm.y0 + Y_HALF_BYTES);
+                        bulk_commit();
+                    }
                 }
             } else {
                 // generic path (N % 8 != 0 or unaligned y): element stores
@@ -440,26 +521,31 @@ constexpr int SMEM_BYTES = 1024 + XS * X_BYTES + AS * A_BYTES + 2 * Y_HALF_BYTES
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 struct Params {
-    const float *absmax;
-    const uint8_t *absmax_q;
-    const float *absmax2;
-    const float *code2;
-    const float *offset;
+    WeightScales w;          // the weight (PAIR: the first of the two stacked weights)
+    WeightScales w1;         // PAIR: the second weight
     const float *code16;
     const uint16_t *lora_a;  // [r, K] or null
     int r;
     int lora_chunks;
-    uint16_t *dx;            // [T, K]
+    uint16_t *dx;            // [T, K] (SWIGLU_BWD: the gate / up gradients [T, 2K])
+    const uint16_t *gate, *up;  // SWIGLU_BWD: the forward's 16-bit gate and up [T, K]
     int64_t T, N, K;
+    int nkw0;                // PAIR: contraction steps (64 rows each) over the first weight
     int k_tiles, t_tiles;
     int tma_store;
     int *status;
 };
 
-template <bool BF16, bool DQ>
+// PAIR: the contraction runs over two NF4 weights stacked along N (rows [0, N0)
+// from tm_w, [N0, N) from tm_w2), e.g. the gate and up projections of an MLP whose
+// dY is [dgate | dup].  SWIGLU_BWD: this is the down projection of a SwiGLU MLP;
+// the epilogue turns its dX (= dh, rounded to 16 bits) and the forward's gate /
+// up into [dgate | dup] with the SwiGLU backward, so dh never reaches HBM.
+template <bool BF16, bool DQ, bool PAIR, bool SWIGLU_BWD>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_w,
-              const __grid_constant__ CUtensorMap tm_dyb, const __grid_constant__ CUtensorMap tm_dx, const Params p) {
+              const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_dyb,
+              const __grid_constant__ CUtensorMap tm_dx, const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *x0 = base;                              // XS x 32 KiB (1024-aligned)
@@ -492,7 +578,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
     }
     if (threadIdx.x < 16) lv_s[threadIdx.x] = p.code16[threadIdx.x];
     if (DQ) {
-        for (int i = threadIdx.x; i < 256; i += NUM_THREADS) c2[i] = p.code2[i];
+        for (int i = threadIdx.x; i < 256; i += NUM_THREADS) c2[i] = p.w.code2[i];
     }
     if (warp == 1) tmem_alloc(tmem_slot, 512);
     tc_fence_before();
@@ -524,6 +610,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
         // ------------------------------- producer: packed weight tiles (64 x 128)
         if (lane == 0) {
             prefetch_tensormap(&tm_w);
+            if (PAIR) prefetch_tensormap(&tm_w2);
             uint32_t wt = 0;
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
@@ -532,7 +619,8 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                     const int s = wt % WS;
                     if (!mbar_wait(&wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
                     mbar_arrive_expect_tx(&wfull[s], W_BYTES);
-                    tma_load_2d(w0 + s * W_BYTES, &tm_w, k0 / 2, ks * BK, &wfull[s]);
+                    if (PAIR && ks >= p.nkw0) tma_load_2d(w0 + s * W_BYTES, &tm_w2, k0 / 2, (ks - p.nkw0) * BK, &wfull[s]);
+                    else tma_load_2d(w0 + s * W_BYTES, &tm_w, k0 / 2, ks * BK, &wfull[s]);
                 }
             }
             for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
@@ -587,12 +675,10 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
             int64_t wrow, kblk;
             const int ks = block_of(it, wrow, kblk);
             if (ks >= nkw || wrow >= p.N || kblk >= kbl) return 0.f;
-            const int64_t b = wrow * kbl + kblk;
-            if constexpr (DQ) {
-                return __fadd_rn(__fmul_rn(c2[__ldg(p.absmax_q + b)], __ldg(p.absmax2 + (b >> 8))), *p.offset);
-            } else {
-                return __ldg(p.absmax + b);
-            }
+            if (PAIR && ks >= p.nkw0)  // a row of the second weight (step-uniform choice); its code2
+                // table is read from global memory (shared memory has room for one table only)
+                return block_scale<DQ>(p.w1, p.w1.code2, (wrow - int64_t(p.nkw0) * BK) * kbl + kblk);
+            return block_scale<DQ>(p.w, c2, wrow * kbl + kblk);
         };
         const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
         float am_next = absmax_of(uint32_t(grp));
@@ -656,7 +742,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
             const int64_t k0 = int64_t(tile % p.k_tiles) * BM;
             const int64_t t0 = int64_t(tile / p.k_tiles) * BN;
             const uint32_t acc = tmem + lane_addr + uint32_t(ab * 256);
-            if (p.tma_store) {
+            if (SWIGLU_BWD || p.tma_store) {
                 if (leader) bulk_wait_read0();
                 named_bar_sync(1, 128);
 #pragma unroll 1
@@ -684,12 +770,38 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                         stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
                     }
                 }
-                fence_proxy_async_smem();
-                named_bar_sync(1, 128);
-                if (leader) {
-                    tma_store_2d(&tm_dx, int32_t(k0), int32_t(t0), y0);
-                    if (k0 + 64 < p.K) tma_store_2d(&tm_dx, int32_t(k0 + 64), int32_t(t0), y0 + Y_HALF_BYTES);
-                    bulk_commit();
+                if constexpr (SWIGLU_BWD) {
+                    // the staged tile is dh (16-bit, as the plain kernel would store it):
+                    // with the forward's gate and up, form dgate and dup and write them as
+                    // [dgate | dup] rows of width 2K, 8 columns per 16-byte chunk
+                    named_bar_sync(1, 128);
+                    const int etid = int(threadIdx.x) - EPI_WARP0 * 32;
+                    const int ntok = int(p.T - t0 < BN ? p.T - t0 : BN);
+                    for (int idx = etid; idx < ntok * 16; idx += 128) {
+                        const int tok = idx >> 4, hc = idx & 15, half = hc >> 3, chunk = hc & 7;
+                        const int64_t k = k0 + half * 64 + chunk * 8;
+                        if (k >= p.K) continue;
+                        const uint4 dv = *reinterpret_cast<const uint4 *>(y0 + half * Y_HALF_BYTES + tok * 128 +
+                                                                          ((chunk ^ (tok & 7)) << 4));
+                        const int64_t at = (t0 + tok) * p.K + k;
+                        float g[8], u[8], dh[8], dg[8], du[8];
+                        h16::unpack8<BF16>(dv, dh);
+                        h16::unpack8<BF16>(*reinterpret_cast<const uint4 *>(p.gate + at), g);
+                        h16::unpack8<BF16>(*reinterpret_cast<const uint4 *>(p.up + at), u);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) h16::swiglu_bwd1<BF16>(g[i], u[i], dh[i], dg[i], du[i]);
+                        uint16_t *row = p.dx + (t0 + tok) * (2 * p.K);
+                        *reinterpret_cast<uint4 *>(row + k) = h16::pack8<BF16>(dg);
+                        *reinterpret_cast<uint4 *>(row + p.K + k) = h16::pack8<BF16>(du);
+                    }
+                } else {
+                    fence_proxy_async_smem();
+                    named_bar_sync(1, 128);
+                    if (leader) {
+                        tma_store_2d(&tm_dx, int32_t(k0), int32_t(t0), y0);
+                        if (k0 + 64 < p.K) tma_store_2d(&tm_dx, int32_t(k0 + 64), int32_t(t0), y0 + Y_HALF_BYTES);
+                        bulk_commit();
+                    }
                 }
             } else {
                 const int64_t k = k0 + q * 32 + lane;
@@ -769,10 +881,10 @@ int *status_ptr() {
     return cached;
 }
 
-template <bool BF16, bool DQ>
-int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mxa, const CUtensorMap &my,
-               const FwdParams &p, cudaStream_t st) {
-    auto kern = k_nf4_gemm_fwd<BF16, DQ>;
+template <bool BF16, bool DQ, bool SWIGLU>
+int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mw2, const CUtensorMap &mxa,
+               const CUtensorMap &my, const FwdParams &p, cudaStream_t st) {
+    auto kern = k_nf4_gemm_fwd<BF16, DQ, SWIGLU>;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -783,14 +895,14 @@ int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &
     }
     const int ntiles = p.n_tiles * p.t_tiles;
     const int grid = ntiles < sm_count() ? ntiles : sm_count();
-    kern<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(mx, mw, mxa, my, p);
-    return check_launch("nf4_gemm_fwd");
+    kern<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(mx, mw, mw2, mxa, my, p);
+    return check_launch(SWIGLU ? "nf4_gemm_swiglu_fwd" : "nf4_gemm_fwd");
 }
 
-template <bool BF16, bool DQ>
-int launch_dx(const CUtensorMap &mdy, const CUtensorMap &mw, const CUtensorMap &mdyb, const CUtensorMap &mdx,
-              const dx::Params &p, cudaStream_t st) {
-    auto kern = dx::k_nf4_gemm_dx<BF16, DQ>;
+template <bool BF16, bool DQ, bool PAIR, bool SWIGLU_BWD>
+int launch_dx(const CUtensorMap &mdy, const CUtensorMap &mw, const CUtensorMap &mw2, const CUtensorMap &mdyb,
+              const CUtensorMap &mdx, const dx::Params &p, cudaStream_t st) {
+    auto kern = dx::k_nf4_gemm_dx<BF16, DQ, PAIR, SWIGLU_BWD>;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -801,8 +913,98 @@ int launch_dx(const CUtensorMap &mdy, const CUtensorMap &mw, const CUtensorMap &
     }
     const int ntiles = p.k_tiles * p.t_tiles;
     const int grid = ntiles < sm_count() ? ntiles : sm_count();
-    kern<<<grid, dx::NUM_THREADS, dx::SMEM_BYTES, st>>>(mdy, mw, mdyb, mdx, p);
-    return check_launch("nf4_gemm_dx");
+    kern<<<grid, dx::NUM_THREADS, dx::SMEM_BYTES, st>>>(mdy, mw, mw2, mdyb, mdx, p);
+    return check_launch(PAIR ? "nf4_gemm_dx_pair" : SWIGLU_BWD ? "nf4_gemm_dx_swiglu" : "nf4_gemm_dx");
+}
+
+// Shared set-up of the input-gradient entry points: validation, tensor maps,
+// parameters and the launch.  w1 != NULL: PAIR (w0's N0 rows, then w1's N - N0);
+// gate != NULL: SWIGLU_BWD (dx_out is [T, 2K] = [dgate | dup]).
+int dx_run(const void *dy, int dtype, int64_t T, int64_t N, const stratum_nf4_weight &w0, const stratum_nf4_weight *w1,
+           int64_t N0, const float *code16, int64_t K, const void *lora_dyb, const void *lora_a, int r, void *dx_out,
+           const void *gate, const void *up, void *stream, const char *what) {
+    const bool pair = w1 != nullptr, swiglu = gate != nullptr;
+    STRATUM_REQUIRE(T >= 0 && N >= 0 && K >= 0, "%s: negative size", what);
+    if (T == 0 || K == 0) return STRATUM_OK;
+    STRATUM_REQUIRE(dy && w0.packed && code16 && dx_out && (!pair || w1->packed), "%s: null pointer", what);
+    if (dtype != STRATUM_BF16 && dtype != STRATUM_F16) return fail(STRATUM_ERR_UNSUPPORTED, "%s: dy must be bf16 or fp16", what);
+    if (K % 64 != 0) return fail(STRATUM_ERR_UNSUPPORTED, "%s: K=%lld must be a multiple of 64", what, (long long)K);
+    if (N % 8 != 0 || N == 0)
+        return fail(STRATUM_ERR_UNSUPPORTED, "%s: N=%lld must be a positive multiple of 8", what, (long long)N);
+    const bool dq = w0.absmax == nullptr;
+    STRATUM_REQUIRE(!dq || (w0.absmax_q && w0.absmax2 && w0.code2 && w0.offset), "%s: need absmax or the double-quant "
+                                                                                 "set", what);
+    if (pair) {
+        STRATUM_REQUIRE((w1->absmax == nullptr) == dq, "%s: both weights must be plain or both double quantized", what);
+        STRATUM_REQUIRE(!dq || (w1->absmax_q && w1->absmax2 && w1->offset && w1->code2),
+                        "%s: the second weight needs its double-quant set", what);
+    }
+    STRATUM_REQUIRE(r >= 0 && r <= 256, "%s: lora rank %d out of range", what, r);
+    STRATUM_REQUIRE(r == 0 || (lora_dyb && lora_a), "%s: lora needs dyb and A", what);
+    auto a16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+    STRATUM_REQUIRE(a16(dy) && a16(w0.packed) && (!pair || a16(w1->packed)) && (r == 0 || a16(lora_a)),
+                    "%s: dy, packed and lora_A must be 16-byte aligned", what);
+    STRATUM_REQUIRE(!swiglu || (up && a16(gate) && a16(up) && a16(dx_out)),
+                    "%s: gate, up and dgate_up must be 16-byte aligned", what);
+    STRATUM_BIND_STREAM(stream);
+    int *status = status_ptr();
+    if (!status) return fail(STRATUM_ERR_CUDA, "%s: no status word", what);
+    const bool bf16 = dtype == STRATUM_BF16;
+    const CUtensorMapDataType xdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap mdy, mw, mw2, mdyb, mdx;
+    int rc = make_map_2d(&mdy, xdt, dy, uint64_t(N), uint64_t(T), uint64_t(N) * 2, dx::BK, dx::BN,
+                         CU_TENSOR_MAP_SWIZZLE_128B, what);
+    if (rc) return rc;
+    // packed W viewed as [rows][K/2 bytes]; box 64 bytes (128 columns) x 64 rows, 64-byte swizzle
+    const int64_t rows0 = pair ? N0 : N;
+    rc = make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w0.packed, uint64_t(K / 2), uint64_t(rows0), uint64_t(K / 2),
+                     64, dx::BK, CU_TENSOR_MAP_SWIZZLE_64B, what);
+    if (rc) return rc;
+    mw2 = mw;
+    if (pair) {
+        rc = make_map_2d(&mw2, CU_TENSOR_MAP_DATA_TYPE_UINT8, w1->packed, uint64_t(K / 2), uint64_t(N - N0),
+                         uint64_t(K / 2), 64, dx::BK, CU_TENSOR_MAP_SWIZZLE_64B, what);
+        if (rc) return rc;
+    }
+    const int lora_chunks = (r + 63) / 64;
+    if (r > 0) {
+        STRATUM_REQUIRE(a16(lora_dyb), "%s: dyb must be 16-byte aligned", what);
+        rc = make_map_2d(&mdyb, xdt, lora_dyb, uint64_t(lora_chunks * 64), uint64_t(T), uint64_t(lora_chunks * 64) * 2,
+                         64, dx::BN, CU_TENSOR_MAP_SWIZZLE_128B, what);
+        if (rc) return rc;
+    } else {
+        mdyb = mdy;
+    }
+    dx::Params p{};
+    p.w = WeightScales{w0.absmax, w0.absmax_q, w0.absmax2, w0.code2, w0.offset};
+    if (pair) p.w1 = WeightScales{w1->absmax, w1->absmax_q, w1->absmax2, w1->code2, w1->offset};
+    p.code16 = code16;
+    p.lora_a = static_cast<const uint16_t *>(lora_a);
+    p.r = r;
+    p.lora_chunks = lora_chunks;
+    p.dx = static_cast<uint16_t *>(dx_out);
+    p.gate = static_cast<const uint16_t *>(gate);
+    p.up = static_cast<const uint16_t *>(up);
+    p.T = T; p.N = N; p.K = K;
+    p.nkw0 = pair ? int(N0 / dx::BK) : 0;
+    p.k_tiles = int((K + dx::BM - 1) / dx::BM);
+    p.t_tiles = int((T + dx::BN - 1) / dx::BN);
+    p.status = status;
+    p.tma_store = !swiglu && a16(dx_out);
+    mdx = mdy;
+    if (p.tma_store) {
+        rc = make_map_2d(&mdx, xdt, dx_out, uint64_t(K), uint64_t(T), uint64_t(K) * 2, 64, dx::BN,
+                         CU_TENSOR_MAP_SWIZZLE_128B, what);
+        if (rc) return rc;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define STRATUM_DX(B, D) \
+    (pair ? launch_dx<B, D, true, false>(mdy, mw, mw2, mdyb, mdx, p, st) \
+          : swiglu ? launch_dx<B, D, false, true>(mdy, mw, mw2, mdyb, mdx, p, st) \
+                   : launch_dx<B, D, false, false>(mdy, mw, mw2, mdyb, mdx, p, st))
+    if (bf16) return dq ? STRATUM_DX(true, true) : STRATUM_DX(true, false);
+    return dq ? STRATUM_DX(false, true) : STRATUM_DX(false, false);
+#undef STRATUM_DX
 }
 
 }  // namespace gemm
@@ -872,11 +1074,7 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
         mxa = mx;
     }
     gemm::FwdParams p{};
-    p.absmax = absmax;
-    p.absmax_q = absmax_q;
-    p.absmax2 = absmax2;
-    p.code2 = code2;
-    p.offset = offset;
+    p.w = gemm::WeightScales{absmax, absmax_q, absmax2, code2, offset};
     p.code16 = code16;
     p.bias = bias;
     p.bias_dtype = bias_dtype;
@@ -898,73 +1096,120 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
         if (rc) return rc;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (bf16) return dq ? gemm::launch_fwd<true, true>(mx, mw, mxa, my, p, st) : gemm::launch_fwd<true, false>(mx, mw, mxa, my, p, st);
-    return dq ? gemm::launch_fwd<false, true>(mx, mw, mxa, my, p, st) : gemm::launch_fwd<false, false>(mx, mw, mxa, my, p, st);
+    if (bf16)
+        return dq ? gemm::launch_fwd<true, true, false>(mx, mw, mw, mxa, my, p, st)
+                  : gemm::launch_fwd<true, false, false>(mx, mw, mw, mxa, my, p, st);
+    return dq ? gemm::launch_fwd<false, true, false>(mx, mw, mw, mxa, my, p, st)
+              : gemm::launch_fwd<false, false, false>(mx, mw, mw, mxa, my, p, st);
+}
+
+int stratum_nf4_gemm_swiglu_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const stratum_nf4_weight *gate,
+                                const stratum_nf4_weight *up, const float *code16, int64_t I, const void *lora_xa,
+                                const void *lora_b_gate, const void *lora_b_up, int r, void *h, void *gate_out,
+                                void *up_out, void *stream) {
+    STRATUM_REQUIRE(T >= 0 && I >= 0 && K >= 0, "nf4_gemm_swiglu_fwd: negative size");
+    if (T == 0 || I == 0) return STRATUM_OK;
+    STRATUM_REQUIRE(x && gate && up && gate->packed && up->packed && code16 && h, "nf4_gemm_swiglu_fwd: null pointer");
+    if (x_dtype != STRATUM_BF16 && x_dtype != STRATUM_F16)
+        return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_swiglu_fwd: x must be bf16 or fp16");
+    if (K % gemm::BK != 0 || K == 0)
+        return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_swiglu_fwd: K=%lld must be a positive multiple of 64",
+                    (long long)K);
+    if (I % 64 != 0)
+        return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_swiglu_fwd: I=%lld must be a multiple of 64", (long long)I);
+    const bool dq = gate->absmax == nullptr;
+    STRATUM_REQUIRE((up->absmax == nullptr) == dq, "nf4_gemm_swiglu_fwd: gate and up must both be plain or both "
+                                                   "double quantized");
+    STRATUM_REQUIRE(!dq || (gate->absmax_q && gate->absmax2 && gate->code2 && gate->offset && up->absmax_q &&
+                            up->absmax2 && up->code2 && up->offset),
+                    "nf4_gemm_swiglu_fwd: need absmax or the double-quant set for both weights");
+    STRATUM_REQUIRE(r >= 0 && r <= 256 && r % 2 == 0, "nf4_gemm_swiglu_fwd: lora rank %d must be even, <= 256", r);
+    STRATUM_REQUIRE(r == 0 || (lora_xa && lora_b_gate && lora_b_up), "nf4_gemm_swiglu_fwd: lora needs xa and both B");
+    auto a16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+    STRATUM_REQUIRE(a16(x) && a16(gate->packed) && a16(up->packed) && a16(h) && a16(gate_out) && a16(up_out),
+                    "nf4_gemm_swiglu_fwd: x, packed and the outputs must be 16-byte aligned");
+    STRATUM_REQUIRE(T <= (int64_t(1) << 31) && I <= (int64_t(1) << 30), "nf4_gemm_swiglu_fwd: size too large");
+    STRATUM_BIND_STREAM(stream);
+    int *status = gemm::status_ptr();
+    if (!status) return fail(STRATUM_ERR_CUDA, "nf4_gemm_swiglu_fwd: no status word");
+
+    const bool bf16 = x_dtype == STRATUM_BF16;
+    const CUtensorMapDataType xdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap mx, mw, mw2, mxa;
+    int rc = gemm::make_map_2d(&mx, xdt, x, uint64_t(K), uint64_t(T), uint64_t(K) * 2, gemm::BK, gemm::BN,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_swiglu_fwd x");
+    if (rc) return rc;
+    // each weight contributes 64 rows per tile: boxes of 32 bytes x 64 rows
+    rc = gemm::make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, gate->packed, uint64_t(K / 2), uint64_t(I),
+                           uint64_t(K / 2), gemm::BK / 2, 64, CU_TENSOR_MAP_SWIZZLE_32B, "nf4_gemm_swiglu_fwd gate");
+    if (rc) return rc;
+    rc = gemm::make_map_2d(&mw2, CU_TENSOR_MAP_DATA_TYPE_UINT8, up->packed, uint64_t(K / 2), uint64_t(I),
+                           uint64_t(K / 2), gemm::BK / 2, 64, CU_TENSOR_MAP_SWIZZLE_32B, "nf4_gemm_swiglu_fwd up");
+    if (rc) return rc;
+    const int rp = (r + gemm::BK - 1) / gemm::BK * gemm::BK;
+    const int lora_chunks = 2 * rp / gemm::BK;
+    if (r > 0) {
+        STRATUM_REQUIRE(a16(lora_xa), "nf4_gemm_swiglu_fwd: xa must be 16-byte aligned");
+        rc = gemm::make_map_2d(&mxa, xdt, lora_xa, uint64_t(2 * rp), uint64_t(T), uint64_t(2 * rp) * 2, gemm::BK,
+                               gemm::BN, CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_swiglu_fwd xa");
+        if (rc) return rc;
+    } else {
+        mxa = mx;
+    }
+    gemm::FwdParams p{};
+    p.w = gemm::WeightScales{gate->absmax, gate->absmax_q, gate->absmax2, gate->code2, gate->offset};
+    p.wu = gemm::WeightScales{up->absmax, up->absmax_q, up->absmax2, up->code2, up->offset};
+    p.code16 = code16;
+    p.lora_b = static_cast<const uint16_t *>(lora_b_gate);
+    p.lora_bu = static_cast<const uint16_t *>(lora_b_up);
+    p.r = r;
+    p.lora_rp = rp;
+    p.lora_chunks = lora_chunks;
+    p.y = static_cast<uint16_t *>(h);
+    p.gate = static_cast<uint16_t *>(gate_out);
+    p.up = static_cast<uint16_t *>(up_out);
+    p.T = T;
+    p.N = I;
+    p.K = K;
+    p.n_tiles = int(I / 64);
+    p.t_tiles = int((T + gemm::BN - 1) / gemm::BN);
+    p.status = status;
+    p.tma_store = 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (bf16)
+        return dq ? gemm::launch_fwd<true, true, true>(mx, mw, mw2, mxa, mx, p, st)
+                  : gemm::launch_fwd<true, false, true>(mx, mw, mw2, mxa, mx, p, st);
+    return dq ? gemm::launch_fwd<false, true, true>(mx, mw, mw2, mxa, mx, p, st)
+              : gemm::launch_fwd<false, false, true>(mx, mw, mw2, mxa, mx, p, st);
 }
 
 int stratum_nf4_gemm_dx(const void *dy, int dtype, int64_t T, int64_t N, const uint8_t *packed, const float *absmax,
                         const uint8_t *absmax_q, const float *absmax2, const float *code2, const float *offset,
                         const float *code16, int64_t K, const void *lora_dyb, const void *lora_a, int r, void *dx_out,
                         void *stream) {
-    STRATUM_REQUIRE(T >= 0 && N >= 0 && K >= 0, "nf4_gemm_dx: negative size");
-    if (T == 0 || K == 0) return STRATUM_OK;
-    STRATUM_REQUIRE(dy && packed && code16 && dx_out, "nf4_gemm_dx: null pointer");
-    if (dtype != STRATUM_BF16 && dtype != STRATUM_F16)
-        return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_dx: dy must be bf16 or fp16");
-    if (K % 64 != 0) return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_dx: K=%lld must be a multiple of 64", (long long)K);
-    if (N % 8 != 0 || N == 0)
-        return fail(STRATUM_ERR_UNSUPPORTED, "nf4_gemm_dx: N=%lld must be a positive multiple of 8", (long long)N);
-    const bool dq = absmax == nullptr;
-    STRATUM_REQUIRE(!dq || (absmax_q && absmax2 && code2 && offset), "nf4_gemm_dx: need absmax or the double-quant set");
-    STRATUM_REQUIRE(r >= 0 && r <= 256, "nf4_gemm_dx: lora rank %d out of range", r);
-    STRATUM_REQUIRE(r == 0 || (lora_dyb && lora_a), "nf4_gemm_dx: lora needs dyb and A");
-    STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(dy) % 16 == 0 && reinterpret_cast<uintptr_t>(packed) % 16 == 0 &&
-                        (r == 0 || reinterpret_cast<uintptr_t>(lora_a) % 16 == 0),
-                    "nf4_gemm_dx: dy, packed and lora_A must be 16-byte aligned");
-    STRATUM_BIND_STREAM(stream);
-    int *status = gemm::status_ptr();
-    if (!status) return fail(STRATUM_ERR_CUDA, "nf4_gemm_dx: no status word");
-    const bool bf16 = dtype == STRATUM_BF16;
-    const CUtensorMapDataType xdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUtensorMap mdy, mw, mdyb, mdx;
-    int rc = gemm::make_map_2d(&mdy, xdt, dy, uint64_t(N), uint64_t(T), uint64_t(N) * 2, gemm::dx::BK, gemm::dx::BN,
-                               CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_dx dy");
-    if (rc) return rc;
-    // packed W viewed as [N rows][K/2 bytes]; box 64 bytes (128 columns) x 64 rows, 64-byte swizzle
-    rc = gemm::make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, uint64_t(K / 2), uint64_t(N), uint64_t(K / 2), 64,
-                           gemm::dx::BK, CU_TENSOR_MAP_SWIZZLE_64B, "nf4_gemm_dx packed");
-    if (rc) return rc;
-    const int lora_chunks = (r + 63) / 64;
-    if (r > 0) {
-        STRATUM_REQUIRE(reinterpret_cast<uintptr_t>(lora_dyb) % 16 == 0, "nf4_gemm_dx: dyb must be 16-byte aligned");
-        rc = gemm::make_map_2d(&mdyb, xdt, lora_dyb, uint64_t(lora_chunks * 64), uint64_t(T),
-                               uint64_t(lora_chunks * 64) * 2, 64, gemm::dx::BN, CU_TENSOR_MAP_SWIZZLE_128B,
-                               "nf4_gemm_dx dyb");
-        if (rc) return rc;
-    } else {
-        mdyb = mdy;
-    }
-    gemm::dx::Params p{};
-    p.absmax = absmax; p.absmax_q = absmax_q; p.absmax2 = absmax2; p.code2 = code2; p.offset = offset;
-    p.code16 = code16;
-    p.lora_a = static_cast<const uint16_t *>(lora_a);
-    p.r = r;
-    p.lora_chunks = lora_chunks;
-    p.dx = static_cast<uint16_t *>(dx_out);
-    p.T = T; p.N = N; p.K = K;
-    p.k_tiles = int((K + gemm::dx::BM - 1) / gemm::dx::BM);
-    p.t_tiles = int((T + gemm::dx::BN - 1) / gemm::dx::BN);
-    p.status = status;
-    p.tma_store = reinterpret_cast<uintptr_t>(dx_out) % 16 == 0;
-    mdx = mdy;
-    if (p.tma_store) {
-        rc = gemm::make_map_2d(&mdx, xdt, dx_out, uint64_t(K), uint64_t(T), uint64_t(K) * 2, 64, gemm::dx::BN,
-                               CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_dx dx");
-        if (rc) return rc;
-    }
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (bf16) return dq ? gemm::launch_dx<true, true>(mdy, mw, mdyb, mdx, p, st) : gemm::launch_dx<true, false>(mdy, mw, mdyb, mdx, p, st);
-    return dq ? gemm::launch_dx<false, true>(mdy, mw, mdyb, mdx, p, st) : gemm::launch_dx<false, false>(mdy, mw, mdyb, mdx, p, st);
+    const stratum_nf4_weight w{packed, absmax, absmax_q, absmax2, code2, offset};
+    return gemm::dx_run(dy, dtype, T, N, w, nullptr, 0, code16, K, lora_dyb, lora_a, r, dx_out, nullptr, nullptr,
+                        stream, "nf4_gemm_dx");
+}
+
+int stratum_nf4_gemm_dx_pair(const void *dy, int dtype, int64_t T, const stratum_nf4_weight *w0, int64_t N0,
+                             const stratum_nf4_weight *w1, int64_t N1, const float *code16, int64_t K,
+                             const void *lora_dyb, const void *lora_a, int r, void *dx_out, void *stream) {
+    STRATUM_REQUIRE(w0 && w1, "nf4_gemm_dx_pair: null weight");
+    STRATUM_REQUIRE(N0 > 0 && N1 > 0 && N0 % 64 == 0 && N1 % 64 == 0,
+                    "nf4_gemm_dx_pair: N0=%lld and N1=%lld must be positive multiples of 64", (long long)N0,
+                    (long long)N1);
+    return gemm::dx_run(dy, dtype, T, N0 + N1, *w0, w1, N0, code16, K, lora_dyb, lora_a, r, dx_out, nullptr, nullptr,
+                        stream, "nf4_gemm_dx_pair");
+}
+
+int stratum_nf4_gemm_dx_swiglu(const void *dy, int dtype, int64_t T, int64_t N, const stratum_nf4_weight *w,
+                               const float *code16, int64_t I, const void *lora_dyb, const void *lora_a, int r,
+                               const void *gate, const void *up, void *dgate_up, void *stream) {
+    STRATUM_REQUIRE(w, "nf4_gemm_dx_swiglu: null weight");
+    STRATUM_REQUIRE(T == 0 || I == 0 || (gate && up), "nf4_gemm_dx_swiglu: gate and up are required");
+    return gemm::dx_run(dy, dtype, T, N, *w, nullptr, 0, code16, I, lora_dyb, lora_a, r, dgate_up, gate, up, stream,
+                        "nf4_gemm_dx_swiglu");
 }
 
 }  // extern "C"

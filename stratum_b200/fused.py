@@ -105,15 +105,127 @@ def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return _SwiGLUFn.apply(gate, up)
 
 
-class FusedMLP(nn.Module):
-    """``down(swiglu(gate(x), up(x)))`` (LlamaMLP / Qwen3MLP with SiLU)."""
+class _SwiGLUMLPFn(torch.autograd.Function):
+    """The whole NF4 SwiGLU MLP with LoRA in three fused kernels:
 
-    def __init__(self, gate_proj: nn.Module, up_proj: nn.Module, down_proj: nn.Module):
+    forward   gate|up GEMM with the SwiGLU epilogue (h, plus 16-bit gate / up kept),
+              then the down GEMM;
+    backward  the down projection's input-gradient GEMM with the SwiGLU backward in
+              its epilogue ([dgate | dup], dh never stored), then one input-gradient
+              pass through the stacked gate / up weights.
+    LoRA terms ride in the same accumulators (extra K chunks); dA / dB are small
+    cuBLAS GEMMs as in NF4Linear."""
+
+    @staticmethod
+    def forward(ctx, x, Ag, Bg, Au, Bu, Ad, Bd, mods):
+        from . import ops
+
+        gate, up, down = mods
+        H = x.shape[-1]
+        x2 = x.reshape(-1, H)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        gw = (gate.quantized, gate.quant_state)
+        uw = (up.quantized, up.quant_state)
+        dw = (down.quantized, down.quant_state)
+        xa = ops.mlp_lora_down(x2, Ag, Au, gate.scaling, up.scaling) if Ag is not None else None
+        h, g, u = ops.nf4_swiglu_fwd(x2, gw, uw, xa, Bg, Bu, keep_gate_up=True)
+        xad = ops.lora_down(h, Ad.to(h.dtype), down.scaling) if Ad is not None else None
+        y = ops.nf4_gemm_fwd(h, dw[0], dw[1], lora_A=Ad, lora_B=Bd, scaling=down.scaling, xa=xad)
+        ctx.weights = (gw, uw, dw)
+        ctx.scales = (gate.scaling, up.scaling, down.scaling)
+        ctx.shape = x.shape
+        ctx.save_for_backward(x2, xa, g, u, h, xad, Ag, Bg, Au, Bu, Ad, Bd)
+        return y.reshape(*x.shape[:-1], y.shape[-1])
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import ops
+
+        x2, xa, g, u, h, xad, Ag, Bg, Au, Bu, Ad, Bd = ctx.saved_tensors
+        gw, uw, dw = ctx.weights
+        sg, su, sd = ctx.scales
+        Hout = dy.shape[-1]
+        dy2 = dy.reshape(-1, Hout)
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        I = g.shape[-1]
+        grads = [None] * 6
+        dyb_d = None
+        if Ad is not None:
+            rd = Ad.shape[0]
+            dyb_d = ops.lora_down(dy2, Bd.t().to(dy2.dtype), sd)
+            grads[4] = (dyb_d[:, :rd].t() @ h).to(Ad.dtype)
+            grads[5] = (dy2.t() @ xad[:, :rd]).to(Bd.dtype)
+        dgu = ops.nf4_gemm_dx_swiglu(dy2, dw, g, u, dyb_d, Ad)
+        dg, du = dgu[:, :I], dgu[:, I:]
+        dyb = A_cat = None
+        if Ag is not None:
+            r = Ag.shape[0]
+            rp = xa.shape[1] // 2
+            dyb = torch.zeros((dy2.shape[0], 2 * rp), dtype=dy2.dtype, device=dy2.device)
+            dyb[:, :r] = ops.scaled_matmul(dg, Bg.to(dy2.dtype), sg)
+            dyb[:, rp:rp + r] = ops.scaled_matmul(du, Bu.to(dy2.dtype), su)
+            A_cat = torch.zeros((2 * rp, x2.shape[1]), dtype=dy2.dtype, device=dy2.device)
+            A_cat[:r] = Ag
+            A_cat[rp:rp + r] = Au
+            grads[0] = (dyb[:, :r].t() @ x2).to(Ag.dtype)
+            grads[1] = (dg.t() @ xa[:, :r]).to(Bg.dtype)
+            grads[2] = (dyb[:, rp:rp + r].t() @ x2).to(Au.dtype)
+            grads[3] = (du.t() @ xa[:, rp:rp + r]).to(Bu.dtype)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = ops.nf4_gemm_dx_pair(dgu, gw, uw, dyb, A_cat).reshape(ctx.shape)
+        return (dx, *grads, None)
+
+
+def _fusable(gate, up, down, x: torch.Tensor) -> bool:
+    """Whether the three projections can run as the fused SwiGLU MLP kernels."""
+    from .nf4_linear import NF4Linear
+
+    mods = (gate, up, down)
+    if not all(isinstance(m, NF4Linear) and m.quantized is not None and m.bias is None for m in mods):
+        return False
+    if x.dtype not in (torch.bfloat16, torch.float16) or x.device.type != "cuda":
+        return False
+    gq, uq, dq = gate.quant_state, up.quant_state, down.quant_state
+    if any(q.blocksize != 64 or len(q.shape) != 2 for q in (gq, uq, dq)):
+        return False
+    I, H = int(gq.shape[0]), int(gq.shape[1])
+    if tuple(uq.shape) != (I, H) or tuple(dq.shape) != (H, I) or I % 64 or H % 64:
+        return False
+    if bool(gq.nested) != bool(uq.nested):
+        return False
+    if (gate.lora_A is None) != (up.lora_A is None):
+        return False
+    if gate.lora_A is not None:
+        r = gate.lora_A.shape[0]
+        if r % 2 or up.lora_A.shape[0] != r or r > 128:
+            return False
+    if down.lora_A is not None and down.lora_A.shape[0] > 256:
+        return False
+    return True
+
+
+class FusedMLP(nn.Module):
+    """``down(swiglu(gate(x), up(x)))`` (LlamaMLP / Qwen3MLP with SiLU).
+
+    With NF4Linear projections (blocksize 64, no bias, intermediate size a multiple
+    of 64, gate and up LoRA of one even rank) the MLP runs as three fused kernels
+    (``_SwiGLUMLPFn``), the dense counterpart of the reference's fused frozen MLP
+    (stratum/model/mlp_opt.py:154-245); otherwise as the three NF4Linears around
+    one SwiGLU kernel."""
+
+    def __init__(self, gate_proj: nn.Module, up_proj: nn.Module, down_proj: nn.Module, fuse: bool = True):
         super().__init__()
         self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
+        self.fuse = fuse
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.down_proj(swiglu(self.gate_proj(x), self.up_proj(x)))
+        g, u, d = self.gate_proj, self.up_proj, self.down_proj
+        if self.fuse and _fusable(g, u, d, x):
+            return _SwiGLUMLPFn.apply(x, g.lora_A, g.lora_B, u.lora_A, u.lora_B, d.lora_A, d.lora_B, (g, u, d))
+        return d(swiglu(g(x), u(x)))
 
 
 class _HeadsFn(torch.autograd.Function):

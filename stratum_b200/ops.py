@@ -171,6 +171,157 @@ def nf4_gemm_dx(
 
 
 # --------------------------------------------------------------------------------
+# fused SwiGLU MLP (dense): one gate|up GEMM with the SwiGLU epilogue, and the
+# matching input gradients
+# --------------------------------------------------------------------------------
+
+def _nf4_weight(packed: torch.Tensor, qs: QuantState, dev: torch.device, keep: list) -> "_lib.NF4Weight":
+    absmax, absmax_q, absmax2, code2, offset, code16 = _weight_args(qs, dev)
+    keep += [t for t in (packed, absmax, absmax_q, absmax2, code2, offset, code16) if t is not None]
+    w = _lib.NF4Weight()
+    w.packed = packed.data_ptr()
+    w.absmax = 0 if absmax is None else absmax.data_ptr()
+    w.absmax_q = 0 if absmax_q is None else absmax_q.data_ptr()
+    w.absmax2 = 0 if absmax2 is None else absmax2.data_ptr()
+    w.code2 = 0 if code2 is None else code2.data_ptr()
+    w.offset = 0 if offset is None else offset.data_ptr()
+    return w
+
+
+def _addr(w) -> "ctypes.c_void_p":
+    import ctypes
+
+    return ctypes.c_void_p(ctypes.addressof(w))
+
+
+def mlp_lora_down(x2: torch.Tensor, A_gate: torch.Tensor, A_up: torch.Tensor, s_gate: float,
+                  s_up: float) -> torch.Tensor:
+    """xa = [s_gate x A_gate^T | 0 | s_up x A_up^T | 0] with each half ceil(r/64)*64 wide."""
+    r = int(A_gate.shape[0])
+    rp = -(-r // LORA_CHUNK) * LORA_CHUNK
+    xa = torch.zeros((x2.shape[0], 2 * rp), dtype=x2.dtype, device=x2.device)
+    for c0, A, s in ((0, A_gate, s_gate), (rp, A_up, s_up)):
+        xa[:, c0:c0 + r] = scaled_matmul(x2, A.to(x2.dtype).t(), s)
+    return xa
+
+
+def scaled_matmul(a: torch.Tensor, b: torch.Tensor, s: float) -> torch.Tensor:
+    """s * (a @ b) with the scale applied in cuBLAS's fp32 epilogue (one rounding)."""
+    if s == 1.0:
+        return torch.matmul(a, b)
+    return torch.addmm(torch.empty((a.shape[0], b.shape[1]), dtype=a.dtype, device=a.device), a, b, beta=0, alpha=s)
+
+
+def nf4_swiglu_fwd(x: torch.Tensor, gate: tuple, up: tuple, xa: Optional[torch.Tensor] = None,
+                   lora_B_gate: Optional[torch.Tensor] = None, lora_B_up: Optional[torch.Tensor] = None,
+                   keep_gate_up: bool = True):
+    """h = silu(x Wg^T + LoRA_g) * (x Wu^T + LoRA_u) with HF's bf16 roundings, one fused kernel.
+
+    ``gate`` / ``up``: ``(packed, QuantState)`` of two NF4 weights [I, K] (blocksize 64,
+    I % 64 == 0); ``xa`` from :func:`mlp_lora_down` with the LoRA B matrices [I, r].
+    Returns ``(h, gate_out, up_out)`` ([rows, I]; the last two None unless kept)."""
+    _lib.require_cuda(x, "nf4_swiglu_fwd")
+    (gp, gqs), (upk, uqs) = gate, up
+    I, K = int(gqs.shape[0]), int(gqs.shape[1])
+    if tuple(uqs.shape) != (I, K) or gqs.blocksize != 64 or uqs.blocksize != 64:
+        raise ValueError("nf4_swiglu_fwd: gate and up must be [I, K] NF4 weights with blocksize 64")
+    dev = x.device
+    x2 = x.reshape(-1, K)
+    if not x2.is_contiguous() or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    T = x2.shape[0]
+    h = torch.empty((T, I), dtype=x.dtype, device=dev)
+    g_out = torch.empty((T, I), dtype=x.dtype, device=dev) if keep_gate_up else None
+    u_out = torch.empty((T, I), dtype=x.dtype, device=dev) if keep_gate_up else None
+    r = 0
+    lbg = lbu = None
+    if lora_B_gate is not None:
+        r = int(lora_B_gate.shape[1])
+        if r % 2:
+            raise ValueError("nf4_swiglu_fwd: the LoRA rank must be even")
+        lbg = lora_B_gate.to(x.dtype).contiguous()
+        lbu = lora_B_up.to(x.dtype).contiguous()
+    keep: list = []
+    wg = _nf4_weight(gp, gqs, dev, keep)
+    wu = _nf4_weight(upk, uqs, dev, keep)
+    code16 = keep[-1]
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.stratum_nf4_gemm_swiglu_fwd(
+            _lib.ptr(x2), _lib.DTYPE_CODE[x.dtype], T, K, _addr(wg), _addr(wu), _lib.ptr(code16), I, _lib.ptr(xa),
+            _lib.ptr(lbg), _lib.ptr(lbu), r, _lib.ptr(h), _lib.ptr(g_out), _lib.ptr(u_out), _lib.stream_of(dev)),
+            "nf4_swiglu_fwd")
+    shp = x.shape[:-1]
+    return (h.reshape(*shp, I), None if g_out is None else g_out.reshape(*shp, I),
+            None if u_out is None else u_out.reshape(*shp, I))
+
+
+def nf4_gemm_dx_swiglu(dy: torch.Tensor, down: tuple, gate_out: torch.Tensor, up_out: torch.Tensor,
+                       dyb: Optional[torch.Tensor] = None, lora_A: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[dgate | dup] ([rows, 2I]) of a SwiGLU MLP from the down projection's output gradient:
+    dh = dy Wd + dyb lora_A (never stored), then the SwiGLU backward with the forward's
+    16-bit gate and up -- the down projection's input-gradient kernel with that epilogue."""
+    _lib.require_cuda(dy, "nf4_gemm_dx_swiglu")
+    packed, qs = down
+    N, I = int(qs.shape[0]), int(qs.shape[1])
+    dev = dy.device
+    dy2 = dy.reshape(-1, N)
+    if not dy2.is_contiguous() or dy2.data_ptr() % 16:
+        dy2 = dy2.contiguous()
+    T = dy2.shape[0]
+    g2 = gate_out.reshape(T, I).contiguous()
+    u2 = up_out.reshape(T, I).contiguous()
+    out = torch.empty((T, 2 * I), dtype=dy.dtype, device=dev)
+    r = 0
+    la = None
+    if lora_A is not None:
+        r = int(lora_A.shape[0])
+        la = lora_A.to(dy.dtype).contiguous()
+    keep: list = []
+    w = _nf4_weight(packed, qs, dev, keep)
+    code16 = keep[-1]
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.stratum_nf4_gemm_dx_swiglu(
+            _lib.ptr(dy2), _lib.DTYPE_CODE[dy.dtype], T, N, _addr(w), _lib.ptr(code16), I, _lib.ptr(dyb), _lib.ptr(la),
+            r, _lib.ptr(g2), _lib.ptr(u2), _lib.ptr(out), _lib.stream_of(dev)), "nf4_gemm_dx_swiglu")
+    return out
+
+
+def nf4_gemm_dx_pair(dy: torch.Tensor, w0: tuple, w1: tuple, dyb: Optional[torch.Tensor] = None,
+                     lora_A: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """dx = dy [W0; W1] + dyb lora_A for two NF4 weights stacked along their rows
+    (dy [rows, N0 + N1]), one fused input-gradient pass."""
+    _lib.require_cuda(dy, "nf4_gemm_dx_pair")
+    (p0, q0), (p1, q1) = w0, w1
+    N0, K = int(q0.shape[0]), int(q0.shape[1])
+    N1 = int(q1.shape[0])
+    if int(q1.shape[1]) != K:
+        raise ValueError("nf4_gemm_dx_pair: the weights need the same number of columns")
+    dev = dy.device
+    dy2 = dy.reshape(-1, N0 + N1)
+    if not dy2.is_contiguous() or dy2.data_ptr() % 16:
+        dy2 = dy2.contiguous()
+    T = dy2.shape[0]
+    dx = torch.empty((T, K), dtype=dy.dtype, device=dev)
+    r = 0
+    la = None
+    if lora_A is not None:
+        r = int(lora_A.shape[0])
+        la = lora_A.to(dy.dtype).contiguous()
+    keep: list = []
+    a = _nf4_weight(p0, q0, dev, keep)
+    b = _nf4_weight(p1, q1, dev, keep)
+    code16 = keep[-1]
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.stratum_nf4_gemm_dx_pair(
+            _lib.ptr(dy2), _lib.DTYPE_CODE[dy.dtype], T, _addr(a), N0, _addr(b), N1, _lib.ptr(code16), K, _lib.ptr(dyb),
+            _lib.ptr(la), r, _lib.ptr(dx), _lib.stream_of(dev)), "nf4_gemm_dx_pair")
+    return dx.reshape(*dy.shape[:-1], K)
+
+
+# --------------------------------------------------------------------------------
 # routed experts (include/stratum_moe.h)
 # --------------------------------------------------------------------------------
 
