@@ -48,6 +48,12 @@ int stratum_swiglu_fwd(const void *gate, const void *up, int dtype, int64_t n, v
 int stratum_swiglu_bwd(const void *gate, const void *up, const void *dh, int dtype, int64_t n, void *dgate, void *dup,
                        void *stream);
 
+/* The same backward with the two gradients written side by side as rows of
+ * dgate_up[rows, 2I] = [dgate | dup] (gate, up, dh: [rows, I], I % 8 == 0): the dY
+ * of the stacked gate/up input gradient, stratum_nf4_gemm_dx_pair. */
+int stratum_swiglu_bwd_cat(const void *gate, const void *up, const void *dh, int dtype, int64_t rows, int64_t I,
+                           void *dgate_up, void *stream);
+
 /* Next-token cross entropy of one row of logits per token, forward and gradient
  * in one pass (replaces the log_softmax / nll / autograd chain of the reference's
  * chunked_linear_cross_entropy, stratum/model/chunked_loss.py):

@@ -234,19 +234,6 @@ int stratum_nf4_gemm_dx_pair(const void *dy, int dtype, int64_t T,
                              const float *code16, int64_t K, const void *lora_dyb,
                              const void *lora_a, int r, void *dx, void *stream);
 
-/* Input gradient of a SwiGLU MLP's down projection with the SwiGLU backward in
- * the epilogue: dh = dy . Wd + lora_dyb . lora_a (as stratum_nf4_gemm_dx, rounded
- * to 16 bits), then with the forward's 16-bit gate and up
- *   dup   = r16(dh * r16(silu(gate)))
- *   dgate = r16(r16(dh * up) * s * (1 + gate * (1 - s))),  s = sigmoid(gate)
- * written as dgate_up[T, 2I] = [dgate | dup] (dh itself is never stored).
- * Replaces the down_proj backward and the SiLU / multiply backward of the
- * reference's MLP (stratum/model/mlp_opt.py:154-245).  I % 64 == 0. */
-int stratum_nf4_gemm_dx_swiglu(const void *dy, int dtype, int64_t T, int64_t N,
-                               const stratum_nf4_weight *w, const float *code16, int64_t I,
-                               const void *lora_dyb, const void *lora_a, int r,
-                               const void *gate, const void *up, void *dgate_up, void *stream);
-
 #ifdef __cplusplus
 }
 #endif

@@ -51,7 +51,6 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_nf4_gemm_swiglu_fwd": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _int, _vp, _vp,
                                            _vp, _vp]),
     "stratum_nf4_gemm_dx_pair": (_int, [_vp, _int, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _int, _vp, _vp]),
-    "stratum_nf4_gemm_dx_swiglu": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     # include/stratum_moe.h
     "stratum_moe_route_workspace_bytes": (_sz, [_i64, _int]),
     "stratum_moe_route": (_int, [_vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
@@ -71,6 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_rope_from_heads": (_int, [_vp, _vp, _vp, _int, _int, _int, _int, _vp, _vp]),
     "stratum_swiglu_fwd": (_int, [_vp, _vp, _int, _i64, _vp, _vp]),
     "stratum_swiglu_bwd": (_int, [_vp, _vp, _vp, _int, _i64, _vp, _vp, _vp]),
+    "stratum_swiglu_bwd_cat": (_int, [_vp, _vp, _vp, _int, _i64, _i64, _vp, _vp]),
     "stratum_ce_fwd_grad": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
 }
 

@@ -193,6 +193,25 @@ __global__ void k_swiglu_bwd(const uint4 *__restrict__ g, const uint4 *__restric
     }
 }
 
+// The same backward for an MLP whose gate and up gradients feed one stacked
+// input-gradient GEMM: rows of [dgate | dup] (width 2I) from gate, up, dh [rows, I].
+template <bool BF16>
+__global__ void k_swiglu_bwd_cat(const uint4 *__restrict__ g, const uint4 *__restrict__ u,
+                                 const uint4 *__restrict__ dh, int64_t rows, int64_t iv, uint4 *__restrict__ dgu) {
+    const int64_t n = rows * iv;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = i / iv, c = i - r * iv;
+        float a[8], b[8], d[8], oa[8], ob[8];
+        unpack8<BF16>(g[i], a);
+        unpack8<BF16>(u[i], b);
+        unpack8<BF16>(dh[i], d);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) h16::swiglu_bwd1<BF16>(a[k], b[k], d[k], oa[k], ob[k]);
+        dgu[r * 2 * iv + c] = pack8<BF16>(oa);
+        dgu[r * 2 * iv + iv + c] = pack8<BF16>(ob);
+    }
+}
+
 // ------------------------------------------------------------ cross entropy --
 
 // Next-token cross entropy over bf16/fp16 logits, forward and gradient in one
@@ -411,6 +430,26 @@ int stratum_swiglu_fwd(const void *gate, const void *up, int dtype, int64_t n, v
         k_swiglu_fwd<false><<<grid, 256, 0, st>>>(static_cast<const uint4 *>(gate), static_cast<const uint4 *>(up), nv,
                                                   static_cast<uint4 *>(h));
     return check_launch("swiglu_fwd");
+}
+
+int stratum_swiglu_bwd_cat(const void *gate, const void *up, const void *dh, int dtype, int64_t rows, int64_t I,
+                           void *dgate_up, void *stream) {
+    STRATUM_REQUIRE(rows >= 0 && I >= 0, "swiglu_bwd_cat: bad size");
+    if (rows == 0 || I == 0) return STRATUM_OK;
+    FUSED_DTYPE_CHECK(dtype, "swiglu_bwd_cat");
+    STRATUM_REQUIRE(gate && up && dh && dgate_up, "swiglu_bwd_cat: null pointer");
+    STRATUM_REQUIRE(I % 8 == 0 && a16(gate) && a16(up) && a16(dh) && a16(dgate_up),
+                    "swiglu_bwd_cat: I % 8 and 16-byte alignment");
+    STRATUM_BIND_STREAM(stream);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t iv = I / 8;
+    const int grid = grid_for(rows * iv, 256);
+    auto G = static_cast<const uint4 *>(gate), U = static_cast<const uint4 *>(up), D = static_cast<const uint4 *>(dh);
+    if (dtype == STRATUM_BF16)
+        k_swiglu_bwd_cat<true><<<grid, 256, 0, st>>>(G, U, D, rows, iv, static_cast<uint4 *>(dgate_up));
+    else
+        k_swiglu_bwd_cat<false><<<grid, 256, 0, st>>>(G, U, D, rows, iv, static_cast<uint4 *>(dgate_up));
+    return check_launch("swiglu_bwd_cat");
 }
 
 int stratum_swiglu_bwd(const void *gate, const void *up, const void *dh, int dtype, int64_t n, void *dgate, void *dup,

@@ -55,6 +55,41 @@ __device__ __forceinline__ float swiglu_fwd1(float g, float u) {
     return rnd<BF16>(g / (1.f + expf(-g))) * u;
 }
 
+// True when fp32 v lies within `margin` fp32 ulps of a round-to-nearest-even
+// boundary of bf16 (the dropped 16 bits near 0x8000), i.e. where an error of
+// fewer than `margin` ulps in v could change its bf16 rounding.
+__device__ __forceinline__ bool near_bf16_tie(float v, int margin) {
+    const int low = int(__float_as_uint(v) & 0xFFFFu) - 0x8000;
+    return low < margin && low > -margin;
+}
+
+// h for 8 elements, the same values as swiglu_fwd1 at a third of its cost: silu
+// from the approximate exp and divide (relative error below 2^-20 for |g| <= 16:
+// ex2.approx, the rounding of g * log2(e), a rounding of 1 + e and the
+// approximate reciprocal), which rounds to the same bf16 as the exact silu
+// unless it lies within 64 ulps of a rounding boundary; those elements, and
+// |g| > 16, are recomputed exactly.  FP16 output always takes the exact path.
+template <bool BF16>
+__device__ __forceinline__ void swiglu_fwd8(const float g[8], const float u[8], float h[8]) {
+    if constexpr (!BF16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = swiglu_fwd1<BF16>(g[i], u[i]);
+    } else {
+        uint32_t redo = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float s = __fdividef(g[i], 1.f + __expf(-g[i]));
+            if (!(fabsf(g[i]) <= 16.f) || near_bf16_tie(s, 64)) redo |= 1u << i;
+            h[i] = rnd<BF16>(s) * u[i];
+        }
+        while (redo) {
+            const int i = __ffs(redo) - 1;
+            redo &= redo - 1;
+            h[i] = swiglu_fwd1<BF16>(g[i], u[i]);
+        }
+    }
+}
+
 // (dg, du) for one element from the 16-bit gate, up and dh values (as floats).
 template <bool BF16>
 __device__ __forceinline__ void swiglu_bwd1(float g, float u, float dh, float &dg, float &du) {

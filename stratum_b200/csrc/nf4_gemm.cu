@@ -440,8 +440,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                         float g[8], u[8], h[8];
                         h16::unpack8<BF16>(gv, g);
                         h16::unpack8<BF16>(uv, u);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) h[i] = h16::swiglu_fwd1<BF16>(g[i], u[i]);
+                        h16::swiglu_fwd8<BF16>(g, u, h);  // cheap on the SM the decode warps share
                         const int64_t at = (t0 + tok) * p.N + col;
                         *reinterpret_cast<uint4 *>(p.y + at) = h16::pack8<BF16>(h);
                         if (p.gate) *reinterpret_cast<uint4 *>(p.gate + at) = gv;
@@ -527,8 +526,7 @@ struct Params {
     const uint16_t *lora_a;  // [r, K] or null
     int r;
     int lora_chunks;
-    uint16_t *dx;            // [T, K] (SWIGLU_BWD: the gate / up gradients [T, 2K])
-    const uint16_t *gate, *up;  // SWIGLU_BWD: the forward's 16-bit gate and up [T, K]
+    uint16_t *dx;            // [T, K]
     int64_t T, N, K;
     int nkw0;                // PAIR: contraction steps (64 rows each) over the first weight
     int k_tiles, t_tiles;
@@ -538,10 +536,8 @@ struct Params {
 
 // PAIR: the contraction runs over two NF4 weights stacked along N (rows [0, N0)
 // from tm_w, [N0, N) from tm_w2), e.g. the gate and up projections of an MLP whose
-// dY is [dgate | dup].  SWIGLU_BWD: this is the down projection of a SwiGLU MLP;
-// the epilogue turns its dX (= dh, rounded to 16 bits) and the forward's gate /
-// up into [dgate | dup] with the SwiGLU backward, so dh never reaches HBM.
-template <bool BF16, bool DQ, bool PAIR, bool SWIGLU_BWD>
+// dY is [dgate | dup].
+template <bool BF16, bool DQ, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_w,
               const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_dyb,
@@ -742,7 +738,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
             const int64_t k0 = int64_t(tile % p.k_tiles) * BM;
             const int64_t t0 = int64_t(tile / p.k_tiles) * BN;
             const uint32_t acc = tmem + lane_addr + uint32_t(ab * 256);
-            if (SWIGLU_BWD || p.tma_store) {
+            if (p.tma_store) {
                 if (leader) bulk_wait_read0();
                 named_bar_sync(1, 128);
 #pragma unroll 1
@@ -770,38 +766,12 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                         stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
                     }
                 }
-                if constexpr (SWIGLU_BWD) {
-                    // the staged tile is dh (16-bit, as the plain kernel would store it):
-                    // with the forward's gate and up, form dgate and dup and write them as
-                    // [dgate | dup] rows of width 2K, 8 columns per 16-byte chunk
-                    named_bar_sync(1, 128);
-                    const int etid = int(threadIdx.x) - EPI_WARP0 * 32;
-                    const int ntok = int(p.T - t0 < BN ? p.T - t0 : BN);
-                    for (int idx = etid; idx < ntok * 16; idx += 128) {
-                        const int tok = idx >> 4, hc = idx & 15, half = hc >> 3, chunk = hc & 7;
-                        const int64_t k = k0 + half * 64 + chunk * 8;
-                        if (k >= p.K) continue;
-                        const uint4 dv = *reinterpret_cast<const uint4 *>(y0 + half * Y_HALF_BYTES + tok * 128 +
-                                                                          ((chunk ^ (tok & 7)) << 4));
-                        const int64_t at = (t0 + tok) * p.K + k;
-                        float g[8], u[8], dh[8], dg[8], du[8];
-                        h16::unpack8<BF16>(dv, dh);
-                        h16::unpack8<BF16>(*reinterpret_cast<const uint4 *>(p.gate + at), g);
-                        h16::unpack8<BF16>(*reinterpret_cast<const uint4 *>(p.up + at), u);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) h16::swiglu_bwd1<BF16>(g[i], u[i], dh[i], dg[i], du[i]);
-                        uint16_t *row = p.dx + (t0 + tok) * (2 * p.K);
-                        *reinterpret_cast<uint4 *>(row + k) = h16::pack8<BF16>(dg);
-                        *reinterpret_cast<uint4 *>(row + p.K + k) = h16::pack8<BF16>(du);
-                    }
-                } else {
-                    fence_proxy_async_smem();
-                    named_bar_sync(1, 128);
-                    if (leader) {
-                        tma_store_2d(&tm_dx, int32_t(k0), int32_t(t0), y0);
-                        if (k0 + 64 < p.K) tma_store_2d(&tm_dx, int32_t(k0 + 64), int32_t(t0), y0 + Y_HALF_BYTES);
-                        bulk_commit();
-                    }
+                fence_proxy_async_smem();
+                named_bar_sync(1, 128);
+                if (leader) {
+                    tma_store_2d(&tm_dx, int32_t(k0), int32_t(t0), y0);
+                    if (k0 + 64 < p.K) tma_store_2d(&tm_dx, int32_t(k0 + 64), int32_t(t0), y0 + Y_HALF_BYTES);
+                    bulk_commit();
                 }
             } else {
                 const int64_t k = k0 + q * 32 + lane;
@@ -899,10 +869,10 @@ int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &
     return check_launch(SWIGLU ? "nf4_gemm_swiglu_fwd" : "nf4_gemm_fwd");
 }
 
-template <bool BF16, bool DQ, bool PAIR, bool SWIGLU_BWD>
+template <bool BF16, bool DQ, bool PAIR>
 int launch_dx(const CUtensorMap &mdy, const CUtensorMap &mw, const CUtensorMap &mw2, const CUtensorMap &mdyb,
               const CUtensorMap &mdx, const dx::Params &p, cudaStream_t st) {
-    auto kern = dx::k_nf4_gemm_dx<BF16, DQ, PAIR, SWIGLU_BWD>;
+    auto kern = dx::k_nf4_gemm_dx<BF16, DQ, PAIR>;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -914,16 +884,15 @@ int launch_dx(const CUtensorMap &mdy, const CUtensorMap &mw, const CUtensorMap &
     const int ntiles = p.k_tiles * p.t_tiles;
     const int grid = ntiles < sm_count() ? ntiles : sm_count();
     kern<<<grid, dx::NUM_THREADS, dx::SMEM_BYTES, st>>>(mdy, mw, mw2, mdyb, mdx, p);
-    return check_launch(PAIR ? "nf4_gemm_dx_pair" : SWIGLU_BWD ? "nf4_gemm_dx_swiglu" : "nf4_gemm_dx");
+    return check_launch(PAIR ? "nf4_gemm_dx_pair" : "nf4_gemm_dx");
 }
 
 // Shared set-up of the input-gradient entry points: validation, tensor maps,
-// parameters and the launch.  w1 != NULL: PAIR (w0's N0 rows, then w1's N - N0);
-// gate != NULL: SWIGLU_BWD (dx_out is [T, 2K] = [dgate | dup]).
+// parameters and the launch.  w1 != NULL: PAIR (w0's N0 rows, then w1's N - N0).
 int dx_run(const void *dy, int dtype, int64_t T, int64_t N, const stratum_nf4_weight &w0, const stratum_nf4_weight *w1,
            int64_t N0, const float *code16, int64_t K, const void *lora_dyb, const void *lora_a, int r, void *dx_out,
-           const void *gate, const void *up, void *stream, const char *what) {
-    const bool pair = w1 != nullptr, swiglu = gate != nullptr;
+           void *stream, const char *what) {
+    const bool pair = w1 != nullptr;
     STRATUM_REQUIRE(T >= 0 && N >= 0 && K >= 0, "%s: negative size", what);
     if (T == 0 || K == 0) return STRATUM_OK;
     STRATUM_REQUIRE(dy && w0.packed && code16 && dx_out && (!pair || w1->packed), "%s: null pointer", what);
@@ -944,8 +913,6 @@ int dx_run(const void *dy, int dtype, int64_t T, int64_t N, const stratum_nf4_we
     auto a16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
     STRATUM_REQUIRE(a16(dy) && a16(w0.packed) && (!pair || a16(w1->packed)) && (r == 0 || a16(lora_a)),
                     "%s: dy, packed and lora_A must be 16-byte aligned", what);
-    STRATUM_REQUIRE(!swiglu || (up && a16(gate) && a16(up) && a16(dx_out)),
-                    "%s: gate, up and dgate_up must be 16-byte aligned", what);
     STRATUM_BIND_STREAM(stream);
     int *status = status_ptr();
     if (!status) return fail(STRATUM_ERR_CUDA, "%s: no status word", what);
@@ -983,14 +950,12 @@ int dx_run(const void *dy, int dtype, int64_t T, int64_t N, const stratum_nf4_we
     p.r = r;
     p.lora_chunks = lora_chunks;
     p.dx = static_cast<uint16_t *>(dx_out);
-    p.gate = static_cast<const uint16_t *>(gate);
-    p.up = static_cast<const uint16_t *>(up);
     p.T = T; p.N = N; p.K = K;
     p.nkw0 = pair ? int(N0 / dx::BK) : 0;
     p.k_tiles = int((K + dx::BM - 1) / dx::BM);
     p.t_tiles = int((T + dx::BN - 1) / dx::BN);
     p.status = status;
-    p.tma_store = !swiglu && a16(dx_out);
+    p.tma_store = a16(dx_out);
     mdx = mdy;
     if (p.tma_store) {
         rc = make_map_2d(&mdx, xdt, dx_out, uint64_t(K), uint64_t(T), uint64_t(K) * 2, 64, dx::BN,
@@ -999,9 +964,7 @@ int dx_run(const void *dy, int dtype, int64_t T, int64_t N, const stratum_nf4_we
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define STRATUM_DX(B, D) \
-    (pair ? launch_dx<B, D, true, false>(mdy, mw, mw2, mdyb, mdx, p, st) \
-          : swiglu ? launch_dx<B, D, false, true>(mdy, mw, mw2, mdyb, mdx, p, st) \
-                   : launch_dx<B, D, false, false>(mdy, mw, mw2, mdyb, mdx, p, st))
+    (pair ? launch_dx<B, D, true>(mdy, mw, mw2, mdyb, mdx, p, st) : launch_dx<B, D, false>(mdy, mw, mw2, mdyb, mdx, p, st))
     if (bf16) return dq ? STRATUM_DX(true, true) : STRATUM_DX(true, false);
     return dq ? STRATUM_DX(false, true) : STRATUM_DX(false, false);
 #undef STRATUM_DX
@@ -1188,8 +1151,8 @@ int stratum_nf4_gemm_dx(const void *dy, int dtype, int64_t T, int64_t N, const u
                         const float *code16, int64_t K, const void *lora_dyb, const void *lora_a, int r, void *dx_out,
                         void *stream) {
     const stratum_nf4_weight w{packed, absmax, absmax_q, absmax2, code2, offset};
-    return gemm::dx_run(dy, dtype, T, N, w, nullptr, 0, code16, K, lora_dyb, lora_a, r, dx_out, nullptr, nullptr,
-                        stream, "nf4_gemm_dx");
+    return gemm::dx_run(dy, dtype, T, N, w, nullptr, 0, code16, K, lora_dyb, lora_a, r, dx_out, stream,
+                        "nf4_gemm_dx");
 }
 
 int stratum_nf4_gemm_dx_pair(const void *dy, int dtype, int64_t T, const stratum_nf4_weight *w0, int64_t N0,
@@ -1199,17 +1162,8 @@ int stratum_nf4_gemm_dx_pair(const void *dy, int dtype, int64_t T, const stratum
     STRATUM_REQUIRE(N0 > 0 && N1 > 0 && N0 % 64 == 0 && N1 % 64 == 0,
                     "nf4_gemm_dx_pair: N0=%lld and N1=%lld must be positive multiples of 64", (long long)N0,
                     (long long)N1);
-    return gemm::dx_run(dy, dtype, T, N0 + N1, *w0, w1, N0, code16, K, lora_dyb, lora_a, r, dx_out, nullptr, nullptr,
-                        stream, "nf4_gemm_dx_pair");
-}
-
-int stratum_nf4_gemm_dx_swiglu(const void *dy, int dtype, int64_t T, int64_t N, const stratum_nf4_weight *w,
-                               const float *code16, int64_t I, const void *lora_dyb, const void *lora_a, int r,
-                               const void *gate, const void *up, void *dgate_up, void *stream) {
-    STRATUM_REQUIRE(w, "nf4_gemm_dx_swiglu: null weight");
-    STRATUM_REQUIRE(T == 0 || I == 0 || (gate && up), "nf4_gemm_dx_swiglu: gate and up are required");
-    return gemm::dx_run(dy, dtype, T, N, *w, nullptr, 0, code16, I, lora_dyb, lora_a, r, dgate_up, gate, up, stream,
-                        "nf4_gemm_dx_swiglu");
+    return gemm::dx_run(dy, dtype, T, N0 + N1, *w0, w1, N0, code16, K, lora_dyb, lora_a, r, dx_out, stream,
+                        "nf4_gemm_dx_pair");
 }
 
 }  // extern "C"

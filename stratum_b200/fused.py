@@ -99,6 +99,17 @@ class _SwiGLUFn(torch.autograd.Function):
         return dg, du
 
 
+def swiglu_backward_cat(gate: torch.Tensor, up: torch.Tensor, dh: torch.Tensor) -> torch.Tensor:
+    """[dgate | dup] rows ([rows, 2I]) of ``h = silu(gate) * up`` with HF's roundings."""
+    I = gate.shape[-1]
+    g2, u2, d2 = (t.reshape(-1, I).contiguous() for t in (gate, up, dh))
+    out = torch.empty((g2.shape[0], 2 * I), dtype=gate.dtype, device=gate.device)
+    with torch.cuda.device(gate.device):
+        _call("stratum_swiglu_bwd_cat", _lib.ptr(g2), _lib.ptr(u2), _lib.ptr(d2), _lib.DTYPE_CODE[gate.dtype],
+              g2.shape[0], I, _lib.ptr(out), _stream(gate))
+    return out
+
+
 def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` with HF's bf16 roundings, one kernel each way."""
     _lib.require_cuda(gate, "swiglu")
@@ -108,16 +119,20 @@ def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
 class _SwiGLUMLPFn(torch.autograd.Function):
     """The whole NF4 SwiGLU MLP with LoRA in three fused kernels:
 
-    forward   gate|up GEMM with the SwiGLU epilogue (h, plus 16-bit gate / up kept),
-              then the down GEMM;
-    backward  the down projection's input-gradient GEMM with the SwiGLU backward in
-              its epilogue ([dgate | dup], dh never stored), then one input-gradient
-              pass through the stacked gate / up weights.
+    forward   gate and up GEMMs and one SwiGLU pass -- or, with ``fuse_forward``,
+              one gate|up GEMM with the SwiGLU epilogue (h, plus 16-bit gate / up
+              kept) -- then the down GEMM;
+    backward  the down projection's input-gradient GEMM, one SwiGLU-backward pass
+              writing [dgate | dup] rows, then one input-gradient pass through the
+              stacked gate / up weights.  (The SwiGLU backward is not an epilogue of
+              the down GEMM: its exp / divide per element would compete for issue
+              slots with the NF4 decode on every SM and cost more than the
+              standalone pass, which runs at HBM speed.)
     LoRA terms ride in the same accumulators (extra K chunks); dA / dB are small
     cuBLAS GEMMs as in NF4Linear."""
 
     @staticmethod
-    def forward(ctx, x, Ag, Bg, Au, Bu, Ad, Bd, mods):
+    def forward(ctx, x, Ag, Bg, Au, Bu, Ad, Bd, mods, fuse_forward):
         from . import ops
 
         gate, up, down = mods
@@ -128,21 +143,39 @@ class _SwiGLUMLPFn(torch.autograd.Function):
         gw = (gate.quantized, gate.quant_state)
         uw = (up.quantized, up.quant_state)
         dw = (down.quantized, down.quant_state)
-        xa = ops.mlp_lora_down(x2, Ag, Au, gate.scaling, up.scaling) if Ag is not None else None
-        h, g, u = ops.nf4_swiglu_fwd(x2, gw, uw, xa, Bg, Bu, keep_gate_up=True)
+        xa_g = xa_u = None
+        if fuse_forward:
+            xa = ops.mlp_lora_down(x2, Ag, Au, gate.scaling, up.scaling) if Ag is not None else None
+            h, g, u = ops.nf4_swiglu_fwd(x2, gw, uw, xa, Bg, Bu, keep_gate_up=True)
+            if xa is not None:
+                r, rp = Ag.shape[0], xa.shape[1] // 2
+                xa_g, xa_u = xa[:, :r], xa[:, rp:rp + r]
+        else:  # the two projections' GEMMs, then one SwiGLU pass
+            if Ag is not None:
+                xa_g = ops.lora_down(x2, Ag.to(x2.dtype), gate.scaling)
+                xa_u = ops.lora_down(x2, Au.to(x2.dtype), up.scaling)
+            g = ops.nf4_gemm_fwd(x2, gw[0], gw[1], lora_A=Ag, lora_B=Bg, scaling=gate.scaling, xa=xa_g)
+            u = ops.nf4_gemm_fwd(x2, uw[0], uw[1], lora_A=Au, lora_B=Bu, scaling=up.scaling, xa=xa_u)
+            h = torch.empty_like(g)
+            with torch.cuda.device(g.device):
+                _call("stratum_swiglu_fwd", _lib.ptr(g), _lib.ptr(u), _lib.DTYPE_CODE[g.dtype], g.numel(),
+                      _lib.ptr(h), _stream(g))
+            if Ag is not None:
+                r = Ag.shape[0]
+                xa_g, xa_u = xa_g[:, :r], xa_u[:, :r]
         xad = ops.lora_down(h, Ad.to(h.dtype), down.scaling) if Ad is not None else None
         y = ops.nf4_gemm_fwd(h, dw[0], dw[1], lora_A=Ad, lora_B=Bd, scaling=down.scaling, xa=xad)
         ctx.weights = (gw, uw, dw)
         ctx.scales = (gate.scaling, up.scaling, down.scaling)
         ctx.shape = x.shape
-        ctx.save_for_backward(x2, xa, g, u, h, xad, Ag, Bg, Au, Bu, Ad, Bd)
+        ctx.save_for_backward(x2, xa_g, xa_u, g, u, h, xad, Ag, Bg, Au, Bu, Ad, Bd)
         return y.reshape(*x.shape[:-1], y.shape[-1])
 
     @staticmethod
     def backward(ctx, dy):
         from . import ops
 
-        x2, xa, g, u, h, xad, Ag, Bg, Au, Bu, Ad, Bd = ctx.saved_tensors
+        x2, xa_g, xa_u, g, u, h, xad, Ag, Bg, Au, Bu, Ad, Bd = ctx.saved_tensors
         gw, uw, dw = ctx.weights
         sg, su, sd = ctx.scales
         Hout = dy.shape[-1]
@@ -157,12 +190,16 @@ class _SwiGLUMLPFn(torch.autograd.Function):
             dyb_d = ops.lora_down(dy2, Bd.t().to(dy2.dtype), sd)
             grads[4] = (dyb_d[:, :rd].t() @ h).to(Ad.dtype)
             grads[5] = (dy2.t() @ xad[:, :rd]).to(Bd.dtype)
-        dgu = ops.nf4_gemm_dx_swiglu(dy2, dw, g, u, dyb_d, Ad)
+        # dh through the down projection (its plain input-gradient kernel), then the
+        # SwiGLU backward as one memory-bound pass writing [dgate | dup] rows
+        dh = ops.nf4_gemm_dx(dy2, dw[0], dw[1], lora_A=Ad, lora_B=Bd, scaling=sd, dyb=dyb_d)
+        dgu = swiglu_backward_cat(g, u, dh)
+        del dh
         dg, du = dgu[:, :I], dgu[:, I:]
         dyb = A_cat = None
         if Ag is not None:
             r = Ag.shape[0]
-            rp = xa.shape[1] // 2
+            rp = -(-r // ops.LORA_CHUNK) * ops.LORA_CHUNK
             dyb = torch.zeros((dy2.shape[0], 2 * rp), dtype=dy2.dtype, device=dy2.device)
             dyb[:, :r] = ops.scaled_matmul(dg, Bg.to(dy2.dtype), sg)
             dyb[:, rp:rp + r] = ops.scaled_matmul(du, Bu.to(dy2.dtype), su)
@@ -170,13 +207,13 @@ class _SwiGLUMLPFn(torch.autograd.Function):
             A_cat[:r] = Ag
             A_cat[rp:rp + r] = Au
             grads[0] = (dyb[:, :r].t() @ x2).to(Ag.dtype)
-            grads[1] = (dg.t() @ xa[:, :r]).to(Bg.dtype)
+            grads[1] = (dg.t() @ xa_g).to(Bg.dtype)
             grads[2] = (dyb[:, rp:rp + r].t() @ x2).to(Au.dtype)
-            grads[3] = (du.t() @ xa[:, rp:rp + r]).to(Bu.dtype)
+            grads[3] = (du.t() @ xa_u).to(Bu.dtype)
         dx = None
         if ctx.needs_input_grad[0]:
             dx = ops.nf4_gemm_dx_pair(dgu, gw, uw, dyb, A_cat).reshape(ctx.shape)
-        return (dx, *grads, None)
+        return (dx, *grads, None, None)
 
 
 def _fusable(gate, up, down, x: torch.Tensor) -> bool:
@@ -211,20 +248,29 @@ class FusedMLP(nn.Module):
     """``down(swiglu(gate(x), up(x)))`` (LlamaMLP / Qwen3MLP with SiLU).
 
     With NF4Linear projections (blocksize 64, no bias, intermediate size a multiple
-    of 64, gate and up LoRA of one even rank) the MLP runs as three fused kernels
-    (``_SwiGLUMLPFn``), the dense counterpart of the reference's fused frozen MLP
-    (stratum/model/mlp_opt.py:154-245); otherwise as the three NF4Linears around
-    one SwiGLU kernel."""
+    of 64, gate and up LoRA of one even rank) the MLP runs through ``_SwiGLUMLPFn``,
+    the dense counterpart of the reference's fused frozen MLP
+    (stratum/model/mlp_opt.py:154-245): the backward takes the gate and up
+    gradients through one stacked input-gradient GEMM fed by a single SwiGLU pass.
+    ``fuse_forward=True`` also forms h in the gate|up GEMM's epilogue (one pass over
+    x, gate and up never re-read); measured in the training pipeline on one B200 it
+    wins at Qwen3-0.6B shapes and loses ~1% at Llama-3-8B shapes under the power
+    cap, where the per-element exp / divide competes with the NF4 decode, so it is
+    off by default.  Other projections run as three NF4Linears around one SwiGLU
+    kernel."""
 
-    def __init__(self, gate_proj: nn.Module, up_proj: nn.Module, down_proj: nn.Module, fuse: bool = True):
+    def __init__(self, gate_proj: nn.Module, up_proj: nn.Module, down_proj: nn.Module, fuse: bool = True,
+                 fuse_forward: bool = False):
         super().__init__()
         self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
         self.fuse = fuse
+        self.fuse_forward = fuse_forward
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         g, u, d = self.gate_proj, self.up_proj, self.down_proj
         if self.fuse and _fusable(g, u, d, x):
-            return _SwiGLUMLPFn.apply(x, g.lora_A, g.lora_B, u.lora_A, u.lora_B, d.lora_A, d.lora_B, (g, u, d))
+            return _SwiGLUMLPFn.apply(x, g.lora_A, g.lora_B, u.lora_A, u.lora_B, d.lora_A, d.lora_B, (g, u, d),
+                                      bool(self.fuse_forward))
         return d(swiglu(g(x), u(x)))
 
 

@@ -256,38 +256,6 @@ def nf4_swiglu_fwd(x: torch.Tensor, gate: tuple, up: tuple, xa: Optional[torch.T
             None if u_out is None else u_out.reshape(*shp, I))
 
 
-def nf4_gemm_dx_swiglu(dy: torch.Tensor, down: tuple, gate_out: torch.Tensor, up_out: torch.Tensor,
-                       dyb: Optional[torch.Tensor] = None, lora_A: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """[dgate | dup] ([rows, 2I]) of a SwiGLU MLP from the down projection's output gradient:
-    dh = dy Wd + dyb lora_A (never stored), then the SwiGLU backward with the forward's
-    16-bit gate and up -- the down projection's input-gradient kernel with that epilogue."""
-    _lib.require_cuda(dy, "nf4_gemm_dx_swiglu")
-    packed, qs = down
-    N, I = int(qs.shape[0]), int(qs.shape[1])
-    dev = dy.device
-    dy2 = dy.reshape(-1, N)
-    if not dy2.is_contiguous() or dy2.data_ptr() % 16:
-        dy2 = dy2.contiguous()
-    T = dy2.shape[0]
-    g2 = gate_out.reshape(T, I).contiguous()
-    u2 = up_out.reshape(T, I).contiguous()
-    out = torch.empty((T, 2 * I), dtype=dy.dtype, device=dev)
-    r = 0
-    la = None
-    if lora_A is not None:
-        r = int(lora_A.shape[0])
-        la = lora_A.to(dy.dtype).contiguous()
-    keep: list = []
-    w = _nf4_weight(packed, qs, dev, keep)
-    code16 = keep[-1]
-    L = _lib.lib()
-    with torch.cuda.device(dev):
-        _lib.check(L.stratum_nf4_gemm_dx_swiglu(
-            _lib.ptr(dy2), _lib.DTYPE_CODE[dy.dtype], T, N, _addr(w), _lib.ptr(code16), I, _lib.ptr(dyb), _lib.ptr(la),
-            r, _lib.ptr(g2), _lib.ptr(u2), _lib.ptr(out), _lib.stream_of(dev)), "nf4_gemm_dx_swiglu")
-    return out
-
-
 def nf4_gemm_dx_pair(dy: torch.Tensor, w0: tuple, w1: tuple, dyb: Optional[torch.Tensor] = None,
                      lora_A: Optional[torch.Tensor] = None) -> torch.Tensor:
     """dx = dy [W0; W1] + dyb lora_A for two NF4 weights stacked along their rows

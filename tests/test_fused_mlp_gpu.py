@@ -3,9 +3,9 @@
 * The gate|up GEMM with the SwiGLU epilogue reproduces, bit for bit, the
   unfused path it replaces (the gate and up NF4 GEMMs, then the SwiGLU kernel):
   each output row is the same dot product over the same dequantized weights.
-* The down projection's input gradient with the SwiGLU backward in its epilogue
-  reproduces, bit for bit, the plain input-gradient kernel followed by the
-  SwiGLU backward kernel.
+* The SwiGLU backward written as [dgate | dup] rows (the dY of the stacked
+  gate/up input gradient) equals the two-output SwiGLU backward kernel bit for
+  bit.
 * The whole MLP (forward, input gradient, LoRA gradients) is within 1e-2
   relative (Frobenius) of an fp32 reference on the exact dequantized weights,
   and within 1e-2 of HF's LlamaMLP run on the same weights with the adapters
@@ -96,17 +96,14 @@ def test_swiglu_forward_matches_unfused_kernels_bitwise(T, H, I, r, dq):
     assert torch.equal(h, h_ref)
 
 
-@pytest.mark.parametrize("T,H,I,r,dq", CASES)
-def test_down_dx_with_swiglu_backward_matches_unfused_kernels_bitwise(T, H, I, r, dq):
-    gate, up, down = _mlp(H, I, r, dq, seed=T + 1)
+def test_swiglu_backward_rows_match_the_separate_kernel_bitwise():
+    """[dgate | dup] rows (the stacked input gradient's dY) equal the two-output kernel's."""
+    T, I = 1000, 1536
     gen = torch.Generator(device=DEV).manual_seed(6)
     g = (torch.randn(T, I, generator=gen, device=DEV) * 2).to(torch.bfloat16)
     u = torch.randn(T, I, generator=gen, device=DEV).to(torch.bfloat16)
-    dy = torch.randn(T, H, generator=gen, device=DEV).to(torch.bfloat16)
-    dyb = ops.lora_down(dy, down.lora_B.t().to(dy.dtype), down.scaling) if r else None
-    dgu = ops.nf4_gemm_dx_swiglu(dy, (down.quantized, down.quant_state), g, u, dyb, down.lora_A)
-    dh = ops.nf4_gemm_dx(dy, down.quantized, down.quant_state, lora_A=down.lora_A, lora_B=down.lora_B,
-                         scaling=down.scaling, dyb=dyb)
+    dh = torch.randn(T, I, generator=gen, device=DEV).to(torch.bfloat16)
+    dgu = FZ.swiglu_backward_cat(g, u, dh)
     gg, uu = g.clone().requires_grad_(), u.clone().requires_grad_()
     FZ.swiglu(gg, uu).backward(dh)
     torch.cuda.synchronize()
@@ -114,10 +111,11 @@ def test_down_dx_with_swiglu_backward_matches_unfused_kernels_bitwise(T, H, I, r
     assert torch.equal(dgu[:, I:], uu.grad)
 
 
+@pytest.mark.parametrize("fuse_forward", [True, False], ids=["fused-forward", "split-forward"])
 @pytest.mark.parametrize("T,H,I,r,dq", CASES)
-def test_fused_mlp_matches_fp32_reference(T, H, I, r, dq):
+def test_fused_mlp_matches_fp32_reference(T, H, I, r, dq, fuse_forward):
     gate, up, down = _mlp(H, I, r, dq, seed=T + 2)
-    mlp = FZ.FusedMLP(gate, up, down)
+    mlp = FZ.FusedMLP(gate, up, down, fuse_forward=fuse_forward)
     gen = torch.Generator(device=DEV).manual_seed(7)
     x = torch.randn(1, T, H, generator=gen, device=DEV).to(torch.bfloat16).requires_grad_()
     assert FZ._fusable(gate, up, down, x)
@@ -163,19 +161,25 @@ def test_fused_mlp_matches_hf_llama_mlp(T, H, I, r, dq):
     gen = torch.Generator(device=DEV).manual_seed(8)
     x = torch.randn(1, T, H, generator=gen, device=DEV).to(torch.bfloat16)
     dy = torch.randn(1, T, H, generator=gen, device=DEV).to(torch.bfloat16)
-    outs = []
-    for mod in (hf, FZ.FusedMLP(gate, up, down)):
+    xi = x.clone().requires_grad_()
+    y_ref = hf(xi)
+    y_ref.backward(dy)
+    ref = (y_ref.detach().float(), xi.grad.float())
+    for fuse_forward in (False, True):
+        for m in (gate, up, down):
+            for p in (m.lora_A, m.lora_B):
+                if p is not None:
+                    p.grad = None
         xi = x.clone().requires_grad_()
-        y = mod(xi)
+        y = FZ.FusedMLP(gate, up, down, fuse_forward=fuse_forward)(xi)
         y.backward(dy)
-        outs.append((y.detach().float(), xi.grad.float()))
-    assert relative_error(outs[1][0], outs[0][0]) < 1e-2
-    assert relative_error(outs[1][1], outs[0][1]) < 1e-2
-    if r:
-        for name, m in (("gate_proj", gate), ("up_proj", up), ("down_proj", down)):
-            p = getattr(hf, name)
-            assert relative_error(m.lora_A.grad.float(), p.A.grad.float()) < 1e-2, name
-            assert relative_error(m.lora_B.grad.float(), p.B.grad.float()) < 1e-2, name
+        assert relative_error(y.detach().float(), ref[0]) < 1e-2
+        assert relative_error(xi.grad.float(), ref[1]) < 1e-2
+        if r:
+            for name, m in (("gate_proj", gate), ("up_proj", up), ("down_proj", down)):
+                p = getattr(hf, name)
+                assert relative_error(m.lora_A.grad.float(), p.A.grad.float()) < 1e-2, name
+                assert relative_error(m.lora_B.grad.float(), p.B.grad.float()) < 1e-2, name
 
 
 def test_fused_mlp_pair_input_gradient_matches_two_passes():
