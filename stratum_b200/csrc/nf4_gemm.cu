@@ -41,6 +41,7 @@ namespace gemm {
 
 using namespace sm100;
 
+
 constexpr int BM = 128;       // weight rows per tile (TMEM lanes, MMA M)
 constexpr int BN = 256;       // tokens per tile (MMA N)
 constexpr int BK = 64;        // K per step: one NF4 block per weight row
@@ -215,7 +216,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 }
             }
             for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)  // every copy lands before exit
-                mbar_wait(&sm.full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&sm.full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         // ---------------------------------- producer: packed weight tiles
@@ -242,7 +243,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 }
             }
             for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
-                mbar_wait(&sm.wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&sm.wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
@@ -272,7 +273,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 if (ok) mma_commit(sm.accfull);
             }
             mma_commit(sm.drain);  // all issued MMAs complete before TMEM is released
-            mbar_wait(sm.drain, 0, p.status, kErrTimeoutTeardown);
+            mbar_wait_issued(sm.drain, 0, p.status, kErrTimeoutTeardown);
         }
     } else if (warp >= 4 && warp < EPI_WARP0) {
         // ---------------------------------------------------- dequant warps
@@ -600,7 +601,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 }
             }
             for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
-                mbar_wait(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         // ------------------------------- producer: packed weight tiles (64 x 128)
@@ -620,7 +621,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 }
             }
             for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
-                mbar_wait(&wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
@@ -647,7 +648,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 if (ok) mma_commit(&accfull[ab]);
             }
             mma_commit(drain);
-            mbar_wait(drain, 0, p.status, kErrTimeoutTeardown);
+            mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown);
         }
     } else if (warp >= 4 && warp < EPI_WARP0) {
         // ---------------------------------------------------- dequant warps
@@ -804,6 +805,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
 }
 
 }  // namespace dx
+
 
 // ------------------------------------------------------------------- host --
 

@@ -285,7 +285,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 }
             }
             for (uint32_t j = (it > F_XS ? it - F_XS : 0); j < it; ++j)
-                mbar_wait(&full[j % F_XS], (j / F_XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&full[j % F_XS], (j / F_XS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         if (lane == 0) {
@@ -304,7 +304,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 }
             }
             for (uint32_t j = (wt > F_WS ? wt - F_WS : 0); j < wt; ++j)
-                mbar_wait(&wfull[j % F_WS], (j / F_WS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&wfull[j % F_WS], (j / F_WS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -335,7 +335,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 if (ok) mma_commit(accfull);
             }
             mma_commit(drain);
-            mbar_wait(drain, 0, p.status, kErrTimeoutTeardown);
+            mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown);
         }
     } else if (warp >= 4 && warp < EPI_WARP0) {
         const int grp = (warp - 4) >> 2;
@@ -576,7 +576,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                 }
             }
             for (uint32_t j = (it > D_XS ? it - D_XS : 0); j < it; ++j)
-                mbar_wait(&full[j % D_XS], (j / D_XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&full[j % D_XS], (j / D_XS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         if (lane == 0) {
@@ -593,7 +593,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                 }
             }
             for (uint32_t j = (wt > D_WS ? wt - D_WS : 0); j < wt; ++j)
-                mbar_wait(&wfull[j % D_WS], (j / D_WS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&wfull[j % D_WS], (j / D_WS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -619,7 +619,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                 if (ok) mma_commit(&accfull[ab]);
             }
             mma_commit(drain);
-            mbar_wait(drain, 0, p.status, kErrTimeoutTeardown);
+            mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown);
         }
     } else if (warp >= 4 && warp < EPI_WARP0) {
         const int grp = (warp - 4) >> 2;

@@ -99,6 +99,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     }
 }
 
+// Bounded wait for work this CTA already issued (teardown): unlike mbar_wait it
+// does not give up when another thread recorded an error, so a CTA that unwinds
+// still waits -- up to the time limit -- for its own copies and MMAs before it
+// frees shared memory or TMEM.
+__device__ __forceinline__ bool mbar_wait_issued(uint64_t *bar, uint32_t parity, int *err, int code) {
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
+        if (globaltimer() - t0 > kWaitTimeoutNs) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+}
+
 // 2-D TMA tile load into shared memory, completion counted on `bar` (bytes).
 // Every CTA fetches its own tiles (no cluster-wide broadcast form).
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int32_t c0, int32_t c1,
