@@ -82,10 +82,10 @@ __device__ __forceinline__ void swiglu_fwd8(const float g[8], const float u[8], 
             if (!(fabsf(g[i]) <= 16.f) || near_bf16_tie(s, 64)) redo |= 1u << i;
             h[i] = rnd<BF16>(s) * u[i];
         }
-        while (redo) {
-            const int i = __ffs(redo) - 1;
-            redo &= redo - 1;
-            h[i] = swiglu_fwd1<BF16>(g[i], u[i]);
+        if (redo) {  // rare; unrolled so the arrays stay in registers
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (redo & (1u << i)) h[i] = swiglu_fwd1<BF16>(g[i], u[i]);
         }
     }
 }
