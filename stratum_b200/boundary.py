@@ -65,6 +65,20 @@ def _copy_after(x: torch.Tensor, dst: torch.device) -> torch.Tensor:
     return x.to(dst)
 
 
+def _typed_buffer_view(buffer: torch.Tensor, dtype: torch.dtype, numel: int) -> torch.Tensor:
+    """The first ``numel`` elements of ``dtype`` over a byte buffer (the staging
+    buffer of a host-staged boundary copy)."""
+    nbytes = numel * torch.empty((), dtype=dtype).element_size()
+    return buffer.narrow(0, 0, nbytes).view(dtype)
+
+
+def _peer_ok(a: torch.device, b: torch.device) -> bool:
+    try:
+        return torch.cuda.can_device_access_peer(a.index or 0, b.index or 0)
+    except (RuntimeError, AssertionError):
+        return False
+
+
 def transfer(x: torch.Tensor, dst_device) -> torch.Tensor:
     """Move a boundary activation to ``dst_device`` (differentiable)."""
     dst = _device(dst_device)
@@ -78,12 +92,33 @@ def transfer(x: torch.Tensor, dst_device) -> torch.Tensor:
 class DeviceTransferPool:
     """Drop-in for ``HostStagingPool`` (stratum/host_staging.py:47-200): same
     ``transfer`` / ``transfer_async`` calls, but a direct device-to-device copy
-    with no host staging buffer and no host synchronisation."""
+    (NVLink peer access, every GPU pair of an NVSwitch box) with no host
+    synchronisation.  Only between GPUs without peer access does a copy go
+    through a pinned host buffer, as the reference's always does."""
 
-    def ensure(self, size_bytes: int) -> None:  # no staging buffer to grow
-        return None
+    def __init__(self):
+        self._buf: Optional[torch.Tensor] = None
+
+    def ensure(self, size_bytes: int) -> None:
+        """Grow the pinned staging buffer (used only between GPUs without peer access)."""
+        if self._buf is None or self._buf.numel() < size_bytes:
+            self._buf = torch.empty(int(size_bytes), dtype=torch.uint8, pin_memory=torch.cuda.is_available())
+
+    def _staged(self, x: torch.Tensor, dst: torch.device) -> torch.Tensor:
+        flat = x.detach().reshape(-1)
+        self.ensure(flat.numel() * flat.element_size())
+        host = _typed_buffer_view(self._buf, flat.dtype, flat.numel())
+        host.copy_(flat)  # synchronous D2H: the buffer is reused by the next transfer
+        out = torch.empty(x.shape, dtype=x.dtype, device=dst)
+        out.view(-1).copy_(host)
+        torch.cuda.current_stream(dst).synchronize()
+        return out
 
     def transfer(self, tensor: torch.Tensor, dst_device, src_device=None) -> torch.Tensor:
+        dst = _device(dst_device)
+        if (tensor.is_cuda and dst.type == "cuda" and tensor.device != dst and not tensor.requires_grad
+                and not _peer_ok(tensor.device, dst)):
+            return self._staged(tensor, dst)
         return transfer(tensor, dst_device)
 
     def transfer_async(self, tensor: torch.Tensor, dst_device, src_device=None):

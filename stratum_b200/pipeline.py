@@ -41,16 +41,21 @@ import torch.nn as nn
 
 from .boundary import P2PChannel, transfer
 from .nf4_linear import NF4Linear
+from .runtime import anchor_explicit_group_backward
+from .scheduler import ModelExecutePlan
 from .stage import DeviceStage
-from .upload import ensure_weights, free_weights
+from .upload import (ensure_prefetched_weights, ensure_weights, free_weights, prefetch_weights, restore_module_buffers,
+                     snapshot_module_buffers)
 
 
 def _dev(d) -> torch.device:
+    """A stage's device: ``torch.device`` / string as given; an integer id names a
+    CUDA device (or the CPU on a machine without one, as the reference's tests run)."""
     if isinstance(d, torch.device):
         return d
     if isinstance(d, str):
         return torch.device(d)
-    return torch.device("cuda", int(d))
+    return torch.device("cuda", int(d)) if torch.cuda.is_available() else torch.device("cpu")
 
 
 def _on(device: torch.device):
@@ -211,15 +216,30 @@ class _AuxState:
 
 
 class _Runner:
-    """Runs layers [i0, i1) of a stage on the 7-tuple, with streaming and router taps."""
+    """Runs layers [i0, i1) of a stage on the pipeline tuple: forward without an
+    autograd graph, and again with one for the backward (the recompute anchor of
+    ``runtime.anchor_explicit_group_backward``), with per-layer weight streaming,
+    the group's buffer snapshot and the router taps of MoE layers."""
 
-    def __init__(self, layers: list[nn.Module], i0: int, i1: int, rest: tuple, streamer: _Streamer,
-                 policy: str, sink=None, aux: Optional[_AuxState] = None, offload: bool = False):
-        self.layers, self.i0, self.i1, self.rest = layers, i0, i1, rest
-        self.streamer, self.policy, self.sink, self.aux, self.offload = streamer, policy, sink, aux, offload
+    def __init__(self, stage, i0: int, i1: int, streamer: _Streamer, policy: str, sink=None,
+                 aux: Optional[_AuxState] = None, group_module: Optional[nn.Module] = None,
+                 buffers: Optional[dict] = None, reload=None, unload=None):
+        self.stage, self.layers = stage, list(stage.layers)
+        self.i0, self.i1 = i0, i1
+        self.streamer, self.policy, self.sink, self.aux = streamer, policy, sink, aux
+        self.group_module, self.buffers = group_module, buffers
+        # groups made resident as a whole (not streamed): weights again for the
+        # recomputation, dropped after the group's backward
+        self.reload, self.unload = reload, unload
+        self.extra: list = []
 
-    def _run(self, hidden: torch.Tensor, collect_grad_probs: Optional[list]) -> torch.Tensor:
-        t = (hidden,) + self.rest
+    def _run(self, tup: tuple, collect_grad_probs: Optional[list]) -> tuple:
+        if self.sink is None:  # the stage's own range runner (timing spans), or the whole stage module
+            if hasattr(self.stage, "forward_range"):
+                return self.stage.forward_range(tup, local_start=self.i0, local_stop=self.i1)
+            if self.i0 == 0 and self.i1 == len(self.layers):
+                return self.stage(tup)
+        t = tup
         for i in range(self.i0, self.i1):
             if self.sink is not None:
                 self.sink.clear()
@@ -236,14 +256,15 @@ class _Runner:
                     else:
                         collect_grad_probs.append(probs)
                 self.sink.clear()
-        return t[0]
+        return t
 
-    def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+    def forward(self, tup: tuple) -> tuple:
         s = self.streamer
         for i in range(self.i0, self.i1):
             s.acquire(i)
         s.prefetch(self.i1)
-        out = self._run(hidden, None)
+        with torch.no_grad():
+            out = self._run(tup, None)
         if self.policy == "group":  # reference behaviour: free after forward, upload again for backward
             last = len(self.layers) - 1
             for i in range(self.i0, self.i1):
@@ -251,61 +272,46 @@ class _Runner:
                     s.release(i)
         return out
 
-    def recompute(self, x: torch.Tensor):
+    def recompute(self, tup: tuple) -> tuple:
+        """The group again with autograd on (called by the anchor's backward); the
+        router aux loss's gradient term, if any, is left in ``self.extra``."""
         s = self.streamer
         for i in range(self.i0, self.i1):
             s.acquire(i)
         s.prefetch(self.i0 - 1)
+        if self.reload is not None:
+            self.reload()
+        if self.buffers is not None and self.group_module is not None:
+            # the recomputation starts from the buffers the forward saw
+            restore_module_buffers(self.group_module, self.buffers)
         probs: Optional[list] = [] if self.sink is not None else None
-        out = self._run(x, probs)
-        extra = []
+        out = self._run(tup, probs)
+        self.extra = []
         if probs and self.aux is not None and self.aux.weight is not None:
             term = sum((torch.softmax(p.float(), dim=-1) * self.aux.weight.to(p.device)).sum() for p in probs)
             if term.requires_grad:  # else the term reaches no trainable parameter
-                extra.append(term)
-        return out, extra
+                self.extra.append(term)
+        return out
+
+    def extra_terms(self) -> list:
+        out, self.extra = self.extra, []
+        return out
 
     def after_backward(self) -> None:
         if self.policy == "group":
             for i in range(self.i0, self.i1):
                 self.streamer.release(i)
+        if self.unload is not None:
+            self.unload()
 
 
-class _Anchor(torch.autograd.Function):
-    """Output of a layer group computed without a graph; its backward recomputes
-    the group from the saved input and backpropagates (LoRA gradients accumulate
-    into the parameters directly).  The group's trainable parameters are inputs
-    only so that the output requires grad when the input does not."""
-
-    @staticmethod
-    def forward(ctx, runner: _Runner, hidden: torch.Tensor, *params):
-        ctx.runner = runner
-        ctx.in_grad = hidden.requires_grad
-        saved = hidden.detach()
-        if runner.offload and saved.is_cuda:
-            saved = saved.to("cpu")
-        ctx.saved_hidden = saved
-        ctx.n_params = len(params)
-        with torch.no_grad():
-            out = runner.forward(hidden)
-        return out
-
-    @staticmethod
-    def backward(ctx, grad: torch.Tensor):
-        runner: _Runner = ctx.runner
-        h = ctx.saved_hidden
-        if h.device != grad.device:
-            h = h.to(grad.device)
-        x = h.detach().requires_grad_(ctx.in_grad)
-        with torch.enable_grad():
-            out, extra = runner.recompute(x)
-        outs = [out] + extra
-        grads = [grad] + [torch.ones((), dtype=e.dtype, device=e.device) for e in extra]
-        torch.autograd.backward(outs, grads)
-        runner.after_backward()
-        ctx.runner = None
-        ctx.saved_hidden = None
-        return (None, x.grad if ctx.in_grad else None) + (None,) * ctx.n_params
+def _anchor_group(runner: _Runner, tup: tuple, offload: bool, look_ahead=None) -> tuple:
+    """Forward of one layer group without a graph, anchored so its backward recomputes it."""
+    out = runner.forward(tup)
+    return anchor_explicit_group_backward(run_group=runner.recompute, group_input=tup, group_output=out,
+                                          offload_input_to_cpu=offload, look_ahead_upload=look_ahead,
+                                          on_backward_complete=runner.after_backward,
+                                          extra_terms=runner.extra_terms)
 
 
 def _trainable(modules: list[nn.Module]) -> list[torch.Tensor]:
@@ -318,29 +324,46 @@ def _stage_layers(stage) -> list[nn.Module]:
 
 def _run_stage(stage, hidden: torch.Tensor, rest: tuple, streamer: _Streamer, policy: str, sink, aux,
                offload: bool) -> torch.Tensor:
-    layers = _stage_layers(stage)
-    for i in range(len(layers)):
-        runner = _Runner(layers, i, i + 1, rest, streamer, policy, sink, aux, offload)
-        hidden = _Anchor.apply(runner, hidden, *_trainable([layers[i]]))
-    return hidden
+    """Every layer of ``stage`` as its own recompute group (the per-rank pipeline)."""
+    tup = (hidden,) + tuple(rest)
+    for i in range(len(stage.layers)):
+        runner = _Runner(stage, i, i + 1, streamer, policy, sink, aux)
+        tup = _anchor_group(runner, tup, offload)
+    return tup[0]
 
 
 # --------------------------------------------------------------------------------
 # one process, several GPUs (the reference's class)
 # --------------------------------------------------------------------------------
 
+def _move_tensor_tree(value: Any, device) -> Any:
+    """Tensors of a nested tuple / list / dict moved to ``device`` (other leaves kept):
+    the non-hidden parts of the pipeline tuple crossing a stage boundary."""
+    return _move_tree(value, device)
+
+
 class StratumPipeline(nn.Module):
     """A multi-GPU pipeline of DeviceStages driven by one process.
 
     Same constructor and calls as the reference (stratum/pipeline.py:90-99,
-    646-652, 1027, 1073).  ``prefix`` runs on the first stage's device, each
-    stage on its own device, ``postfix`` on the last stage's device; boundaries
-    are NVLink device copies; every layer is a recompute group.  ``execute_plan``
-    is accepted for compatibility; the grouping is always one layer.
-    ``prefetch_nf4`` is accepted too: streamed layers always upload on a side
-    stream, one layer ahead.  ``offload_stage_inputs`` keeps each group's saved
-    input in host memory.  For MoE models pass the ``router_sink`` the layers
-    were built with and the aux-loss coefficient.
+    646-1071).  ``prefix`` runs on the first stage's device, each stage on its own
+    device, ``postfix`` on the last stage's device; boundaries are NVLink device
+    copies.  Layers run in recompute groups: ``execute_plan`` (a
+    ``scheduler.ModelExecutePlan``; groups may not cross stages) or, by default,
+    one group per layer.  Each group's forward runs without a graph after its
+    buffers are snapshotted; its weights are freed right after (the reference's
+    memory model) and its backward recomputes it (``runtime``), starting the
+    previous group's upload first (the look-ahead).
+
+    Weights: a stage of fused-mode NF4Linear layers streams them per layer on a
+    side stream (``_param_upload_stream``).  Otherwise each group's module is
+    made resident with ``ensure_weights`` -- with ``prefetch_nf4``, through
+    ``prefetch_weights`` / ``ensure_prefetched_weights``, the next group's (or the
+    postfix's) copies started before the current group runs -- as the reference
+    does on its group-level path; the prefix and postfix always are.
+    ``offload_stage_inputs`` keeps each group's saved input in host memory.  For
+    MoE models pass the ``router_sink`` the layers were built with and the
+    aux-loss coefficient.
     """
 
     def __init__(self, prefix: nn.Module, stages: list, postfix: nn.Module, *, prefetch_nf4: bool = False,
@@ -352,10 +375,34 @@ class StratumPipeline(nn.Module):
         self.postfix = postfix
         self.prefetch_nf4 = prefetch_nf4
         self.offload_stage_inputs = offload_stage_inputs
-        self.execute_plan = execute_plan
         self.router_sink = router_sink
         self.router_aux_coef = float(router_aux_coef)
         self.n_experts = int(n_experts)
+        self._stage_ranges = []
+        start = 0
+        for st in stages:
+            self._stage_ranges.append(range(start, start + len(st.layers)))
+            start += len(st.layers)
+        total = start
+        plan = execute_plan if execute_plan is not None else ModelExecutePlan.per_layer(total)
+        plan.check_valid(total, "train")
+        if {(r.start, r.stop) for r in plan.fwd_plan} != {(r.start, r.stop) for r in plan.bwd_plan}:
+            raise ValueError("StratumPipeline: backward groups must be the forward groups (each forward group "
+                             "is recomputed as one backward group)")
+        self.execute_plan = plan
+        # (stage index, first layer in the stage, end layer in the stage, global layer range) per group
+        self._groups: list[tuple[int, int, int, range]] = []
+        for r in plan.fwd_plan:
+            owner = next((si for si, sr in enumerate(self._stage_ranges) if sr.start <= r.start and r.stop <= sr.stop),
+                         None)
+            if owner is None:
+                raise ValueError(f"StratumPipeline: layer group {r.start}:{r.stop} must lie inside one stage")
+            sr = self._stage_ranges[owner]
+            self._groups.append((owner, r.start - sr.start, r.stop - sr.start, r))
+        # the module that holds each group's layers (the stage itself when the group is the whole stage)
+        self._fwd_group_modules: list[nn.Module] = [
+            stages[si] if (a == 0 and b == len(stages[si].layers)) else nn.ModuleList(list(stages[si].layers)[a:b])
+            for si, a, b, _ in self._groups]
         self._streamers = [
             _Streamer(_stage_layers(s), _dev(s.device_id), any(_needs_streaming(l, _dev(s.device_id))
                                                                for l in s.layers))
@@ -364,47 +411,111 @@ class StratumPipeline(nn.Module):
         self.timing_recorder = None
         self._layer_timer = None
         self._plan_adapt_after_n = 0
-        # the reference's bookkeeping names, kept for callers and tests that inspect them:
-        # one module per recompute group (here: per layer), the backward look-ahead fences
-        # of the current step (streamed layers carry their own events here, so it stays empty)
-        self._fwd_group_modules: list[nn.Module] = [layer for s in stages for layer in s.layers]
+        # backward look-ahead fences of the current step, by group (streamed groups carry their
+        # upload events in their streamer, so this stays empty on that path)
         self._pending_bwd_fences: dict = {}
 
     @property
     def n_devices(self) -> int:
-        return len({int(_dev(s.device_id).index or 0) for s in self.stages})
+        return len({str(_dev(s.device_id)) for s in self.stages})
+
+    # ---------------------------------------------------------- weights
+
+    def _param_upload_stream(self, device_id) -> Optional["torch.cuda.Stream"]:
+        """The side stream streamed layers of ``device_id`` upload on (None when the
+        stage's weights are made resident group by group instead)."""
+        for stage, st in zip(self.stages, self._streamers):
+            if _dev(stage.device_id) == _dev(device_id) and st.enabled:
+                return st.stream
+        return None
+
+    def _prefetch_module(self, module: nn.Module, device_id):
+        if not self.prefetch_nf4:
+            return None
+        return prefetch_weights(module, device_id)
+
+    def _ensure_module(self, module: nn.Module, device_id, prefetch=None) -> int:
+        if self.prefetch_nf4:
+            return ensure_prefetched_weights(module, device_id, prefetch)
+        return ensure_weights(module, device_id)
+
+    def _start_bwd_look_ahead(self, gid: int) -> None:
+        """Backward of group ``gid + 1`` is starting: make group ``gid`` resident early
+        (streamed stages: its first layer's upload on the side stream)."""
+        si, a, _, _ = self._groups[gid]
+        st = self._streamers[si]
+        if st.enabled:
+            with _on(st.device):
+                st.prefetch(a)
+
+    # ---------------------------------------------------------- forward
 
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
                 labels: Optional[torch.Tensor] = None, **kwargs):
-        """Run forward through all stages; returns the loss when labels are given."""
+        """Run forward through all stages; returns the postfix's output (the loss when
+        labels are given)."""
         self._pending_bwd_fences = {}
         # the previous step's backward ran after the last check: report a kernel that gave up
         _check_status([_dev(s.device_id) for s in self.stages], "StratumPipeline.forward")
         if self._layer_timer is not None and hasattr(self._layer_timer, "update_times"):
             self._layer_timer.update_times()
-        dev0 = _dev(self.stages[0].device_id)
+        dev0 = _dev(self.stages[0].device_id) if len(self.stages) else _dev(0)
+        last = _dev(self.stages[-1].device_id) if len(self.stages) else dev0
         if input_ids.device != dev0:
             input_ids = input_ids.to(dev0, non_blocking=True)
         if labels is not None and labels.device != dev0:
             labels = labels.to(dev0, non_blocking=True)
         if attention_mask is not None and attention_mask.device != dev0:
             attention_mask = attention_mask.to(dev0, non_blocking=True)
-        tup = self.prefix(input_ids=input_ids, attention_mask=attention_mask, labels=labels, **kwargs)
+        n = len(self._groups)
+        grouped = [self._param_upload_stream(self.stages[si].device_id) is None for si, *_ in self._groups]
+        with _on(dev0):
+            self._ensure_module(self.prefix, dev0)
+            pending = self._prefetch_module(self._fwd_group_modules[0], dev0) if n and grouped[0] else None
+            tup = self.prefix(input_ids=input_ids, attention_mask=attention_mask, labels=labels, **kwargs)
+        if not isinstance(tup, tuple):
+            raise TypeError(f"StratumPipeline: the prefix must return the pipeline tuple, got {type(tup).__name__}")
         aux = _AuxState(self.n_experts, self.router_aux_coef) if (self.router_sink is not None and
                                                                   self.router_aux_coef) else None
         sink = self.router_sink if aux is not None else None
-        hidden, rest = tup[0], tup[1:]
-        for si, stage in enumerate(self.stages):
+        pending_postfix = None
+        for gid, (si, a, b, _) in enumerate(self._groups):
+            stage = self.stages[si]
             dev = _dev(stage.device_id)
-            if hidden.device != dev:
-                hidden = transfer(hidden, dev)
-                rest = _move_tree(rest, dev)
+            if tup[0].device != dev:  # stage boundary: NVLink copy of the hidden state
+                tup = (transfer(tup[0], dev),) + tuple(_move_tree(tuple(tup[1:]), dev))
+            module = self._fwd_group_modules[gid]
             with _on(dev):
-                hidden = _run_stage(stage, hidden, rest, self._streamers[si], "group", sink, aux,
-                                    self.offload_stage_inputs)
-        last = _dev(self.stages[-1].device_id)
+                if grouped[gid]:
+                    self._ensure_module(module, dev, pending)
+                    pending = None
+                # start the next group's (or the postfix's) copies before this group runs
+                if gid + 1 < n:
+                    if grouped[gid + 1]:
+                        pending = self._prefetch_module(self._fwd_group_modules[gid + 1],
+                                                        _dev(self.stages[self._groups[gid + 1][0]].device_id))
+                else:
+                    pending_postfix = self._prefetch_module(self.postfix, last)
+                snapshot = snapshot_module_buffers(module)
+                runner = _Runner(stage, a, b, self._streamers[si], "group", sink, aux, group_module=module,
+                                 buffers=snapshot,
+                                 reload=(lambda m=module, d=dev: self._ensure_module(m, d)) if grouped[gid] else None,
+                                 unload=(lambda m=module: free_weights(m)) if grouped[gid] else None)
+                out = runner.forward(tup)
+                if grouped[gid]:
+                    free_weights(module)  # at most one group's weights resident at a time
+                look = None if gid == 0 else (lambda g=gid - 1: self._start_bwd_look_ahead(g))
+                tup = anchor_explicit_group_backward(run_group=runner.recompute, group_input=tup,
+                                                     group_output=out,
+                                                     offload_input_to_cpu=self.offload_stage_inputs,
+                                                     look_ahead_upload=look,
+                                                     on_backward_complete=runner.after_backward,
+                                                     extra_terms=runner.extra_terms)
+        if tup[0].device != last:
+            tup = (transfer(tup[0], last),) + tuple(_move_tree(tuple(tup[1:]), last))
         with _on(last):
-            loss = self.postfix((hidden,) + tuple(rest))
+            self._ensure_module(self.postfix, last, pending_postfix)
+            loss = self.postfix(tup)
         if aux is not None and aux.counts is not None:
             aux.finalize(aux.counts, aux.psum, aux.rows)
             self.last_aux = aux.value.detach()
@@ -421,18 +532,11 @@ class StratumPipeline(nn.Module):
             start += len(stage.layers)
 
     def set_layer_timer(self, timer, *, adapt_every_n: int = 0) -> None:
-        """Attach a per-layer timer (stratum/pipeline.py:247-268); there is no execute plan
-        to adapt here (every layer is its own recompute group), so ``adapt_every_n`` is kept
-        for the call's shape only."""
+        """Attach a per-layer timer (stratum/pipeline.py:247-268).  Plans are not
+        adapted from its timings here (the reference's timing-driven plan search is
+        not part of this build), so ``adapt_every_n`` is kept for the call's shape."""
         self._layer_timer = timer
         self._plan_adapt_after_n = adapt_every_n
-
-    def _param_upload_stream(self, device_id: int) -> Optional["torch.cuda.Stream"]:
-        """The side stream streamed layers of ``device_id`` upload on (None when nothing streams)."""
-        for stage, st in zip(self.stages, self._streamers):
-            if _dev(stage.device_id) == _dev(device_id) and st.enabled:
-                return st.stream
-        return None
 
     def free_all_weights(self) -> None:
         """Drop every streamed layer's device copy (reference: call after backward)."""

@@ -537,6 +537,36 @@ def _is_resident(param, payload, owner, pname, device) -> bool:
     return param.data.numel() > 0 and param.data.device == device
 
 
+DEFAULT_CHUNK_UPLOAD_BYTES = 64 << 20
+
+
+@torch.no_grad()
+def copy_tensor_chunked(src: torch.Tensor, dst: torch.Tensor, *, chunk_bytes: int = DEFAULT_CHUNK_UPLOAD_BYTES,
+                        non_blocking: bool = False) -> int:
+    """Copy ``src`` into ``dst`` (same shape and dtype) in flat chunks of at most
+    ``chunk_bytes``; returns the number of copies issued (the reference's
+    stratum/layer_transfer.py:59-89 contract, used for FP16-staged weights)."""
+    if src.shape != dst.shape:
+        raise ValueError(f"shape mismatch: {tuple(src.shape)} != {tuple(dst.shape)}")
+    if src.dtype != dst.dtype:
+        raise ValueError(f"dtype mismatch: {src.dtype} != {dst.dtype}")
+    n = src.numel()
+    if n == 0:
+        return 0
+    if not dst.is_contiguous():
+        dst.copy_(src, non_blocking=non_blocking)
+        return 1
+    a = src.detach().contiguous().view(-1)
+    b = dst.view(-1)
+    step = max(1, int(chunk_bytes) // max(1, src.element_size()))
+    chunks = 0
+    for lo in range(0, n, step):
+        hi = min(n, lo + step)
+        b[lo:hi].copy_(a[lo:hi], non_blocking=non_blocking)
+        chunks += 1
+    return chunks
+
+
 @torch.no_grad()
 def ensure_weights(module: nn.Module, device_id: int) -> int:
     """Upload NF4 payloads (and move other params/buffers) for *module* to ``cuda:device_id``.
@@ -557,7 +587,7 @@ def ensure_weights(module: nn.Module, device_id: int) -> int:
             if param.data.numel() > 0 and param.data.device == device:
                 continue
             dst = torch.empty(fp16.shape, dtype=fp16.dtype, device=device)
-            dst.copy_(fp16.data, non_blocking=True)
+            copy_tensor_chunked(fp16.data, dst, non_blocking=True)
             param.data = dst
             tensors += 1
             continue

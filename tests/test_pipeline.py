@@ -214,7 +214,8 @@ def test_stratum_pipeline_keeps_the_reference_hooks():
     pipe.set_timing_recorder(rec)
     assert stages[1].timing_recorder is rec and stages[1].layer_start == 2
     pipe.set_layer_timer(None, adapt_every_n=0)
-    assert [id(m) for m in pipe._fwd_group_modules] == [id(l) for l in layers]
+    # one recompute group per layer by default: each group's module holds that layer
+    assert [[id(x) for x in m] for m in pipe._fwd_group_modules] == [[id(l)] for l in layers]
     pipe._pending_bwd_fences[99] = object()
     ids, labels = _data(1)
     pipe(ids, labels=labels).backward()
