@@ -34,6 +34,9 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
+
 namespace stratum {
 
 // Status word of the GEMM kernels (0 = ok), one per device.
@@ -839,6 +842,410 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
 
 }  // namespace dx
 
+// ====================================================== forward, 2 SMs ===
+//
+// The same forward on CTA pairs (clusters of two) sharing 2-SM tcgen05 MMAs.
+// A pair tile is 256 weight rows (the MMA's M; each CTA decodes its own 128
+// into a K-major, 128B-swizzled shared-memory A tile) x 512 tokens (two MMAs of
+// N = 256 per 16-wide K slice; each CTA stages half of each MMA's tokens).
+// Why: one thread issuing tcgen05.mma costs ~95 cycles per instruction (~120
+// with ALU-heavy warps on its sub-partition) whatever the instruction's size,
+// so only N = 256 instructions (128 tensor cycles per SM) leave the issuing
+// thread slack, and eight of them per 64-wide K step (1024 tensor cycles)
+// amortise the step's one barrier wait and one commit.  A 512-token tile on one
+// SM would need 80 KiB per stage; the pair halves the token bytes per SM.
+// With the weight tile in shared memory the decode warps are not tied to TMEM
+// lane quarters, so they run on sub-partitions 0, 2 and 3 and leave
+// sub-partition 1 to the MMA thread.  The fp32 accumulator fills TMEM (2 x 256
+// columns): a tile's epilogue runs before the next tile's mainloop.
+// Barriers: the first CTA's full[s] counts its producer's expect_tx (both CTAs'
+// token bytes: each CTA's TMA signals it) and one arrival per decode warp of
+// both CTAs; empty[s], accfull and drain are arrived on in both CTAs by
+// multicast commits; the first CTA's accempty counts both CTAs' epilogue warps.
+// Every wait is bounded, as in the single-CTA kernels.
+namespace fwd2 {
+
+constexpr int BM = 128;                        // weight rows per CTA; the pair's MMA M is 256
+constexpr int BN = 512;                        // tokens per pair tile: two MMAs of NH
+constexpr int NH = 256;                        // tokens per MMA (N)
+constexpr int CT = NH / 2;                     // tokens of each MMA staged by each CTA
+constexpr int BK = 64;                         // K per step: one NF4 block per weight row
+constexpr int XS = 3;                          // stages: this CTA's token halves + its A tile
+constexpr int WS = 6;                          // packed weight tiles (4 KiB), released by the decode warps
+constexpr int X_HALF = CT * BK * 2;            // 16 KiB: [128 tokens][64] of one MMA
+constexpr int X_BYTES = 2 * X_HALF;
+constexpr int A_BYTES = BM * BK * 2;           // 16 KiB: [128 rows][64], K-major, 128B swizzle
+constexpr int W_BYTES = BM * BK / 2;           // 4 KiB
+constexpr int CH = 64;                         // tokens per epilogue chunk
+constexpr int Y_HALF_BYTES = CH * 64 * 2;      // [64 tokens][64 rows]
+constexpr int Y_BUF_BYTES = 2 * Y_HALF_BYTES;  // one chunk (both 64-row halves); two buffers alternate
+constexpr int DQG = 2;                         // decode groups (four warps each) taking turns by K step
+constexpr int EPI_WARP0 = 16;
+constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
+constexpr int BAR_BYTES = 256;
+constexpr int SMEM_BYTES =
+    1024 + XS * (X_BYTES + A_BYTES) + 2 * Y_BUF_BYTES + WS * W_BYTES + BAR_BYTES + (16 + 256) * 4;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+static_assert((2 * XS + 2 * WS + 3) * 8 + 8 <= BAR_BYTES, "barrier area");
+
+// Decode warps: 4 * DQG warps among 4..15 that are not on sub-partition 1
+// (warp % 4 == 1), which the MMA thread keeps to itself; -1 for the others.
+__device__ __forceinline__ int dq_index(int warp) {
+    if (warp < 4 || warp >= EPI_WARP0 || (warp & 3) == 1) return -1;
+    const int a = warp - 4;
+    const int idx = a - (a + 3) / 4;
+    return idx < 4 * DQG ? idx : -1;
+}
+
+template <bool BF16, bool DQ>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                const __grid_constant__ CUtensorMap tm_xa, const __grid_constant__ CUtensorMap tm_y,
+                const FwdParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *x0 = base;                       // XS x 32 KiB (1024-aligned)
+    uint8_t *a0 = x0 + XS * X_BYTES;          // XS x 16 KiB (1024-aligned)
+    uint8_t *y0 = a0 + XS * A_BYTES;          // 2 x 16 KiB (1024-aligned)
+    uint8_t *w0 = y0 + 2 * Y_BUF_BYTES;       // WS x 4 KiB
+    uint64_t *bars = reinterpret_cast<uint64_t *>(w0 + WS * W_BYTES);
+    uint64_t *full = bars, *empty = full + XS, *wfull = empty + XS, *wempty = wfull + WS;
+    uint64_t *accfull = wempty + WS, *accempty = accfull + 1, *drain = accempty + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    float *lv_s = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES);
+    float *c2 = lv_s + 16;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool first = rank == 0;
+    const int cluster = int(cluster_id_x()), nclusters = int(n_clusters_x());
+    const int nkw = int(p.K / BK);
+    const int nk = nkw + p.lora_chunks;
+    const int ntiles = p.n_tiles * p.t_tiles;  // n_tiles counts 256-row pair tiles
+    const int my_tiles = ntiles > cluster ? (ntiles - cluster + nclusters - 1) / nclusters : 0;
+    // pair tile of this cluster's tl-th turn: weight rows from m * 256, tokens from t0
+    auto tile_of = [&](int tl, int &m, int64_t &t0, int &ntok) {
+        const int tile = cluster + tl * nclusters;
+        m = tile % p.n_tiles;
+        t0 = int64_t(tile / p.n_tiles) * BN;
+        ntok = int(p.T - t0 < BN ? p.T - t0 : BN);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < XS; ++i) {
+            mbar_init(&full[i], 1 + 2 * 4);  // the first producer's expect-tx + the owning group's warps, both CTAs
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < WS; ++i) {
+            mbar_init(&wfull[i], 1);
+            mbar_init(&wempty[i], 4);  // the owning group's four warps
+        }
+        mbar_init(accfull, 1);
+        mbar_init(accempty, 2 * 4);  // both CTAs' epilogue warps
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (threadIdx.x < 16) lv_s[threadIdx.x] = p.code16[threadIdx.x];
+    if (DQ) {
+        for (int i = threadIdx.x; i < 256; i += NUM_THREADS) c2[i] = p.w.code2[i];
+    }
+    cluster_sync();  // both CTAs' barriers exist before any remote arrival or TMA completion
+    if (warp == 1) tmem_alloc_pair(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // the first CTA's full[0] / accempty as shared::cluster addresses (8 bytes per stage)
+    const uint32_t full_c = mapa_shared(full, 0);
+    const uint32_t accempty_c = mapa_shared(accempty, 0);
+
+    if (warp == 0) {
+        // --------------------------- producer: this CTA's token halves (and xa)
+        if (lane == 0) {
+            prefetch_tensormap(&tm_x);
+            if (p.lora_chunks) prefetch_tensormap(&tm_xa);
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                int m, ntok;
+                int64_t t0;
+                tile_of(tl, m, t0, ntok);
+                const bool two = ntok > NH;  // the tile has a second MMA
+                const int ta = int(t0) + int(rank) * CT, tb = ta + NH;
+                for (int ks = 0; ks < nk; ++ks, ++it) {
+                    const int s = it % XS;
+                    if (!mbar_wait(&empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    if (first) mbar_arrive_expect_tx(&full[s], uint32_t((two ? 2 : 1) * 2 * X_HALF));  // both CTAs
+                    const CUtensorMap *map = ks < nkw ? &tm_x : &tm_xa;
+                    const int kc = (ks < nkw ? ks : ks - nkw) * BK;
+                    // zero-filled past the last token
+                    tma_load_2d_pair(x0 + s * X_BYTES, map, kc, ta, full_c + 8u * uint32_t(s));
+                    if (two) tma_load_2d_pair(x0 + s * X_BYTES + X_HALF, map, kc, tb, full_c + 8u * uint32_t(s));
+                }
+            }
+            if (first)  // the pair's copies land before either CTA exits
+                for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
+                    mbar_wait_cluster_issued(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+        }
+    } else if (warp == 2) {
+        // ------------------------------ producer: this CTA's packed weight tiles
+        if (lane == 0) {
+            prefetch_tensormap(&tm_w);
+            uint32_t wt = 0;
+            bool ok = true;
+            for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                int m, ntok;
+                int64_t t0;
+                tile_of(tl, m, t0, ntok);
+                const int row0 = m * (2 * BM) + int(rank) * BM;
+                for (int ks = 0; ks < nkw; ++ks, ++wt) {
+                    const int s = wt % WS;
+                    if (!mbar_wait(&wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&wfull[s], W_BYTES);
+                    tma_load_2d(w0 + s * W_BYTES, &tm_w, ks * (BK / 2), row0, &wfull[s]);
+                }
+            }
+            for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
+                mbar_wait_issued(&wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------ MMA issuer (first CTA of the pair)
+        if (lane == 0 && first) {
+            constexpr uint32_t idesc = idesc_f16(BF16, 2 * BM, NH);
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tl = 0; ok && tl < my_tiles; ++tl) {
+                int m, ntok;
+                int64_t t0;
+                tile_of(tl, m, t0, ntok);
+                const bool two = ntok > NH;
+                if (!mbar_wait_cluster(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int ks = 0; ks < nk; ++ks, ++it) {
+                    const int s = it % XS;
+                    if (!mbar_wait_cluster(&full[s], (it / XS) & 1, p.status, kErrTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = smem_desc_k_sw128(a0 + s * A_BYTES);
+                    const uint64_t bd = smem_desc_k_sw128(x0 + s * X_BYTES);
+#pragma unroll
+                    for (int j = 0; j < BK / 16; ++j) {
+                        mma_ss_f16_pair(tmem, ad + uint64_t(j * 2), bd + uint64_t(j * 2), idesc, (ks | j) != 0);
+                        if (two)
+                            mma_ss_f16_pair(tmem + NH, ad + uint64_t(j * 2), bd + uint64_t((X_HALF >> 4) + j * 2),
+                                            idesc, (ks | j) != 0);
+                    }
+                    mma_commit_pair(&empty[s], 0x3);
+                }
+                if (ok) mma_commit_pair(accfull, 0x3);
+            }
+            mma_commit_pair(drain, 0x3);  // every MMA done before either CTA frees TMEM
+        }
+    } else if (dq_index(warp) >= 0) {
+        // ------------------------------------------ decode warps (both CTAs)
+        const int di = dq_index(warp);
+        const int grp = di >> 2, q = di & 3;
+        const int row = q * 32 + lane;  // this lane's weight row among the CTA's 128
+        float lv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
+        const int64_t kb = p.K / BK;
+        auto row_of = [&](int tl) -> int64_t {
+            const int tile = cluster + tl * nclusters;
+            return int64_t(tile % p.n_tiles) * (2 * BM) + int64_t(rank) * BM + row;
+        };
+        auto absmax_of = [&](uint32_t it) -> float {
+            const int tl = int(it / nk), ks = int(it % nk);
+            if (tl >= my_tiles || ks >= nkw) return 0.f;
+            const int64_t n = row_of(tl);
+            if (n >= p.N) return 0.f;
+            return block_scale<DQ>(p.w, c2, n * kb + ks);
+        };
+        // this lane's 128-byte row of the A tile: 8-row groups of 1024 bytes, 16-byte
+        // chunk c of row r stored at chunk position c ^ (r % 8) (the TMA 128B swizzle)
+        const int arow = (row >> 3) * 1024 + (row & 7) * 128;
+        const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
+        float am_next = absmax_of(uint32_t(grp));
+        for (uint32_t it = uint32_t(grp); it < total; it += DQG) {
+            const float am = am_next;
+            am_next = absmax_of(it + DQG);  // one owned step ahead
+            const int tl = int(it / nk), ks = int(it % nk);
+            const int64_t n = row_of(tl);
+            uint32_t vals[32];
+            if (ks < nkw) {
+                const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
+                const int s = wt % WS;
+                if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant)))
+                    break;
+                // 32-byte swizzled tile: row r's 16-byte halves are swapped when bit 2 of r is set
+                const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * W_BYTES + row * 32);
+                const int sw = (row >> 2) & 1;
+                const uint4 p0 = src[sw], p1 = src[sw ^ 1];
+                const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+                const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
+                nf4_decode_block(t, w, vals);
+                // release the packed tile once every lane has read it; order these
+                // generic-proxy reads before the TMA refill of the slot
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&wempty[s]);
+            } else {
+                const int j0 = (ks - nkw) * BK;
+                const bool valid = n < p.N;
+#pragma unroll
+                for (int m = 0; m < 32; ++m) {
+                    const int j = j0 + 2 * m;
+                    vals[m] = (valid && j < p.r) ? __ldg(reinterpret_cast<const uint32_t *>(p.lora_b + n * p.r + j))
+                                                 : 0u;
+                }
+            }
+            const int sa = it % XS;
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+                break;
+            uint8_t *dst = a0 + sa * A_BYTES + arow;
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<uint4 *>(dst + ((c ^ (row & 7)) << 4)) =
+                    make_uint4(vals[4 * c], vals[4 * c + 1], vals[4 * c + 2], vals[4 * c + 3]);
+            fence_proxy_async_smem();  // generic-proxy writes -> visible to the pair's tcgen05.mma
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(full_c + 8u * uint32_t(sa), 1);
+        }
+    } else if (warp >= EPI_WARP0) {
+        // -------------------------------------------------- epilogue (both CTAs)
+        const int q = warp & 3;
+        const uint32_t lane_addr = uint32_t(q * 32) << 16;
+        const bool leader = warp == EPI_WARP0 && lane == 0;
+        // this thread's stmatrix row: matrix k = lane/8, row j = lane%8
+        const int kq = lane >> 3, jr = lane & 7;
+        const int tok_in = jr + 8 * (kq >> 1);  // token offset within a 16-column block
+        const int nrow = q * 32 + 8 * (kq & 1);  // + 16h: first weight row of the 8x8 matrix
+        auto release = [&]() {                   // this warp's accumulator reads are done
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(accempty_c, 1);
+        };
+        int buf = 0;
+        for (int tl = 0; tl < my_tiles; ++tl) {
+            if (!__all_sync(0xffffffffu, mbar_wait(accfull, tl & 1, p.status, kErrTimeoutEpilogue))) break;
+            tc_fence_after();
+            int m, ntok;
+            int64_t t0;
+            tile_of(tl, m, t0, ntok);
+            const int64_t n0 = int64_t(m) * (2 * BM) + int64_t(rank) * BM;
+            if (p.tma_store) {
+                // TMEM -> registers as 16x256b fragments, + bias, -> 16-bit ->
+                // stmatrix.trans into a [token][row] staging chunk of 64 tokens, one TMA
+                // store per 64-row half; two staging buffers alternate so a chunk's
+                // store drains while the next chunk is staged
+                float bias[2][2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int64_t n = n0 + q * 32 + h * 16 + (lane >> 2) + 8 * e;
+                        bias[h][e] = (p.bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+                    }
+                const int nchunks = (ntok + CH - 1) / CH;
+#pragma unroll 1
+                for (int c = 0; c < nchunks; ++c) {
+                    const int ctok = (ntok - c * CH < CH ? ntok - c * CH : CH);
+                    const int nblk = (ctok + 15) >> 4;
+                    uint8_t *yb = y0 + buf * Y_BUF_BYTES;
+                    if (leader) bulk_wait_read1();  // the store that last read this buffer is done with it
+                    named_bar_sync(1, 128);
+#pragma unroll 1
+                    for (int cb = 0; cb < nblk; cb += 2) {
+                        const bool pair = cb + 1 < nblk;  // warp-uniform
+                        uint32_t v[2][2][8];
+                        const uint32_t col = uint32_t(c * CH + cb * 16);
+                        tmem_ld_16x256b_x2(tmem + lane_addr + col, v[0][0]);
+                        tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + col, v[0][1]);
+                        if (pair) {
+                            tmem_ld_16x256b_x2(tmem + lane_addr + col + 16, v[1][0]);
+                            tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + col + 16, v[1][1]);
+                        }
+                        tmem_ld_wait();
+                        if (c == nchunks - 1 && cb + 2 >= nblk) release();  // the next tile may start
+#pragma unroll
+                        for (int b = 0; b < 2; ++b) {
+                            if (b == 1 && !pair) break;
+                            const int tok = (cb + b) * 16 + tok_in;
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                uint32_t x4[4];
+#pragma unroll
+                                for (int mm = 0; mm < 4; ++mm) {
+                                    const float bb = bias[h][mm & 1];
+                                    const float lo = __uint_as_float(v[b][h][2 * mm]) + bb;
+                                    const float hi = __uint_as_float(v[b][h][2 * mm + 1]) + bb;
+                                    x4[mm] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+                                }
+                                // registers {0,1}: rows +0, tokens +0..7; {2,3}: rows +8; {4,5}/{6,7}: tokens +8
+                                const int nr = nrow + 16 * h;
+                                const int half = nr >> 6, chunk = (nr & 63) >> 3;
+                                const uint8_t *dst = yb + half * Y_HALF_BYTES + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+                                stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
+                            }
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    named_bar_sync(1, 128);
+                    if (leader && n0 < p.N) {
+                        tma_store_2d(&tm_y, int32_t(n0), int32_t(t0 + c * CH), yb);
+                        if (n0 + 64 < p.N) tma_store_2d(&tm_y, int32_t(n0 + 64), int32_t(t0 + c * CH), yb + Y_HALF_BYTES);
+                    }
+                    if (leader) bulk_commit();  // one group per chunk (possibly empty), so the waits count chunks
+                    buf ^= 1;
+                }
+            } else {
+                // generic path (N % 8 != 0 or unaligned y): element stores
+                const int64_t n = n0 + q * 32 + lane;
+                const float bias = (n < p.N && p.bias) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+                const int nblk = (ntok + 31) >> 5;
+#pragma unroll 1
+                for (int c = 0; c < nblk; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem + lane_addr + c * 32, v);
+                    tmem_ld_wait();
+                    if (c == nblk - 1) release();
+                    if (n < p.N) {
+                        const int64_t tcb = t0 + c * 32;
+                        for (int i = 0; i < 32 && tcb + i < p.T; ++i)
+                            p.y[(tcb + i) * p.N + n] = to16<BF16>(__uint_as_float(v[i]) + bias);
+                    }
+                }
+            }
+        }
+        if (leader) bulk_wait0();  // stores complete before the CTA exits
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1 && lane == 0)  // the pair's MMAs into this CTA's TMEM are complete
+        mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown);
+    __syncwarp();
+    cluster_sync();  // neither CTA leaves while the peer may still signal its barriers
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
+    }
+}
+
+}  // namespace fwd2
+
 
 // ------------------------------------------------------------------- host --
 
@@ -917,6 +1324,83 @@ int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &
     const int grid = ntiles < sm_count() ? ntiles : sm_count();
     kern<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(mx, mw, mw2, mxa, my, p);
     return check_launch(SWIGLU ? "nf4_gemm_swiglu_fwd" : "nf4_gemm_fwd");
+}
+
+// CTA pairs of the 2-SM forward that fit on the device at once; sets the
+// kernel's shared-memory attribute first (0 on failure).
+template <typename Kern>
+int fwd2_pairs_query(Kern kern) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd2::SMEM_BYTES) != cudaSuccess)
+        return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(sm_count()), 1, 1);
+    cfg.blockDim = dim3(fwd2::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = fwd2::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sm_count() / 2;
+    }
+    return n;
+}
+
+template <bool BF16, bool DQ>
+int launch_fwd2(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mxa, const CUtensorMap &my,
+                const FwdParams &p, cudaStream_t st) {
+    auto kern = fwd2::k_nf4_gemm_fwd2<BF16, DQ>;
+    static std::atomic<int> cached[64];  // per instantiation and device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return fail(STRATUM_ERR_CUDA, "nf4_gemm_fwd: device %d out of range", dev);
+    int pairs = cached[dev].load(std::memory_order_acquire);
+    if (pairs <= 0) {
+        pairs = fwd2_pairs_query(kern);
+        if (pairs <= 0)
+            return fail(STRATUM_ERR_CUDA, "nf4_gemm_fwd: cannot set %d bytes of shared memory", fwd2::SMEM_BYTES);
+        cached[dev].store(pairs, std::memory_order_release);
+    }
+    const int ntiles = p.n_tiles * p.t_tiles;
+    const int grid = 2 * (ntiles < pairs ? ntiles : pairs);
+    kern<<<grid, fwd2::NUM_THREADS, fwd2::SMEM_BYTES, st>>>(mx, mw, mxa, my, p);
+    return check_launch("nf4_gemm_fwd");
+}
+
+// Forward kernel selection: STRATUM_FWD_AUTO, _PAIR or _SINGLE (set by
+// stratum_nf4_gemm_set_fwd_kernel; initially from STRATUM_NF4_FWD=pair|single).
+std::atomic<int> g_fwd_kernel{-1};
+
+int fwd_kernel_setting() {
+    int v = g_fwd_kernel.load(std::memory_order_relaxed);
+    if (v >= 0) return v;
+    const char *e = getenv("STRATUM_NF4_FWD");
+    v = STRATUM_FWD_AUTO;
+    if (e && !strcmp(e, "pair")) v = STRATUM_FWD_PAIR;
+    if (e && !strcmp(e, "single")) v = STRATUM_FWD_SINGLE;
+    int expected = -1;
+    g_fwd_kernel.compare_exchange_strong(expected, v);
+    return g_fwd_kernel.load(std::memory_order_relaxed);
+}
+
+// Which forward kernel: the CTA-pair kernel when its estimated makespan is
+// shorter.  A pair tile is 512 tokens x 256 rows on two SMs (512 x 128 per SM);
+// the single-CTA tile is 384 or 192 tokens x 128 rows.  Per token-row the pair
+// kernel costs ~0.75x the single-CTA 384-token tile (measured on B200).
+bool use_fwd2(int64_t T, int64_t N, int tile_tokens) {
+    const int forced = fwd_kernel_setting();
+    if (forced != STRATUM_FWD_AUTO) return forced == STRATUM_FWD_PAIR;
+    const int64_t sms = sm_count(), pairs = sms / 2;
+    const int64_t tiles1 = ((N + BM - 1) / BM) * ((T + tile_tokens - 1) / tile_tokens);
+    const int64_t tiles2 = ((N + 2 * fwd2::BM - 1) / (2 * fwd2::BM)) * ((T + fwd2::BN - 1) / fwd2::BN);
+    const double t1 = double((tiles1 + sms - 1) / sms) * tile_tokens * (tile_tokens == BNH ? 1.4 : 1.0);
+    const double t2 = double((tiles2 + pairs - 1) / pairs) * fwd2::BN * 0.75;
+    return t2 < t1;
 }
 
 template <bool BF16, bool DQ, bool PAIR>
@@ -1043,6 +1527,13 @@ int stratum_device_status(int *out, int reset, void *stream) {
     return STRATUM_OK;
 }
 
+int stratum_nf4_gemm_set_fwd_kernel(int which) {
+    STRATUM_REQUIRE(which == STRATUM_FWD_AUTO || which == STRATUM_FWD_PAIR || which == STRATUM_FWD_SINGLE,
+                    "nf4_gemm_set_fwd_kernel: unknown kernel %d", which);
+    gemm::g_fwd_kernel.store(which, std::memory_order_relaxed);
+    return STRATUM_OK;
+}
+
 int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const uint8_t *packed, const float *absmax,
                          const uint8_t *absmax_q, const float *absmax2, const float *code2, const float *offset,
                          const float *code16, int64_t N, const void *bias, int bias_dtype, const void *lora_xa,
@@ -1103,13 +1594,42 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
     p.t_tiles = int((T + p.tile_tokens - 1) / p.tile_tokens);
     p.status = status;
     p.tma_store = (reinterpret_cast<uintptr_t>(y) % 16 == 0) && (N % 8 == 0);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (gemm::use_fwd2(T, N, p.tile_tokens)) {
+        // CTA-pair kernel: 512-token x 256-row tiles, each CTA stages 128-token boxes
+        namespace f2 = gemm::fwd2;
+        p.n_tiles = int((N + 2 * f2::BM - 1) / (2 * f2::BM));
+        p.tile_tokens = f2::BN;
+        p.t_tiles = int((T + f2::BN - 1) / f2::BN);
+        rc = gemm::make_map_2d(&mx, xdt, x, uint64_t(K), uint64_t(T), uint64_t(K) * 2, f2::BK, f2::CT,
+                               CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_fwd x");
+        if (rc) return rc;
+        if (r > 0) {
+            rc = gemm::make_map_2d(&mxa, xdt, lora_xa, uint64_t(lora_chunks * f2::BK), uint64_t(T),
+                                   uint64_t(lora_chunks * f2::BK) * 2, f2::BK, f2::CT, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   "nf4_gemm_fwd xa");
+            if (rc) return rc;
+        } else {
+            mxa = mx;
+        }
+        CUtensorMap my = mx;
+        if (p.tma_store) {
+            rc = gemm::make_map_2d(&my, xdt, y, uint64_t(N), uint64_t(T), uint64_t(N) * 2, 64, f2::CH,
+                                   CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_fwd y");
+            if (rc) return rc;
+        }
+        if (bf16)
+            return dq ? gemm::launch_fwd2<true, true>(mx, mw, mxa, my, p, st)
+                      : gemm::launch_fwd2<true, false>(mx, mw, mxa, my, p, st);
+        return dq ? gemm::launch_fwd2<false, true>(mx, mw, mxa, my, p, st)
+                  : gemm::launch_fwd2<false, false>(mx, mw, mxa, my, p, st);
+    }
     CUtensorMap my = mx;
     if (p.tma_store) {
         rc = gemm::make_map_2d(&my, xdt, y, uint64_t(N), uint64_t(T), uint64_t(N) * 2, 64, gemm::BNH,
                                CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_fwd y");
         if (rc) return rc;
     }
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bf16)
         return dq ? gemm::launch_fwd<true, true, false>(mx, mw, mw, mxa, my, p, st)
                   : gemm::launch_fwd<true, false, false>(mx, mw, mw, mxa, my, p, st);

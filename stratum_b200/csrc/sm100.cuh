@@ -280,6 +280,134 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int32_t c0,
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// at most one bulk store group still reading its shared-memory source
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
+// ---- CTA pairs (clusters of two CTAs sharing 2-SM tcgen05 MMAs) ------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t n_clusters_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+
+// Every thread of both CTAs: release this CTA's prior writes, wait for the peer's.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+
+// `count` arrivals on an mbarrier given by its shared::cluster address (this CTA's
+// or the peer's), releasing this thread's prior writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr, uint32_t count) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr), "r"(count)
+                 : "memory");
+}
+
+// try_wait that acquires at cluster scope (phases completed by the peer CTA's
+// arrivals), with the same suspend hint as mbar_try_wait_sleep.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded cluster-scope wait: gives up on timeout or once another thread of the
+// grid recorded an error (as mbar_wait).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int *err, int code) {
+    if (mbar_try_wait_cluster(bar, parity, 0u)) return true;
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        if (mbar_try_wait_cluster(bar, parity, kSuspendHintNs)) return true;
+        if (*reinterpret_cast<volatile int *>(err) != 0) return false;
+        if (globaltimer() - t0 > kWaitTimeoutNs) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+}
+
+// Bounded cluster-scope wait for work already issued (teardown): does not give
+// up on another thread's error, only on the time limit (as mbar_wait_issued).
+__device__ __forceinline__ bool mbar_wait_cluster_issued(uint64_t *bar, uint32_t parity, int *err, int code) {
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        if (mbar_try_wait_cluster(bar, parity, kSuspendHintNs)) return true;
+        if (globaltimer() - t0 > kWaitTimeoutNs) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+}
+
+// 2-D TMA tile load into this CTA's shared memory whose completion (bytes) is
+// counted on an mbarrier of either CTA of the pair (`bar_cluster`, a
+// shared::cluster address), as the 2-SM MMA's producers need.  Every CTA loads
+// its own tiles: no cluster-wide broadcast form.
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const CUtensorMap *map, int32_t c0, int32_t c1,
+                                                 uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
+        : "memory");
+}
+
+// TMEM allocation shared by the CTA pair: the same warp of both CTAs executes it.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *smem_slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// 2-SM MMA issued by the pair's first CTA: D (M = 256: 128 rows in each CTA's
+// TMEM, all N columns) (+)= A (each CTA's shared memory holds its 128 rows) * B
+// (each CTA's shared memory holds N/2 of the rows of B^T); kind::f16.
+__device__ __forceinline__ void mma_ss_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// One arrival on the mbarrier at the same offset in every CTA of `cta_mask` when
+// all 2-SM MMAs issued so far by this thread complete (a completion signal, not a load).
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask)
+        : "memory");
+}
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

@@ -44,6 +44,18 @@ def lora_down(x2: torch.Tensor, lora_A: torch.Tensor, scaling: float) -> torch.T
     return xa.contiguous()
 
 
+_FWD_KERNELS = {"auto": 0, "pair": 1, "single": 2}
+
+
+def set_fwd_kernel(which: str) -> None:
+    """Forward GEMM kernel for every later ``nf4_gemm_fwd`` in this process:
+    ``"auto"`` (by estimated makespan), ``"pair"`` (512-token x 256-row tiles on
+    CTA pairs sharing 2-SM MMAs) or ``"single"`` (one-SM 384/192-token tiles)."""
+    if which not in _FWD_KERNELS:
+        raise ValueError(f"set_fwd_kernel: expected one of {sorted(_FWD_KERNELS)}, got {which!r}")
+    _lib.check(_lib.lib().stratum_nf4_gemm_set_fwd_kernel(_FWD_KERNELS[which]), "set_fwd_kernel")
+
+
 def nf4_gemm_fwd(
     x: torch.Tensor,
     packed: torch.Tensor,

@@ -18,6 +18,14 @@ DEV = "cuda"
 TOL = 1e-2
 
 
+@pytest.fixture(autouse=True, params=["single", "pair"])
+def fwd_kernel(request):
+    """Every test runs on both forward kernels: one-SM tiles and CTA pairs."""
+    ops.set_fwd_kernel(request.param)
+    yield request.param
+    ops.set_fwd_kernel("auto")
+
+
 def _make(N, K, T, dtype=torch.bfloat16, seed=0, dq=False, rank=0, bias=False):
     g = torch.Generator(device=DEV).manual_seed(seed)
     w = (torch.randn(N, K, generator=g, device=DEV) * 0.02).to(torch.float16)
@@ -106,3 +114,22 @@ def test_fwd_many_tiles_per_cta_every_tile():
         err = (y - ref).reshape(T // 256, 256, N // 128, 128)
         den = ref.reshape(T // 256, 256, N // 128, 128).pow(2).sum(dim=(1, 3)).sqrt()
         assert (err.pow(2).sum(dim=(1, 3)).sqrt() / den).max().item() < 4e-3
+
+
+@pytest.mark.parametrize(
+    "T,N,K",
+    [
+        (129, 1288, 128),  # N % 256 == 8: the second CTA of the last pair tile has no rows
+        (300, 200, 192),   # one pair tile: second MMA partial, second CTA's rows partly past N
+        (777, 1030, 64),   # N % 8 != 0: element-store epilogue
+        (1, 1288, 64),     # one token
+        (1100, 520, 320),  # last token tile of 76 tokens
+    ],
+)
+def test_fwd_ragged_tiles(T, N, K):
+    _, packed, qs, w_deq, x, b, _, _ = _make(N, K, T, seed=T, bias=True)
+    y = ops.nf4_gemm_fwd(x, packed, qs, bias=b)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    err = relative_error(y.float(), _ref(x, w_deq, b, None, None, 1.0, torch.bfloat16))
+    assert err < 4e-3, f"rel err {err}"
