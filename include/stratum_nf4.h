@@ -152,14 +152,15 @@ int stratum_nf4_dequantize_many(const stratum_nf4_tensor *tensors, int count, co
  * when `reset` is nonzero. */
 int stratum_device_status(int *out, int reset, void *stream);
 
-/* Forward GEMM kernel used by stratum_nf4_gemm_fwd: STRATUM_FWD_AUTO picks by
- * estimated makespan; PAIR forces the CTA-pair kernel (512-token x 256-row
- * tiles shared by two SMs), SINGLE the one-SM kernel (384/192-token x 128-row
- * tiles).  Process-wide; initially from STRATUM_NF4_FWD=pair|single, else AUTO.
- * Both give the same results up to fp32 summation order.  No counterpart in
- * the reference (a tuning control of this library's kernels). */
-enum stratum_fwd_kernel { STRATUM_FWD_AUTO = 0, STRATUM_FWD_PAIR = 1, STRATUM_FWD_SINGLE = 2 };
-int stratum_nf4_gemm_set_fwd_kernel(int which);
+/* GEMM kernel used by stratum_nf4_gemm_fwd and the input-gradient entry points
+ * (stratum_nf4_gemm_dx, stratum_nf4_gemm_dx_pair): STRATUM_GEMM_AUTO picks by
+ * estimated makespan; PAIR forces the CTA-pair kernels (512-token x 256-column
+ * tiles shared by two SMs), SINGLE the one-SM kernels.  Process-wide; initially
+ * from STRATUM_NF4_GEMM=pair|single, else AUTO.  Both give the same results up
+ * to fp32 summation order.  No counterpart in the reference (a tuning control
+ * of this library's kernels). */
+enum stratum_gemm_kernel { STRATUM_GEMM_AUTO = 0, STRATUM_GEMM_PAIR = 1, STRATUM_GEMM_SINGLE = 2 };
+int stratum_nf4_gemm_set_kernel(int which);
 
 /* K3+K4: fused NF4 linear forward with the LoRA update in the same accumulator.
  * Replaces NF4Linear.forward (dequantize_4bit then F.linear,

@@ -35,7 +35,7 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_abi_version": (_int, []),
     "stratum_last_error": (ctypes.c_char_p, []),
     "stratum_launch_count": (ctypes.c_uint64, []),
-    "stratum_nf4_gemm_set_fwd_kernel": (_int, [_int]),
+    "stratum_nf4_gemm_set_kernel": (_int, [_int]),
     "stratum_set_device": (_int, [_int]),
     "stratum_nf4_quantize": (_int, [_vp, _int, _i64, _int, _vp, _vp, _vp, _vp]),
     "stratum_nf4_dq_workspace_bytes": (_sz, [_i64]),

@@ -842,12 +842,13 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
 
 }  // namespace dx
 
-// ====================================================== forward, 2 SMs ===
+// ================================================ CTA-pair GEMMs (2 SMs) ===
 //
-// The same forward on CTA pairs (clusters of two) sharing 2-SM tcgen05 MMAs.
-// A pair tile is 256 weight rows (the MMA's M; each CTA decodes its own 128
-// into a K-major, 128B-swizzled shared-memory A tile) x 512 tokens (two MMAs of
-// N = 256 per 16-wide K slice; each CTA stages half of each MMA's tokens).
+// The forward and the input gradient on CTA pairs (clusters of two) sharing
+// 2-SM tcgen05 MMAs.  A pair tile is 256 output columns (the MMA's M: weight
+// rows for the forward, weight columns for dX; each CTA decodes its own 128
+// into a 128B-swizzled shared-memory A tile) x 512 tokens (two MMAs of N = 256
+// per 16-wide K slice; each CTA stages half of each MMA's tokens).
 // Why: one thread issuing tcgen05.mma costs ~95 cycles per instruction (~120
 // with ALU-heavy warps on its sub-partition) whatever the instruction's size,
 // so only N = 256 instructions (128 tensor cycles per SM) leave the issuing
@@ -858,35 +859,66 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
 // lane quarters, so they run on sub-partitions 0, 2 and 3 and leave
 // sub-partition 1 to the MMA thread.  The fp32 accumulator fills TMEM (2 x 256
 // columns): a tile's epilogue runs before the next tile's mainloop.
-// Barriers: the first CTA's full[s] counts its producer's expect_tx (both CTAs'
-// token bytes: each CTA's TMA signals it) and one arrival per decode warp of
-// both CTAs; empty[s], accfull and drain are arrived on in both CTAs by
-// multicast commits; the first CTA's accempty counts both CTAs' epilogue warps.
+// The decoded tile has one physical layout in both directions: decode thread t
+// writes 128-byte row t (8-row groups of 1024 bytes, 16-byte chunk c at chunk
+// position c ^ (t % 8)).  The forward's thread t decodes weight row t (64
+// values along K) and the MMA reads the tile K-major; dX's thread t decodes
+// weight row t % 64 over columns 64 * (t / 64) .. + 63, i.e. two 64-column
+// MN atoms of 8 KiB, and the MMA reads it MN-major (W^T).
+// Barriers (each waited on by threads of the CTA that holds it): the first
+// CTA's xfull[s] counts its producer's expect_tx (both CTAs' token bytes: each
+// CTA's TMA signals it), its full[s] one arrival per decode warp of both CTAs
+// and its accempty one per epilogue warp of both CTAs; xempty[s], empty[s],
+// accfull and drain are arrived on in both CTAs by multicast commits.  Arrivals
+// from the second CTA use the default (CTA-scope release) semantics, as
+// cluster barriers between the CTAs of a 2-SM MMA are signalled; a
+// cluster-scope release costs the arriving thread ~1500 cycles.
 // Every wait is bounded, as in the single-CTA kernels.
-namespace fwd2 {
+namespace pair {
 
-constexpr int BM = 128;                        // weight rows per CTA; the pair's MMA M is 256
+constexpr int BM = 128;                        // output columns per CTA; the pair's MMA M is 256
 constexpr int BN = 512;                        // tokens per pair tile: two MMAs of NH
 constexpr int NH = 256;                        // tokens per MMA (N)
 constexpr int CT = NH / 2;                     // tokens of each MMA staged by each CTA
-constexpr int BK = 64;                         // K per step: one NF4 block per weight row
-constexpr int XS = 3;                          // stages: this CTA's token halves + its A tile
-constexpr int WS = 6;                          // packed weight tiles (4 KiB), released by the decode warps
+constexpr int BK = 64;                         // contraction per step: one NF4 block per decode thread
+constexpr int XB = 4;                          // token stages: this CTA's two 128-token halves (32 KiB)
+constexpr int XA = 3;                          // A stages: this CTA's decoded 128 x 64 tile (16 KiB)
+constexpr int WS = 4;                          // packed weight tiles (4 KiB), released by the decode warps
 constexpr int X_HALF = CT * BK * 2;            // 16 KiB: [128 tokens][64] of one MMA
 constexpr int X_BYTES = 2 * X_HALF;
-constexpr int A_BYTES = BM * BK * 2;           // 16 KiB: [128 rows][64], K-major, 128B swizzle
+constexpr int A_BYTES = BM * BK * 2;           // 16 KiB
+constexpr int A_ATOM = BK * 128;               // dX: one 64-column MN atom (64 K-rows x 128 B)
 constexpr int W_BYTES = BM * BK / 2;           // 4 KiB
 constexpr int CH = 64;                         // tokens per epilogue chunk
-constexpr int Y_HALF_BYTES = CH * 64 * 2;      // [64 tokens][64 rows]
-constexpr int Y_BUF_BYTES = 2 * Y_HALF_BYTES;  // one chunk (both 64-row halves); two buffers alternate
+constexpr int YW_BYTES = CH * 32 * 2;          // one epilogue warp's chunk: [64 tokens][32 columns], 64B swizzle
+constexpr int Y_BUF_BYTES = 4 * YW_BYTES;      // the four warps' chunks; two buffers per warp alternate
 constexpr int DQG = 2;                         // decode groups (four warps each) taking turns by K step
 constexpr int EPI_WARP0 = 16;
 constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES =
-    1024 + XS * (X_BYTES + A_BYTES) + 2 * Y_BUF_BYTES + WS * W_BYTES + BAR_BYTES + (16 + 256) * 4;
+    1024 + XB * X_BYTES + XA * A_BYTES + 2 * Y_BUF_BYTES + WS * W_BYTES + BAR_BYTES + (16 + 256) * 4;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-static_assert((2 * XS + 2 * WS + 3) * 8 + 8 <= BAR_BYTES, "barrier area");
+static_assert((2 * XB + 2 * XA + 2 * WS + 3) * 8 + 8 <= BAR_BYTES, "barrier area");
+
+struct Params {
+    WeightScales w;            // the weight (dX over two stacked weights: the first)
+    WeightScales w1;           // dX over two stacked weights: the second
+    const float *code16;
+    const void *bias;          // forward: [M] or null
+    int bias_dtype;
+    const uint16_t *lora;      // forward: lora_b [M, r]; dX: lora_a [r, M]; null when r == 0
+    int r, lora_chunks;
+    uint16_t *y;               // output [T, M]
+    int64_t T;
+    int64_t M;                 // output columns (forward: N; dX: K)
+    int64_t C;                 // contraction over the weight (forward: K; dX: N)
+    int64_t kbl;               // NF4 blocks per weight row (the weight's K / 64)
+    int nkw0;                  // dX over two weights: contraction steps over the first
+    int m_tiles, t_tiles;
+    int tma_store;
+    int *status;
+};
 
 // Decode warps: 4 * DQG warps among 4..15 that are not on sub-partition 1
 // (warp % 4 == 1), which the MMA thread keeps to itself; -1 for the others.
@@ -897,19 +929,24 @@ __device__ __forceinline__ int dq_index(int warp) {
     return idx < 4 * DQG ? idx : -1;
 }
 
-template <bool BF16, bool DQ>
+// DX: input gradient (A = W^T, MN-major); TWO_W: its contraction runs over two
+// NF4 weights stacked along N (rows [0, N0) from tm_w, the rest from tm_w2).
+template <bool BF16, bool DQ, bool DX, bool TWO_W>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
-k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                const __grid_constant__ CUtensorMap tm_xa, const __grid_constant__ CUtensorMap tm_y,
-                const FwdParams p) {
+k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_xl,
+                const __grid_constant__ CUtensorMap tm_y, const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *x0 = base;                       // XS x 32 KiB (1024-aligned)
-    uint8_t *a0 = x0 + XS * X_BYTES;          // XS x 16 KiB (1024-aligned)
-    uint8_t *y0 = a0 + XS * A_BYTES;          // 2 x 16 KiB (1024-aligned)
+    uint8_t *x0 = base;                       // XB x 32 KiB (1024-aligned)
+    uint8_t *a0 = x0 + XB * X_BYTES;          // XA x 16 KiB (1024-aligned)
+    uint8_t *y0 = a0 + XA * A_BYTES;          // 2 x 16 KiB (1024-aligned)
     uint8_t *w0 = y0 + 2 * Y_BUF_BYTES;       // WS x 4 KiB
     uint64_t *bars = reinterpret_cast<uint64_t *>(w0 + WS * W_BYTES);
-    uint64_t *full = bars, *empty = full + XS, *wfull = empty + XS, *wempty = wfull + WS;
+    // xfull[s] (first CTA): both CTAs' token bytes of stage s landed; xempty[s]: its MMAs completed.
+    // full[s] (first CTA): A tile s decoded in both CTAs; empty[s]: its MMAs completed.
+    uint64_t *xfull = bars, *xempty = xfull + XB, *full = xempty + XB, *empty = full + XA;
+    uint64_t *wfull = empty + XA, *wempty = wfull + WS;
     uint64_t *accfull = wempty + WS, *accempty = accfull + 1, *drain = accempty + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     float *lv_s = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES);
@@ -920,21 +957,25 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
     const uint32_t rank = cluster_ctarank();
     const bool first = rank == 0;
     const int cluster = int(cluster_id_x()), nclusters = int(n_clusters_x());
-    const int nkw = int(p.K / BK);
+    const int nkw = int((p.C + BK - 1) / BK);  // weight steps (dX: a ragged last step is zero-filled)
     const int nk = nkw + p.lora_chunks;
-    const int ntiles = p.n_tiles * p.t_tiles;  // n_tiles counts 256-row pair tiles
+    const int ntiles = p.m_tiles * p.t_tiles;
     const int my_tiles = ntiles > cluster ? (ntiles - cluster + nclusters - 1) / nclusters : 0;
-    // pair tile of this cluster's tl-th turn: weight rows from m * 256, tokens from t0
+    // pair tile of this cluster's tl-th turn: output columns from m * 256, tokens from t0
     auto tile_of = [&](int tl, int &m, int64_t &t0, int &ntok) {
         const int tile = cluster + tl * nclusters;
-        m = tile % p.n_tiles;
-        t0 = int64_t(tile / p.n_tiles) * BN;
+        m = tile % p.m_tiles;
+        t0 = int64_t(tile / p.m_tiles) * BN;
         ntok = int(p.T - t0 < BN ? p.T - t0 : BN);
     };
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < XS; ++i) {
-            mbar_init(&full[i], 1 + 2 * 4);  // the first producer's expect-tx + the owning group's warps, both CTAs
+        for (int i = 0; i < XB; ++i) {
+            mbar_init(&xfull[i], 1);  // the first producer's expect-tx (both CTAs' bytes)
+            mbar_init(&xempty[i], 1);
+        }
+        for (int i = 0; i < XA; ++i) {
+            mbar_init(&full[i], 2 * 4);  // the owning decode warps of both CTAs
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < WS; ++i) {
@@ -956,15 +997,16 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // the first CTA's full[0] / accempty as shared::cluster addresses (8 bytes per stage)
+    // the first CTA's xfull[0] / full[0] / accempty as shared::cluster addresses (8 bytes per stage)
+    const uint32_t xfull_c = mapa_shared(xfull, 0);
     const uint32_t full_c = mapa_shared(full, 0);
     const uint32_t accempty_c = mapa_shared(accempty, 0);
 
     if (warp == 0) {
-        // --------------------------- producer: this CTA's token halves (and xa)
+        // ------------------ producer: this CTA's token halves (and the LoRA chunks)
         if (lane == 0) {
             prefetch_tensormap(&tm_x);
-            if (p.lora_chunks) prefetch_tensormap(&tm_xa);
+            if (p.lora_chunks) prefetch_tensormap(&tm_xl);
             uint32_t it = 0;
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
@@ -974,34 +1016,35 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 const bool two = ntok > NH;  // the tile has a second MMA
                 const int ta = int(t0) + int(rank) * CT, tb = ta + NH;
                 for (int ks = 0; ks < nk; ++ks, ++it) {
-                    const int s = it % XS;
-                    if (!mbar_wait(&empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                    const int s = it % XB;
+                    if (!mbar_wait(&xempty[s], ((it / XB) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
                         ok = false;
                         break;
                     }
-                    if (first) mbar_arrive_expect_tx(&full[s], uint32_t((two ? 2 : 1) * 2 * X_HALF));  // both CTAs
-                    const CUtensorMap *map = ks < nkw ? &tm_x : &tm_xa;
+                    if (first) mbar_arrive_expect_tx(&xfull[s], uint32_t((two ? 2 : 1) * 2 * X_HALF));  // both CTAs
+                    const CUtensorMap *map = ks < nkw ? &tm_x : &tm_xl;
                     const int kc = (ks < nkw ? ks : ks - nkw) * BK;
-                    // zero-filled past the last token
-                    tma_load_2d_pair(x0 + s * X_BYTES, map, kc, ta, full_c + 8u * uint32_t(s));
-                    if (two) tma_load_2d_pair(x0 + s * X_BYTES + X_HALF, map, kc, tb, full_c + 8u * uint32_t(s));
+                    // zero-filled past the last token (and, for dX, past the last row of W)
+                    tma_load_2d_pair(x0 + s * X_BYTES, map, kc, ta, xfull_c + 8u * uint32_t(s));
+                    if (two) tma_load_2d_pair(x0 + s * X_BYTES + X_HALF, map, kc, tb, xfull_c + 8u * uint32_t(s));
                 }
             }
             if (first)  // the pair's copies land before either CTA exits
-                for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
-                    mbar_wait_cluster_issued(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+                for (uint32_t j = (it > XB ? it - XB : 0); j < it; ++j)
+                    mbar_wait_issued(&xfull[j % XB], (j / XB) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         // ------------------------------ producer: this CTA's packed weight tiles
         if (lane == 0) {
             prefetch_tensormap(&tm_w);
+            if (TWO_W) prefetch_tensormap(&tm_w2);
             uint32_t wt = 0;
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
                 int m, ntok;
                 int64_t t0;
                 tile_of(tl, m, t0, ntok);
-                const int row0 = m * (2 * BM) + int(rank) * BM;
+                const int c0 = m * (2 * BM) + int(rank) * BM;  // this CTA's first output column
                 for (int ks = 0; ks < nkw; ++ks, ++wt) {
                     const int s = wt % WS;
                     if (!mbar_wait(&wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
@@ -1009,7 +1052,14 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                         break;
                     }
                     mbar_arrive_expect_tx(&wfull[s], W_BYTES);
-                    tma_load_2d(w0 + s * W_BYTES, &tm_w, ks * (BK / 2), row0, &wfull[s]);
+                    if constexpr (DX) {  // 64 weight rows x 128 columns (64 bytes)
+                        if (TWO_W && ks >= p.nkw0)
+                            tma_load_2d(w0 + s * W_BYTES, &tm_w2, c0 / 2, (ks - p.nkw0) * BK, &wfull[s]);
+                        else
+                            tma_load_2d(w0 + s * W_BYTES, &tm_w, c0 / 2, ks * BK, &wfull[s]);
+                    } else {  // 128 weight rows x 64 columns (32 bytes)
+                        tma_load_2d(w0 + s * W_BYTES, &tm_w, ks * (BK / 2), c0, &wfull[s]);
+                    }
                 }
             }
             for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
@@ -1018,7 +1068,7 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
     } else if (warp == 1) {
         // ------------------------------------ MMA issuer (first CTA of the pair)
         if (lane == 0 && first) {
-            constexpr uint32_t idesc = idesc_f16(BF16, 2 * BM, NH);
+            constexpr uint32_t idesc = DX ? idesc_f16_amn(BF16, 2 * BM, NH) : idesc_f16(BF16, 2 * BM, NH);
             uint32_t it = 0;
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
@@ -1026,27 +1076,33 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 int64_t t0;
                 tile_of(tl, m, t0, ntok);
                 const bool two = ntok > NH;
-                if (!mbar_wait_cluster(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) {
+                if (!mbar_wait(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
-                    const int s = it % XS;
-                    if (!mbar_wait_cluster(&full[s], (it / XS) & 1, p.status, kErrTimeoutMma)) {
+                    const int s = it % XA, sx = it % XB;
+                    if (!mbar_wait(&xfull[sx], (it / XB) & 1, p.status, kErrTimeoutMma) ||
+                        !mbar_wait(&full[s], (it / XA) & 1, p.status, kErrTimeoutMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ad = smem_desc_k_sw128(a0 + s * A_BYTES);
-                    const uint64_t bd = smem_desc_k_sw128(x0 + s * X_BYTES);
+                    // 16 contraction rows per MMA: 32 bytes along a K-major row, or two
+                    // 8-row groups (2 KiB) of the MN-major atoms
+                    const uint64_t ad = DX ? smem_desc_mn_sw128(a0 + s * A_BYTES, A_ATOM, 1024)
+                                           : smem_desc_k_sw128(a0 + s * A_BYTES);
+                    constexpr uint64_t a_step = DX ? (2048 >> 4) : 2;
+                    const uint64_t bd = smem_desc_k_sw128(x0 + sx * X_BYTES);
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j) {
-                        mma_ss_f16_pair(tmem, ad + uint64_t(j * 2), bd + uint64_t(j * 2), idesc, (ks | j) != 0);
+                        mma_ss_f16_pair(tmem, ad + j * a_step, bd + uint64_t(j * 2), idesc, (ks | j) != 0);
                         if (two)
-                            mma_ss_f16_pair(tmem + NH, ad + uint64_t(j * 2), bd + uint64_t((X_HALF >> 4) + j * 2),
-                                            idesc, (ks | j) != 0);
+                            mma_ss_f16_pair(tmem + NH, ad + j * a_step, bd + uint64_t((X_HALF >> 4) + j * 2), idesc,
+                                            (ks | j) != 0);
                     }
+                    mma_commit_pair(&xempty[sx], 0x3);
                     mma_commit_pair(&empty[s], 0x3);
                 }
                 if (ok) mma_commit_pair(accfull, 0x3);
@@ -1056,43 +1112,71 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
     } else if (dq_index(warp) >= 0) {
         // ------------------------------------------ decode warps (both CTAs)
         const int di = dq_index(warp);
-        const int grp = di >> 2, q = di & 3;
-        const int row = q * 32 + lane;  // this lane's weight row among the CTA's 128
+        const int grp = di >> 2;
+        const int tid = (di & 3) * 32 + lane;  // this thread's 128-byte row of the A tile
+        // forward: weight row tid of the CTA's 128; dX: weight row rl of the step over
+        // the 64 columns of block kb of the CTA's 128
+        const int rl = tid & 63, kb = tid >> 6;
         float lv[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
-        const int64_t kb = p.K / BK;
-        auto row_of = [&](int tl) -> int64_t {
+        // (weight row, NF4 block) this thread decodes in step it (row may be past the weight)
+        auto block_of = [&](uint32_t it, int64_t &wrow, int64_t &blk) {
+            const int tl = int(it / nk), ks = int(it % nk);
             const int tile = cluster + tl * nclusters;
-            return int64_t(tile % p.n_tiles) * (2 * BM) + int64_t(rank) * BM + row;
+            const int64_t c0 = int64_t(tile % p.m_tiles) * (2 * BM) + int64_t(rank) * BM;
+            if constexpr (DX) {
+                wrow = int64_t(ks) * BK + rl;
+                blk = c0 / 64 + kb;
+            } else {
+                wrow = c0 + tid;
+                blk = ks;
+            }
+            return ks;
         };
         auto absmax_of = [&](uint32_t it) -> float {
-            const int tl = int(it / nk), ks = int(it % nk);
-            if (tl >= my_tiles || ks >= nkw) return 0.f;
-            const int64_t n = row_of(tl);
-            if (n >= p.N) return 0.f;
-            return block_scale<DQ>(p.w, c2, n * kb + ks);
+            if (it / nk >= uint32_t(my_tiles)) return 0.f;
+            int64_t wrow, blk;
+            const int ks = block_of(it, wrow, blk);
+            if (ks >= nkw) return 0.f;
+            if constexpr (DX) {
+                if (wrow >= p.C || blk >= p.kbl) return 0.f;
+                if (TWO_W && ks >= p.nkw0)  // the second weight's code2 table is read from global memory
+                    return block_scale<DQ>(p.w1, p.w1.code2, (wrow - int64_t(p.nkw0) * BK) * p.kbl + blk);
+            } else {
+                if (wrow >= p.M) return 0.f;
+            }
+            return block_scale<DQ>(p.w, c2, wrow * p.kbl + blk);
         };
-        // this lane's 128-byte row of the A tile: 8-row groups of 1024 bytes, 16-byte
-        // chunk c of row r stored at chunk position c ^ (r % 8) (the TMA 128B swizzle)
-        const int arow = (row >> 3) * 1024 + (row & 7) * 128;
+        const int arow = (tid >> 3) * 1024 + (tid & 7) * 128;
         const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
         float am_next = absmax_of(uint32_t(grp));
         for (uint32_t it = uint32_t(grp); it < total; it += DQG) {
             const float am = am_next;
             am_next = absmax_of(it + DQG);  // one owned step ahead
-            const int tl = int(it / nk), ks = int(it % nk);
-            const int64_t n = row_of(tl);
+            int64_t wrow, blk;
+            const int ks = block_of(it, wrow, blk);
+            const int tl = int(it / nk);
             uint32_t vals[32];
             if (ks < nkw) {
                 const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
                 const int s = wt % WS;
                 if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant)))
                     break;
-                // 32-byte swizzled tile: row r's 16-byte halves are swapped when bit 2 of r is set
-                const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * W_BYTES + row * 32);
-                const int sw = (row >> 2) & 1;
-                const uint4 p0 = src[sw], p1 = src[sw ^ 1];
+                uint4 p0, p1;
+                if constexpr (DX) {
+                    // 64-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3)
+                    const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * W_BYTES + rl * 64);
+                    const int sw = (rl >> 1) & 3;
+                    p0 = src[(2 * kb) ^ sw];
+                    p1 = src[(2 * kb + 1) ^ sw];
+                } else {
+                    // 32-byte swizzle: row r's 16-byte halves are swapped when bit 2 of r is set
+                    const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * W_BYTES + tid * 32);
+                    const int sw = (tid >> 2) & 1;
+                    p0 = src[sw];
+                    p1 = src[sw ^ 1];
+                }
                 const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
                 const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
                 nf4_decode_block(t, w, vals);
@@ -1101,41 +1185,54 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&wempty[s]);
+            } else if constexpr (DX) {
+                // LoRA chunk: rank row j of lora_A, 64 columns (zero beyond r / the weight's K)
+                const int j = (ks - nkw) * BK + rl;
+                const bool ok_row = j < p.r && blk < p.kbl;
+                const uint4 *src = reinterpret_cast<const uint4 *>(p.lora + int64_t(j) * p.M + blk * 64);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint4 v = ok_row ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+                    vals[4 * c] = v.x;
+                    vals[4 * c + 1] = v.y;
+                    vals[4 * c + 2] = v.z;
+                    vals[4 * c + 3] = v.w;
+                }
             } else {
+                // LoRA chunk: lora_b row wrow, rank columns j0 .. j0 + 63 (zero beyond r / N)
                 const int j0 = (ks - nkw) * BK;
-                const bool valid = n < p.N;
+                const bool valid = wrow < p.M;
 #pragma unroll
                 for (int m = 0; m < 32; ++m) {
                     const int j = j0 + 2 * m;
-                    vals[m] = (valid && j < p.r) ? __ldg(reinterpret_cast<const uint32_t *>(p.lora_b + n * p.r + j))
+                    vals[m] = (valid && j < p.r) ? __ldg(reinterpret_cast<const uint32_t *>(p.lora + wrow * p.r + j))
                                                  : 0u;
                 }
             }
-            const int sa = it % XS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+            const int sa = it % XA;
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / XA) & 1) ^ 1, p.status, kErrTimeoutDequant)))
                 break;
             uint8_t *dst = a0 + sa * A_BYTES + arow;
 #pragma unroll
             for (int c = 0; c < 8; ++c)
-                *reinterpret_cast<uint4 *>(dst + ((c ^ (row & 7)) << 4)) =
+                *reinterpret_cast<uint4 *>(dst + ((c ^ (tid & 7)) << 4)) =
                     make_uint4(vals[4 * c], vals[4 * c + 1], vals[4 * c + 2], vals[4 * c + 3]);
             fence_proxy_async_smem();  // generic-proxy writes -> visible to the pair's tcgen05.mma
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(full_c + 8u * uint32_t(sa), 1);
+            if (lane == 0) mbar_arrive_remote(full_c + 8u * uint32_t(sa));
         }
     } else if (warp >= EPI_WARP0) {
         // -------------------------------------------------- epilogue (both CTAs)
         const int q = warp & 3;
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
-        const bool leader = warp == EPI_WARP0 && lane == 0;
         // this thread's stmatrix row: matrix k = lane/8, row j = lane%8
         const int kq = lane >> 3, jr = lane & 7;
         const int tok_in = jr + 8 * (kq >> 1);  // token offset within a 16-column block
-        const int nrow = q * 32 + 8 * (kq & 1);  // + 16h: first weight row of the 8x8 matrix
+        const int nrow = q * 32 + 8 * (kq & 1);  // + 16h: first output column of the 8x8 matrix
         auto release = [&]() {                   // this warp's accumulator reads are done
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(accempty_c, 1);
+            if (lane == 0) mbar_arrive_remote(accempty_c);
         };
         int buf = 0;
         for (int tl = 0; tl < my_tiles; ++tl) {
@@ -1146,34 +1243,35 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
             tile_of(tl, m, t0, ntok);
             const int64_t n0 = int64_t(m) * (2 * BM) + int64_t(rank) * BM;
             if (p.tma_store) {
-                // TMEM -> registers as 16x256b fragments, + bias, -> 16-bit ->
-                // stmatrix.trans into a [token][row] staging chunk of 64 tokens, one TMA
-                // store per 64-row half; two staging buffers alternate so a chunk's
-                // store drains while the next chunk is staged
+                // Each warp stages its own 32 output columns: TMEM -> registers as
+                // 16x256b fragments, + bias, -> 16-bit -> stmatrix.trans into a [token][32]
+                // chunk of 64 tokens (64-byte rows, 64B swizzle), then its own TMA store;
+                // two buffers per warp alternate, so no warp waits for another
                 float bias[2][2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const int64_t n = n0 + q * 32 + h * 16 + (lane >> 2) + 8 * e;
-                        bias[h][e] = (p.bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+                        bias[h][e] = (p.bias && n < p.M) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
                     }
+                const int64_t nw = n0 + q * 32;  // this warp's first output column
                 const int nchunks = (ntok + CH - 1) / CH;
 #pragma unroll 1
                 for (int c = 0; c < nchunks; ++c) {
                     const int ctok = (ntok - c * CH < CH ? ntok - c * CH : CH);
                     const int nblk = (ctok + 15) >> 4;
-                    uint8_t *yb = y0 + buf * Y_BUF_BYTES;
-                    if (leader) bulk_wait_read1();  // the store that last read this buffer is done with it
-                    named_bar_sync(1, 128);
+                    uint8_t *yb = y0 + (q * 2 + buf) * YW_BYTES;
+                    if (lane == 0) bulk_wait_read1();  // this warp's store that last read the buffer is done with it
+                    __syncwarp();
 #pragma unroll 1
                     for (int cb = 0; cb < nblk; cb += 2) {
-                        const bool pair = cb + 1 < nblk;  // warp-uniform
+                        const bool two_blk = cb + 1 < nblk;  // warp-uniform
                         uint32_t v[2][2][8];
                         const uint32_t col = uint32_t(c * CH + cb * 16);
                         tmem_ld_16x256b_x2(tmem + lane_addr + col, v[0][0]);
                         tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + col, v[0][1]);
-                        if (pair) {
+                        if (two_blk) {
                             tmem_ld_16x256b_x2(tmem + lane_addr + col + 16, v[1][0]);
                             tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + col + 16, v[1][1]);
                         }
@@ -1181,7 +1279,7 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                         if (c == nchunks - 1 && cb + 2 >= nblk) release();  // the next tile may start
 #pragma unroll
                         for (int b = 0; b < 2; ++b) {
-                            if (b == 1 && !pair) break;
+                            if (b == 1 && !two_blk) break;
                             const int tok = (cb + b) * 16 + tok_in;
 #pragma unroll
                             for (int h = 0; h < 2; ++h) {
@@ -1193,27 +1291,26 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                                     const float hi = __uint_as_float(v[b][h][2 * mm + 1]) + bb;
                                     x4[mm] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
                                 }
-                                // registers {0,1}: rows +0, tokens +0..7; {2,3}: rows +8; {4,5}/{6,7}: tokens +8
-                                const int nr = nrow + 16 * h;
-                                const int half = nr >> 6, chunk = (nr & 63) >> 3;
-                                const uint8_t *dst = yb + half * Y_HALF_BYTES + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+                                // registers {0,1}: columns +0, tokens +0..7; {2,3}: columns +8; {4,5}/{6,7}: tokens +8;
+                                // 16-byte chunk (kq & 1) + 2h of the token's 64-byte row, 64B swizzle
+                                const int cw = (kq & 1) + 2 * h;
+                                const uint8_t *dst = yb + tok * 64 + ((cw ^ ((tok >> 1) & 3)) << 4);
                                 stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
                             }
                         }
                     }
                     fence_proxy_async_smem();
-                    named_bar_sync(1, 128);
-                    if (leader && n0 < p.N) {
-                        tma_store_2d(&tm_y, int32_t(n0), int32_t(t0 + c * CH), yb);
-                        if (n0 + 64 < p.N) tma_store_2d(&tm_y, int32_t(n0 + 64), int32_t(t0 + c * CH), yb + Y_HALF_BYTES);
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (nw < p.M) tma_store_2d(&tm_y, int32_t(nw), int32_t(t0 + c * CH), yb);
+                        bulk_commit();  // one group per chunk (possibly empty), so the waits count chunks
                     }
-                    if (leader) bulk_commit();  // one group per chunk (possibly empty), so the waits count chunks
                     buf ^= 1;
                 }
             } else {
-                // generic path (N % 8 != 0 or unaligned y): element stores
+                // generic path (columns % 8 != 0 or unaligned output): element stores
                 const int64_t n = n0 + q * 32 + lane;
-                const float bias = (n < p.N && p.bias) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+                const float bias = (n < p.M && p.bias) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
                 const int nblk = (ntok + 31) >> 5;
 #pragma unroll 1
                 for (int c = 0; c < nblk; ++c) {
@@ -1221,15 +1318,15 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                     tmem_ld_32x32b_x32(tmem + lane_addr + c * 32, v);
                     tmem_ld_wait();
                     if (c == nblk - 1) release();
-                    if (n < p.N) {
+                    if (n < p.M) {
                         const int64_t tcb = t0 + c * 32;
                         for (int i = 0; i < 32 && tcb + i < p.T; ++i)
-                            p.y[(tcb + i) * p.N + n] = to16<BF16>(__uint_as_float(v[i]) + bias);
+                            p.y[(tcb + i) * p.M + n] = to16<BF16>(__uint_as_float(v[i]) + bias);
                     }
                 }
             }
         }
-        if (leader) bulk_wait0();  // stores complete before the CTA exits
+        if (lane == 0) bulk_wait0();  // this warp's stores complete before the CTA exits
     }
 
     tc_fence_before();
@@ -1244,7 +1341,7 @@ k_nf4_gemm_fwd2(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
     }
 }
 
-}  // namespace fwd2
+}  // namespace pair
 
 
 // ------------------------------------------------------------------- host --
@@ -1326,16 +1423,16 @@ int launch_fwd(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &
     return check_launch(SWIGLU ? "nf4_gemm_swiglu_fwd" : "nf4_gemm_fwd");
 }
 
-// CTA pairs of the 2-SM forward that fit on the device at once; sets the
-// kernel's shared-memory attribute first (0 on failure).
+// CTA pairs of a 2-SM GEMM that fit on the device at once; sets the kernel's
+// shared-memory attribute first (0 on failure).
 template <typename Kern>
-int fwd2_pairs_query(Kern kern) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd2::SMEM_BYTES) != cudaSuccess)
+int pair_count_query(Kern kern) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::SMEM_BYTES) != cudaSuccess)
         return 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(sm_count()), 1, 1);
-    cfg.blockDim = dim3(fwd2::NUM_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = fwd2::SMEM_BYTES;
+    cfg.blockDim = dim3(pair::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = pair::SMEM_BYTES;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -1351,55 +1448,58 @@ int fwd2_pairs_query(Kern kern) {
     return n;
 }
 
-template <bool BF16, bool DQ>
-int launch_fwd2(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mxa, const CUtensorMap &my,
-                const FwdParams &p, cudaStream_t st) {
-    auto kern = fwd2::k_nf4_gemm_fwd2<BF16, DQ>;
+template <bool BF16, bool DQ, bool DX, bool TWO_W>
+int launch_pair(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mw2, const CUtensorMap &mxl,
+                const CUtensorMap &my, const pair::Params &p, cudaStream_t st, const char *what) {
+    auto kern = pair::k_nf4_gemm_pair<BF16, DQ, DX, TWO_W>;
     static std::atomic<int> cached[64];  // per instantiation and device
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return fail(STRATUM_ERR_CUDA, "nf4_gemm_fwd: device %d out of range", dev);
+    if (dev < 0 || dev >= 64) return fail(STRATUM_ERR_CUDA, "%s: device %d out of range", what, dev);
     int pairs = cached[dev].load(std::memory_order_acquire);
     if (pairs <= 0) {
-        pairs = fwd2_pairs_query(kern);
-        if (pairs <= 0)
-            return fail(STRATUM_ERR_CUDA, "nf4_gemm_fwd: cannot set %d bytes of shared memory", fwd2::SMEM_BYTES);
+        pairs = pair_count_query(kern);
+        if (pairs <= 0) return fail(STRATUM_ERR_CUDA, "%s: cannot set %d bytes of shared memory", what, pair::SMEM_BYTES);
         cached[dev].store(pairs, std::memory_order_release);
     }
-    const int ntiles = p.n_tiles * p.t_tiles;
+    const int ntiles = p.m_tiles * p.t_tiles;
     const int grid = 2 * (ntiles < pairs ? ntiles : pairs);
-    kern<<<grid, fwd2::NUM_THREADS, fwd2::SMEM_BYTES, st>>>(mx, mw, mxa, my, p);
-    return check_launch("nf4_gemm_fwd");
+    kern<<<grid, pair::NUM_THREADS, pair::SMEM_BYTES, st>>>(mx, mw, mw2, mxl, my, p);
+    return check_launch(what);
 }
 
-// Forward kernel selection: STRATUM_FWD_AUTO, _PAIR or _SINGLE (set by
-// stratum_nf4_gemm_set_fwd_kernel; initially from STRATUM_NF4_FWD=pair|single).
-std::atomic<int> g_fwd_kernel{-1};
+// GEMM kernel selection: STRATUM_GEMM_AUTO, _PAIR or _SINGLE (set by
+// stratum_nf4_gemm_set_kernel; initially from STRATUM_NF4_GEMM=pair|single).
+std::atomic<int> g_gemm_kernel{-1};
 
-int fwd_kernel_setting() {
-    int v = g_fwd_kernel.load(std::memory_order_relaxed);
+int gemm_kernel_setting() {
+    int v = g_gemm_kernel.load(std::memory_order_relaxed);
     if (v >= 0) return v;
-    const char *e = getenv("STRATUM_NF4_FWD");
-    v = STRATUM_FWD_AUTO;
-    if (e && !strcmp(e, "pair")) v = STRATUM_FWD_PAIR;
-    if (e && !strcmp(e, "single")) v = STRATUM_FWD_SINGLE;
+    const char *e = getenv("STRATUM_NF4_GEMM");
+    v = STRATUM_GEMM_AUTO;
+    if (e && !strcmp(e, "pair")) v = STRATUM_GEMM_PAIR;
+    if (e && !strcmp(e, "single")) v = STRATUM_GEMM_SINGLE;
     int expected = -1;
-    g_fwd_kernel.compare_exchange_strong(expected, v);
-    return g_fwd_kernel.load(std::memory_order_relaxed);
+    g_gemm_kernel.compare_exchange_strong(expected, v);
+    return g_gemm_kernel.load(std::memory_order_relaxed);
 }
 
-// Which forward kernel: the CTA-pair kernel when its estimated makespan is
-// shorter.  A pair tile is 512 tokens x 256 rows on two SMs (512 x 128 per SM);
-// the single-CTA tile is 384 or 192 tokens x 128 rows.  Per token-row the pair
-// kernel costs ~0.75x the single-CTA 384-token tile (measured on B200).
-bool use_fwd2(int64_t T, int64_t N, int tile_tokens) {
-    const int forced = fwd_kernel_setting();
-    if (forced != STRATUM_FWD_AUTO) return forced == STRATUM_FWD_PAIR;
+// Whether the CTA-pair kernel runs a GEMM of T tokens and M output columns: by
+// estimated makespan.  A pair tile is 512 tokens x 256 columns on two SMs (512 x
+// 128 per SM); the single-CTA tile is `tile_tokens` x 128 at relative cost
+// `single_cost` per token-column, the pair tile kPairCost, in units of the
+// single-CTA forward's 384-token tile (fitted to B200 measurements over T = 1024
+// .. 8192 and 2048 .. 14336-wide weights: the one-SM forward's 192-token tile
+// costs 1.4, the one-SM input gradient's 256-token tile 1.28).
+constexpr double kPairCost = 0.93;
+bool use_pair(int64_t T, int64_t M, int tile_tokens, double single_cost) {
+    const int forced = gemm_kernel_setting();
+    if (forced != STRATUM_GEMM_AUTO) return forced == STRATUM_GEMM_PAIR;
     const int64_t sms = sm_count(), pairs = sms / 2;
-    const int64_t tiles1 = ((N + BM - 1) / BM) * ((T + tile_tokens - 1) / tile_tokens);
-    const int64_t tiles2 = ((N + 2 * fwd2::BM - 1) / (2 * fwd2::BM)) * ((T + fwd2::BN - 1) / fwd2::BN);
-    const double t1 = double((tiles1 + sms - 1) / sms) * tile_tokens * (tile_tokens == BNH ? 1.4 : 1.0);
-    const double t2 = double((tiles2 + pairs - 1) / pairs) * fwd2::BN * 0.75;
+    const int64_t tiles1 = ((M + BM - 1) / BM) * ((T + tile_tokens - 1) / tile_tokens);
+    const int64_t tiles2 = ((M + 2 * pair::BM - 1) / (2 * pair::BM)) * ((T + pair::BN - 1) / pair::BN);
+    const double t1 = double((tiles1 + sms - 1) / sms) * tile_tokens * single_cost;
+    const double t2 = double((tiles2 + pairs - 1) / pairs) * pair::BN * kPairCost;
     return t2 < t1;
 }
 
@@ -1497,6 +1597,48 @@ int dx_run(const void *dy, int dtype, int64_t T, int64_t N, const stratum_nf4_we
         if (rc) return rc;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (use_pair(T, K, dx::BN, 1.28)) {
+        // CTA-pair kernel: 512-token x 256-column tiles, each CTA stages 128-token boxes
+        pair::Params q{};
+        q.w = p.w;
+        q.w1 = p.w1;
+        q.code16 = code16;
+        q.lora = p.lora_a;
+        q.r = r;
+        q.lora_chunks = lora_chunks;
+        q.y = p.dx;
+        q.T = T;
+        q.M = K;
+        q.C = N;
+        q.kbl = K / 64;
+        q.nkw0 = p.nkw0;
+        q.m_tiles = int((K + 2 * pair::BM - 1) / (2 * pair::BM));
+        q.t_tiles = int((T + pair::BN - 1) / pair::BN);
+        q.tma_store = p.tma_store;
+        q.status = status;
+        rc = make_map_2d(&mdy, xdt, dy, uint64_t(N), uint64_t(T), uint64_t(N) * 2, pair::BK, pair::CT,
+                         CU_TENSOR_MAP_SWIZZLE_128B, what);
+        if (rc) return rc;
+        if (r > 0) {
+            rc = make_map_2d(&mdyb, xdt, lora_dyb, uint64_t(lora_chunks * 64), uint64_t(T),
+                             uint64_t(lora_chunks * 64) * 2, 64, pair::CT, CU_TENSOR_MAP_SWIZZLE_128B, what);
+            if (rc) return rc;
+        } else {
+            mdyb = mdy;
+        }
+        mdx = mdy;
+        if (q.tma_store) {
+            rc = make_map_2d(&mdx, xdt, dx_out, uint64_t(K), uint64_t(T), uint64_t(K) * 2, 32, pair::CH,
+                             CU_TENSOR_MAP_SWIZZLE_64B, what);
+            if (rc) return rc;
+        }
+#define STRATUM_DX2(B, D)                                                                  \
+    (pair ? launch_pair<B, D, true, true>(mdy, mw, mw2, mdyb, mdx, q, st, what)           \
+          : launch_pair<B, D, true, false>(mdy, mw, mw2, mdyb, mdx, q, st, what))
+        if (bf16) return dq ? STRATUM_DX2(true, true) : STRATUM_DX2(true, false);
+        return dq ? STRATUM_DX2(false, true) : STRATUM_DX2(false, false);
+#undef STRATUM_DX2
+    }
 #define STRATUM_DX(B, D) \
     (pair ? launch_dx<B, D, true>(mdy, mw, mw2, mdyb, mdx, p, st) : launch_dx<B, D, false>(mdy, mw, mw2, mdyb, mdx, p, st))
     if (bf16) return dq ? STRATUM_DX(true, true) : STRATUM_DX(true, false);
@@ -1527,10 +1669,10 @@ int stratum_device_status(int *out, int reset, void *stream) {
     return STRATUM_OK;
 }
 
-int stratum_nf4_gemm_set_fwd_kernel(int which) {
-    STRATUM_REQUIRE(which == STRATUM_FWD_AUTO || which == STRATUM_FWD_PAIR || which == STRATUM_FWD_SINGLE,
-                    "nf4_gemm_set_fwd_kernel: unknown kernel %d", which);
-    gemm::g_fwd_kernel.store(which, std::memory_order_relaxed);
+int stratum_nf4_gemm_set_kernel(int which) {
+    STRATUM_REQUIRE(which == STRATUM_GEMM_AUTO || which == STRATUM_GEMM_PAIR || which == STRATUM_GEMM_SINGLE,
+                    "nf4_gemm_set_kernel: unknown kernel %d", which);
+    gemm::g_gemm_kernel.store(which, std::memory_order_relaxed);
     return STRATUM_OK;
 }
 
@@ -1595,34 +1737,48 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
     p.status = status;
     p.tma_store = (reinterpret_cast<uintptr_t>(y) % 16 == 0) && (N % 8 == 0);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (gemm::use_fwd2(T, N, p.tile_tokens)) {
+    if (gemm::use_pair(T, N, p.tile_tokens, p.tile_tokens == gemm::BNH ? 1.4 : 1.0)) {
         // CTA-pair kernel: 512-token x 256-row tiles, each CTA stages 128-token boxes
-        namespace f2 = gemm::fwd2;
-        p.n_tiles = int((N + 2 * f2::BM - 1) / (2 * f2::BM));
-        p.tile_tokens = f2::BN;
-        p.t_tiles = int((T + f2::BN - 1) / f2::BN);
-        rc = gemm::make_map_2d(&mx, xdt, x, uint64_t(K), uint64_t(T), uint64_t(K) * 2, f2::BK, f2::CT,
+        namespace pr = gemm::pair;
+        pr::Params q{};
+        q.w = p.w;
+        q.code16 = code16;
+        q.bias = bias;
+        q.bias_dtype = bias_dtype;
+        q.lora = p.lora_b;
+        q.r = r;
+        q.lora_chunks = lora_chunks;
+        q.y = p.y;
+        q.T = T;
+        q.M = N;
+        q.C = K;
+        q.kbl = K / 64;
+        q.m_tiles = int((N + 2 * pr::BM - 1) / (2 * pr::BM));
+        q.t_tiles = int((T + pr::BN - 1) / pr::BN);
+        q.tma_store = p.tma_store;
+        q.status = status;
+        rc = gemm::make_map_2d(&mx, xdt, x, uint64_t(K), uint64_t(T), uint64_t(K) * 2, pr::BK, pr::CT,
                                CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_fwd x");
         if (rc) return rc;
         if (r > 0) {
-            rc = gemm::make_map_2d(&mxa, xdt, lora_xa, uint64_t(lora_chunks * f2::BK), uint64_t(T),
-                                   uint64_t(lora_chunks * f2::BK) * 2, f2::BK, f2::CT, CU_TENSOR_MAP_SWIZZLE_128B,
+            rc = gemm::make_map_2d(&mxa, xdt, lora_xa, uint64_t(lora_chunks * pr::BK), uint64_t(T),
+                                   uint64_t(lora_chunks * pr::BK) * 2, pr::BK, pr::CT, CU_TENSOR_MAP_SWIZZLE_128B,
                                    "nf4_gemm_fwd xa");
             if (rc) return rc;
         } else {
             mxa = mx;
         }
         CUtensorMap my = mx;
-        if (p.tma_store) {
-            rc = gemm::make_map_2d(&my, xdt, y, uint64_t(N), uint64_t(T), uint64_t(N) * 2, 64, f2::CH,
-                                   CU_TENSOR_MAP_SWIZZLE_128B, "nf4_gemm_fwd y");
+        if (q.tma_store) {
+            rc = gemm::make_map_2d(&my, xdt, y, uint64_t(N), uint64_t(T), uint64_t(N) * 2, 32, pr::CH,
+                                   CU_TENSOR_MAP_SWIZZLE_64B, "nf4_gemm_fwd y");
             if (rc) return rc;
         }
         if (bf16)
-            return dq ? gemm::launch_fwd2<true, true>(mx, mw, mxa, my, p, st)
-                      : gemm::launch_fwd2<true, false>(mx, mw, mxa, my, p, st);
-        return dq ? gemm::launch_fwd2<false, true>(mx, mw, mxa, my, p, st)
-                  : gemm::launch_fwd2<false, false>(mx, mw, mxa, my, p, st);
+            return dq ? gemm::launch_pair<true, true, false, false>(mx, mw, mw, mxa, my, q, st, "nf4_gemm_fwd")
+                      : gemm::launch_pair<true, false, false, false>(mx, mw, mw, mxa, my, q, st, "nf4_gemm_fwd");
+        return dq ? gemm::launch_pair<false, true, false, false>(mx, mw, mw, mxa, my, q, st, "nf4_gemm_fwd")
+                  : gemm::launch_pair<false, false, false, false>(mx, mw, mw, mxa, my, q, st, "nf4_gemm_fwd");
     }
     CUtensorMap my = mx;
     if (p.tma_store) {

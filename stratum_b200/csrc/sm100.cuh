@@ -320,6 +320,14 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr, uint3
                  : "memory");
 }
 
+// One arrival on an mbarrier of either CTA of the pair (shared::cluster address)
+// with the default semantics (release at CTA scope), as cluster barriers are
+// signalled between the CTAs of a 2-SM MMA: cheap, unlike a cluster-scope release,
+// which makes the arriving thread wait ~1500 cycles for its stores to drain.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // try_wait that acquires at cluster scope (phases completed by the peer CTA's
 // arrivals), with the same suspend hint as mbar_try_wait_sleep.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {

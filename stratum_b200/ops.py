@@ -44,16 +44,16 @@ def lora_down(x2: torch.Tensor, lora_A: torch.Tensor, scaling: float) -> torch.T
     return xa.contiguous()
 
 
-_FWD_KERNELS = {"auto": 0, "pair": 1, "single": 2}
+_GEMM_KERNELS = {"auto": 0, "pair": 1, "single": 2}
 
 
-def set_fwd_kernel(which: str) -> None:
-    """Forward GEMM kernel for every later ``nf4_gemm_fwd`` in this process:
-    ``"auto"`` (by estimated makespan), ``"pair"`` (512-token x 256-row tiles on
-    CTA pairs sharing 2-SM MMAs) or ``"single"`` (one-SM 384/192-token tiles)."""
-    if which not in _FWD_KERNELS:
-        raise ValueError(f"set_fwd_kernel: expected one of {sorted(_FWD_KERNELS)}, got {which!r}")
-    _lib.check(_lib.lib().stratum_nf4_gemm_set_fwd_kernel(_FWD_KERNELS[which]), "set_fwd_kernel")
+def set_gemm_kernel(which: str) -> None:
+    """Kernel for every later NF4 forward and input-gradient GEMM in this process:
+    ``"auto"`` (by estimated makespan), ``"pair"`` (512-token x 256-column tiles on
+    CTA pairs sharing 2-SM MMAs) or ``"single"`` (the one-SM kernels)."""
+    if which not in _GEMM_KERNELS:
+        raise ValueError(f"set_gemm_kernel: expected one of {sorted(_GEMM_KERNELS)}, got {which!r}")
+    _lib.check(_lib.lib().stratum_nf4_gemm_set_kernel(_GEMM_KERNELS[which]), "set_gemm_kernel")
 
 
 def nf4_gemm_fwd(

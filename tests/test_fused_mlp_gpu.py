@@ -81,12 +81,17 @@ def test_swiglu_forward_matches_unfused_kernels_bitwise(T, H, I, r, dq):
     xa = ops.mlp_lora_down(x, gate.lora_A, up.lora_A, gate.scaling, up.scaling) if r else None
     h, g_out, u_out = ops.nf4_swiglu_fwd(x, (gate.quantized, gate.quant_state), (up.quantized, up.quant_state), xa,
                                          gate.lora_B, up.lora_B)
-    with torch.no_grad():
-        g_ref = ops.nf4_gemm_fwd(x, gate.quantized, gate.quant_state, lora_A=gate.lora_A, lora_B=gate.lora_B,
-                                 scaling=gate.scaling)
-        u_ref = ops.nf4_gemm_fwd(x, up.quantized, up.quant_state, lora_A=up.lora_A, lora_B=up.lora_B,
-                                 scaling=up.scaling)
-        h_ref = FZ.swiglu(g_ref, u_ref)
+    # bitwise: the same (one-SM) kernel family sums in the same order
+    ops.set_gemm_kernel("single")
+    try:
+        with torch.no_grad():
+            g_ref = ops.nf4_gemm_fwd(x, gate.quantized, gate.quant_state, lora_A=gate.lora_A, lora_B=gate.lora_B,
+                                     scaling=gate.scaling)
+            u_ref = ops.nf4_gemm_fwd(x, up.quantized, up.quant_state, lora_A=up.lora_A, lora_B=up.lora_B,
+                                     scaling=up.scaling)
+            h_ref = FZ.swiglu(g_ref, u_ref)
+    finally:
+        ops.set_gemm_kernel("auto")
     torch.cuda.synchronize()
     from stratum_b200 import _lib
 
@@ -182,13 +187,18 @@ def test_fused_mlp_matches_hf_llama_mlp(T, H, I, r, dq):
                 assert relative_error(m.lora_B.grad.float(), p.B.grad.float()) < 1e-2, name
 
 
-def test_fused_mlp_pair_input_gradient_matches_two_passes():
+@pytest.mark.parametrize("kernel,dq", [("single", False), ("pair", False), ("pair", True)])
+def test_fused_mlp_pair_input_gradient_matches_two_passes(kernel, dq):
     """The stacked gate/up input gradient equals the sum of the two plain passes
-    within one bf16 rounding of the sum."""
+    within one bf16 rounding of the sum, on both kernels."""
     T, H, I = 640, 512, 1024
-    gate, up, _ = _mlp(H, I, 0, False, seed=9)
+    gate, up, _ = _mlp(H, I, 0, dq, seed=9)
     gen = torch.Generator(device=DEV).manual_seed(10)
     dgu = torch.randn(T, 2 * I, generator=gen, device=DEV).to(torch.bfloat16)
-    dx = ops.nf4_gemm_dx_pair(dgu, (gate.quantized, gate.quant_state), (up.quantized, up.quant_state))
+    ops.set_gemm_kernel(kernel)
+    try:
+        dx = ops.nf4_gemm_dx_pair(dgu, (gate.quantized, gate.quant_state), (up.quantized, up.quant_state))
+    finally:
+        ops.set_gemm_kernel("auto")
     ref = (dgu[:, :I].float() @ _w(gate)) + (dgu[:, I:].float() @ _w(up))
     assert relative_error(dx.float(), ref) < 1e-2

@@ -19,11 +19,11 @@ TOL = 1e-2
 
 
 @pytest.fixture(autouse=True, params=["single", "pair"])
-def fwd_kernel(request):
-    """Every test runs on both forward kernels: one-SM tiles and CTA pairs."""
-    ops.set_fwd_kernel(request.param)
+def gemm_kernel(request):
+    """Every test runs on both kernels: one-SM tiles and CTA pairs."""
+    ops.set_gemm_kernel(request.param)
     yield request.param
-    ops.set_fwd_kernel("auto")
+    ops.set_gemm_kernel("auto")
 
 
 def _make(N, K, T, dtype=torch.bfloat16, seed=0, dq=False, rank=0, bias=False):

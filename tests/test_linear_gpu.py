@@ -19,6 +19,14 @@ DEV = "cuda"
 TOL = 1e-2
 
 
+@pytest.fixture(autouse=True, params=["single", "pair"])
+def gemm_kernel(request):
+    """Every test runs on both kernels: one-SM tiles and CTA pairs."""
+    ops.set_gemm_kernel(request.param)
+    yield request.param
+    ops.set_gemm_kernel("auto")
+
+
 def _weight(N, K, seed=0, dq=False):
     g = torch.Generator(device=DEV).manual_seed(seed)
     w = (torch.randn(N, K, generator=g, device=DEV) * 0.02).to(torch.float16)
