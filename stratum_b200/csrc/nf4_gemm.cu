@@ -1120,28 +1120,43 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
         float lv[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
-        // (weight row, NF4 block) this thread decodes in step it (row may be past the weight)
-        auto block_of = [&](uint32_t it, int64_t &wrow, int64_t &blk) {
-            const int tl = int(it / nk), ks = int(it % nk);
-            const int tile = cluster + tl * nclusters;
-            const int64_t c0 = int64_t(tile % p.m_tiles) * (2 * BM) + int64_t(rank) * BM;
-            if constexpr (DX) {
-                wrow = int64_t(ks) * BK + rl;
-                blk = c0 / 64 + kb;
-            } else {
-                wrow = c0 + tid;
-                blk = ks;
-            }
-            return ks;
+        // A position in this group's walk over (tile turn tl, step ks): advanced
+        // by DQG steps at a time with no division in the loop (one per tile change)
+        struct Pos {
+            int tl, ks;
+            int64_t c0;  // this CTA's first output column in tile turn tl
         };
-        auto absmax_of = [&](uint32_t it) -> float {
-            if (it / nk >= uint32_t(my_tiles)) return 0.f;
+        auto set_tile = [&](Pos &q) {
+            const int tile = cluster + q.tl * nclusters;
+            q.c0 = int64_t(tile % p.m_tiles) * (2 * BM) + int64_t(rank) * BM;
+        };
+        auto advance = [&](Pos &q) {
+            q.ks += DQG;
+            if (q.ks >= nk) {
+                while (q.ks >= nk) {
+                    q.ks -= nk;
+                    ++q.tl;
+                }
+                if (q.tl < my_tiles) set_tile(q);
+            }
+        };
+        // (weight row, NF4 block) this thread decodes at q (the row may be past the weight)
+        auto block_at = [&](const Pos &q, int64_t &wrow, int64_t &blk) {
+            if constexpr (DX) {
+                wrow = int64_t(q.ks) * BK + rl;
+                blk = q.c0 / 64 + kb;
+            } else {
+                wrow = q.c0 + tid;
+                blk = q.ks;
+            }
+        };
+        auto absmax_at = [&](const Pos &q) -> float {
+            if (q.tl >= my_tiles || q.ks >= nkw) return 0.f;
             int64_t wrow, blk;
-            const int ks = block_of(it, wrow, blk);
-            if (ks >= nkw) return 0.f;
+            block_at(q, wrow, blk);
             if constexpr (DX) {
                 if (wrow >= p.C || blk >= p.kbl) return 0.f;
-                if (TWO_W && ks >= p.nkw0)  // the second weight's code2 table is read from global memory
+                if (TWO_W && q.ks >= p.nkw0)  // the second weight's code2 table is read from global memory
                     return block_scale<DQ>(p.w1, p.w1.code2, (wrow - int64_t(p.nkw0) * BK) * p.kbl + blk);
             } else {
                 if (wrow >= p.M) return 0.f;
@@ -1149,14 +1164,19 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
             return block_scale<DQ>(p.w, c2, wrow * p.kbl + blk);
         };
         const int arow = (tid >> 3) * 1024 + (tid & 7) * 128;
-        const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
-        float am_next = absmax_of(uint32_t(grp));
-        for (uint32_t it = uint32_t(grp); it < total; it += DQG) {
+        Pos cur{0, grp - DQG, 0};
+        advance(cur);  // normalises (tiles with fewer steps than the groups)
+        if (cur.tl < my_tiles) set_tile(cur);
+        Pos nxt = cur;
+        advance(nxt);
+        float am_next = absmax_at(cur);
+        uint32_t it = uint32_t(cur.tl) * uint32_t(nk) + uint32_t(cur.ks);
+        for (; cur.tl < my_tiles; it += DQG, cur = nxt, advance(nxt)) {
             const float am = am_next;
-            am_next = absmax_of(it + DQG);  // one owned step ahead
+            am_next = absmax_at(nxt);  // one owned step ahead
             int64_t wrow, blk;
-            const int ks = block_of(it, wrow, blk);
-            const int tl = int(it / nk);
+            block_at(cur, wrow, blk);
+            const int ks = cur.ks, tl = cur.tl;
             uint32_t vals[32];
             if (ks < nkw) {
                 const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
