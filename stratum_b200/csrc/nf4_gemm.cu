@@ -866,10 +866,10 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
 // weight row t % 64 over columns 64 * (t / 64) .. + 63, i.e. two 64-column
 // MN atoms of 8 KiB, and the MMA reads it MN-major (W^T).
 // Barriers (each waited on by threads of the CTA that holds it): the first
-// CTA's xfull[s] counts its producer's expect_tx (both CTAs' token bytes: each
-// CTA's TMA signals it), its full[s] one arrival per decode warp of both CTAs
-// and its accempty one per epilogue warp of both CTAs; xempty[s], empty[s],
-// accfull and drain are arrived on in both CTAs by multicast commits.  Arrivals
+// CTA's full[s] counts its producer's expect_tx (both CTAs' token bytes: each
+// CTA's TMA signals it) and one arrival per decode warp of both CTAs, its
+// accempty one per epilogue warp of both CTAs; empty[s], accfull and drain are
+// arrived on in both CTAs by multicast commits.  Arrivals
 // from the second CTA use the default (CTA-scope release) semantics, as
 // cluster barriers between the CTAs of a 2-SM MMA are signalled; a
 // cluster-scope release costs the arriving thread ~1500 cycles.
@@ -881,25 +881,24 @@ constexpr int BN = 512;                        // tokens per pair tile: two MMAs
 constexpr int NH = 256;                        // tokens per MMA (N)
 constexpr int CT = NH / 2;                     // tokens of each MMA staged by each CTA
 constexpr int BK = 64;                         // contraction per step: one NF4 block per decode thread
-constexpr int XB = 4;                          // token stages: this CTA's two 128-token halves (32 KiB)
-constexpr int XA = 3;                          // A stages: this CTA's decoded 128 x 64 tile (16 KiB)
+constexpr int XS = 4;                          // stages: this CTA's two 128-token halves (32 KiB) + its A tile (16 KiB)
 constexpr int WS = 4;                          // packed weight tiles (4 KiB), released by the decode warps
 constexpr int X_HALF = CT * BK * 2;            // 16 KiB: [128 tokens][64] of one MMA
 constexpr int X_BYTES = 2 * X_HALF;
 constexpr int A_BYTES = BM * BK * 2;           // 16 KiB
 constexpr int A_ATOM = BK * 128;               // dX: one 64-column MN atom (64 K-rows x 128 B)
 constexpr int W_BYTES = BM * BK / 2;           // 4 KiB
-constexpr int CH = 64;                         // tokens per epilogue chunk
-constexpr int YW_BYTES = CH * 32 * 2;          // one epilogue warp's chunk: [64 tokens][32 columns], 64B swizzle
+constexpr int CH = 32;                         // tokens per epilogue chunk
+constexpr int YW_BYTES = CH * 32 * 2;          // one epilogue warp's chunk: [32 tokens][32 columns], 64B swizzle
 constexpr int Y_BUF_BYTES = 4 * YW_BYTES;      // the four warps' chunks; two buffers per warp alternate
 constexpr int DQG = 2;                         // decode groups (four warps each) taking turns by K step
 constexpr int EPI_WARP0 = 16;
 constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES =
-    1024 + XB * X_BYTES + XA * A_BYTES + 2 * Y_BUF_BYTES + WS * W_BYTES + BAR_BYTES + (16 + 256) * 4;
+    1024 + XS * (X_BYTES + A_BYTES) + 2 * Y_BUF_BYTES + WS * W_BYTES + BAR_BYTES + (16 + 256) * 4;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-static_assert((2 * XB + 2 * XA + 2 * WS + 3) * 8 + 8 <= BAR_BYTES, "barrier area");
+static_assert((2 * XS + 2 * WS + 3) * 8 + 8 <= BAR_BYTES, "barrier area");
 
 struct Params {
     WeightScales w;            // the weight (dX over two stacked weights: the first)
@@ -938,15 +937,15 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 const __grid_constant__ CUtensorMap tm_y, const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *x0 = base;                       // XB x 32 KiB (1024-aligned)
-    uint8_t *a0 = x0 + XB * X_BYTES;          // XA x 16 KiB (1024-aligned)
-    uint8_t *y0 = a0 + XA * A_BYTES;          // 2 x 16 KiB (1024-aligned)
+    uint8_t *x0 = base;                       // XS x 32 KiB (1024-aligned)
+    uint8_t *a0 = x0 + XS * X_BYTES;          // XS x 16 KiB (1024-aligned)
+    uint8_t *y0 = a0 + XS * A_BYTES;          // 2 x 8 KiB (1024-aligned)
     uint8_t *w0 = y0 + 2 * Y_BUF_BYTES;       // WS x 4 KiB
     uint64_t *bars = reinterpret_cast<uint64_t *>(w0 + WS * W_BYTES);
-    // xfull[s] (first CTA): both CTAs' token bytes of stage s landed; xempty[s]: its MMAs completed.
-    // full[s] (first CTA): A tile s decoded in both CTAs; empty[s]: its MMAs completed.
-    uint64_t *xfull = bars, *xempty = xfull + XB, *full = xempty + XB, *empty = full + XA;
-    uint64_t *wfull = empty + XA, *wempty = wfull + WS;
+    // full[s] (first CTA): stage s's token bytes of both CTAs landed and its A tile is
+    // decoded in both CTAs; empty[s]: the stage's MMAs completed
+    uint64_t *full = bars, *empty = full + XS;
+    uint64_t *wfull = empty + XS, *wempty = wfull + WS;
     uint64_t *accfull = wempty + WS, *accempty = accfull + 1, *drain = accempty + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     float *lv_s = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + BAR_BYTES);
@@ -970,12 +969,8 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
     };
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < XB; ++i) {
-            mbar_init(&xfull[i], 1);  // the first producer's expect-tx (both CTAs' bytes)
-            mbar_init(&xempty[i], 1);
-        }
-        for (int i = 0; i < XA; ++i) {
-            mbar_init(&full[i], 2 * 4);  // the owning decode warps of both CTAs
+        for (int i = 0; i < XS; ++i) {
+            mbar_init(&full[i], 1 + 2 * 4);  // the first producer's expect-tx + the owning decode warps of both CTAs
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < WS; ++i) {
@@ -997,8 +992,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // the first CTA's xfull[0] / full[0] / accempty as shared::cluster addresses (8 bytes per stage)
-    const uint32_t xfull_c = mapa_shared(xfull, 0);
+    // the first CTA's full[0] / accempty as shared::cluster addresses (8 bytes per stage)
     const uint32_t full_c = mapa_shared(full, 0);
     const uint32_t accempty_c = mapa_shared(accempty, 0);
 
@@ -1016,22 +1010,22 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 const bool two = ntok > NH;  // the tile has a second MMA
                 const int ta = int(t0) + int(rank) * CT, tb = ta + NH;
                 for (int ks = 0; ks < nk; ++ks, ++it) {
-                    const int s = it % XB;
-                    if (!mbar_wait(&xempty[s], ((it / XB) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                    const int s = it % XS;
+                    if (!mbar_wait(&empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
                         ok = false;
                         break;
                     }
-                    if (first) mbar_arrive_expect_tx(&xfull[s], uint32_t((two ? 2 : 1) * 2 * X_HALF));  // both CTAs
+                    if (first) mbar_arrive_expect_tx(&full[s], uint32_t((two ? 2 : 1) * 2 * X_HALF));  // both CTAs
                     const CUtensorMap *map = ks < nkw ? &tm_x : &tm_xl;
                     const int kc = (ks < nkw ? ks : ks - nkw) * BK;
                     // zero-filled past the last token (and, for dX, past the last row of W)
-                    tma_load_2d_pair(x0 + s * X_BYTES, map, kc, ta, xfull_c + 8u * uint32_t(s));
-                    if (two) tma_load_2d_pair(x0 + s * X_BYTES + X_HALF, map, kc, tb, xfull_c + 8u * uint32_t(s));
+                    tma_load_2d_pair(x0 + s * X_BYTES, map, kc, ta, full_c + 8u * uint32_t(s));
+                    if (two) tma_load_2d_pair(x0 + s * X_BYTES + X_HALF, map, kc, tb, full_c + 8u * uint32_t(s));
                 }
             }
             if (first)  // the pair's copies land before either CTA exits
-                for (uint32_t j = (it > XB ? it - XB : 0); j < it; ++j)
-                    mbar_wait_issued(&xfull[j % XB], (j / XB) & 1, p.status, kErrTimeoutTeardown);
+                for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
+                    mbar_wait_issued(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
         }
     } else if (warp == 2) {
         // ------------------------------ producer: this CTA's packed weight tiles
@@ -1082,9 +1076,8 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
-                    const int s = it % XA, sx = it % XB;
-                    if (!mbar_wait(&xfull[sx], (it / XB) & 1, p.status, kErrTimeoutMma) ||
-                        !mbar_wait(&full[s], (it / XA) & 1, p.status, kErrTimeoutMma)) {
+                    const int s = it % XS;
+                    if (!mbar_wait(&full[s], (it / XS) & 1, p.status, kErrTimeoutMma)) {
                         ok = false;
                         break;
                     }
@@ -1094,7 +1087,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                     const uint64_t ad = DX ? smem_desc_mn_sw128(a0 + s * A_BYTES, A_ATOM, 1024)
                                            : smem_desc_k_sw128(a0 + s * A_BYTES);
                     constexpr uint64_t a_step = DX ? (2048 >> 4) : 2;
-                    const uint64_t bd = smem_desc_k_sw128(x0 + sx * X_BYTES);
+                    const uint64_t bd = smem_desc_k_sw128(x0 + s * X_BYTES);
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j) {
                         mma_ss_f16_pair(tmem, ad + j * a_step, bd + uint64_t(j * 2), idesc, (ks | j) != 0);
@@ -1102,7 +1095,6 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                             mma_ss_f16_pair(tmem + NH, ad + j * a_step, bd + uint64_t((X_HALF >> 4) + j * 2), idesc,
                                             (ks | j) != 0);
                     }
-                    mma_commit_pair(&xempty[sx], 0x3);
                     mma_commit_pair(&empty[s], 0x3);
                 }
                 if (ok) mma_commit_pair(accfull, 0x3);
@@ -1229,8 +1221,8 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                                                  : 0u;
                 }
             }
-            const int sa = it % XA;
-            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / XA) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+            const int sa = it % XS;
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
                 break;
             uint8_t *dst = a0 + sa * A_BYTES + arow;
 #pragma unroll
