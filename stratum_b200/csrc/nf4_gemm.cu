@@ -856,9 +856,11 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
 // amortise the step's one barrier wait and one commit.  A 512-token tile on one
 // SM would need 80 KiB per stage; the pair halves the token bytes per SM.
 // With the weight tile in shared memory the decode warps are not tied to TMEM
-// lane quarters, so they run on sub-partitions 0, 2 and 3 and leave
-// sub-partition 1 to the MMA thread.  The fp32 accumulator fills TMEM (2 x 256
-// columns): a tile's epilogue runs before the next tile's mainloop.
+// lane quarters (see dq_index for their placement).  The fp32 accumulator fills
+// TMEM (2 x 256 columns): a tile's epilogue runs before the next tile's
+// mainloop, so the epilogue streams: TMEM loads software-pipelined by 16-token
+// blocks, each warp's 32 x 32 chunk transposed through 2 KiB of shared memory
+// and written with 16-byte global stores (no store-completion waits).
 // The decoded tile has one physical layout in both directions: decode thread t
 // writes 128-byte row t (8-row groups of 1024 bytes, 16-byte chunk c at chunk
 // position c ^ (t % 8)).  The forward's thread t decodes weight row t (64
@@ -874,6 +876,9 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
 // cluster barriers between the CTAs of a 2-SM MMA are signalled; a
 // cluster-scope release costs the arriving thread ~1500 cycles.
 // Every wait is bounded, as in the single-CTA kernels.
+#ifndef PAIR_DQG
+#define PAIR_DQG 3
+#endif
 namespace pair {
 
 constexpr int BM = 128;                        // output columns per CTA; the pair's MMA M is 256
@@ -890,13 +895,13 @@ constexpr int A_ATOM = BK * 128;               // dX: one 64-column MN atom (64 
 constexpr int W_BYTES = BM * BK / 2;           // 4 KiB
 constexpr int CH = 32;                         // tokens per epilogue chunk
 constexpr int YW_BYTES = CH * 32 * 2;          // one epilogue warp's chunk: [32 tokens][32 columns], 64B swizzle
-constexpr int Y_BUF_BYTES = 4 * YW_BYTES;      // the four warps' chunks; two buffers per warp alternate
-constexpr int DQG = 2;                         // decode groups (four warps each) taking turns by K step
+constexpr int Y_BUF_BYTES = 4 * YW_BYTES;      // the four warps' chunks
+constexpr int DQG = PAIR_DQG;                  // decode groups (four warps each) taking turns by K step
 constexpr int EPI_WARP0 = 16;
 constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES =
-    1024 + XS * (X_BYTES + A_BYTES) + 2 * Y_BUF_BYTES + WS * W_BYTES + BAR_BYTES + (16 + 256) * 4;
+    1024 + XS * (X_BYTES + A_BYTES) + Y_BUF_BYTES + WS * W_BYTES + BAR_BYTES + (16 + 256) * 4;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 static_assert((2 * XS + 2 * WS + 3) * 8 + 8 <= BAR_BYTES, "barrier area");
 
@@ -915,14 +920,19 @@ struct Params {
     int64_t kbl;               // NF4 blocks per weight row (the weight's K / 64)
     int nkw0;                  // dX over two weights: contraction steps over the first
     int m_tiles, t_tiles;
-    int tma_store;
+    int tma_store;             // the output takes 16-byte vector stores (aligned, M % 8 == 0)
     int *status;
 };
 
-// Decode warps: 4 * DQG warps among 4..15 that are not on sub-partition 1
-// (warp % 4 == 1), which the MMA thread keeps to itself; -1 for the others.
+// Decode warps (-1 for the others): with three groups, warps 4..15 on all four
+// sub-partitions; with two, the eight among them not on sub-partition 1, which
+// then keeps the MMA thread to itself.  Three measured faster: the MMA thread
+// issues its eight MMAs in ~500 of a step's 1024 tensor cycles, so sharing its
+// sub-partition costs less than a third stage of decode slack gains.
 __device__ __forceinline__ int dq_index(int warp) {
-    if (warp < 4 || warp >= EPI_WARP0 || (warp & 3) == 1) return -1;
+    if (warp < 4 || warp >= EPI_WARP0) return -1;
+    if (DQG == 3) return warp - 4;  // warps 4..15 on all four sub-partitions
+    if ((warp & 3) == 1) return -1;
     const int a = warp - 4;
     const int idx = a - (a + 3) / 4;
     return idx < 4 * DQG ? idx : -1;
@@ -934,13 +944,14 @@ template <bool BF16, bool DQ, bool DX, bool TWO_W>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                 const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_xl,
-                const __grid_constant__ CUtensorMap tm_y, const Params p) {
+                const __grid_constant__ CUtensorMap tm_y /* unused: y is written with vector stores */,
+                const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *x0 = base;                       // XS x 32 KiB (1024-aligned)
     uint8_t *a0 = x0 + XS * X_BYTES;          // XS x 16 KiB (1024-aligned)
-    uint8_t *y0 = a0 + XS * A_BYTES;          // 2 x 8 KiB (1024-aligned)
-    uint8_t *w0 = y0 + 2 * Y_BUF_BYTES;       // WS x 4 KiB
+    uint8_t *y0 = a0 + XS * A_BYTES;          // 4 x 2 KiB (1024-aligned)
+    uint8_t *w0 = y0 + Y_BUF_BYTES;           // WS x 4 KiB
     uint64_t *bars = reinterpret_cast<uint64_t *>(w0 + WS * W_BYTES);
     // full[s] (first CTA): stage s's token bytes of both CTAs landed and its A tile is
     // decoded in both CTAs; empty[s]: the stage's MMAs completed
@@ -1246,7 +1257,6 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(accempty_c);
         };
-        int buf = 0;
         for (int tl = 0; tl < my_tiles; ++tl) {
             if (!__all_sync(0xffffffffu, mbar_wait(accfull, tl & 1, p.status, kErrTimeoutEpilogue))) break;
             tc_fence_after();
@@ -1268,56 +1278,69 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                         bias[h][e] = (p.bias && n < p.M) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
                     }
                 const int64_t nw = n0 + q * 32;  // this warp's first output column
-                const int nchunks = (ntok + CH - 1) / CH;
-#pragma unroll 1
-                for (int c = 0; c < nchunks; ++c) {
-                    const int ctok = (ntok - c * CH < CH ? ntok - c * CH : CH);
-                    const int nblk = (ctok + 15) >> 4;
-                    uint8_t *yb = y0 + (q * 2 + buf) * YW_BYTES;
-                    if (lane == 0) bulk_wait_read1();  // this warp's store that last read the buffer is done with it
-                    __syncwarp();
-#pragma unroll 1
-                    for (int cb = 0; cb < nblk; cb += 2) {
-                        const bool two_blk = cb + 1 < nblk;  // warp-uniform
-                        uint32_t v[2][2][8];
-                        const uint32_t col = uint32_t(c * CH + cb * 16);
-                        tmem_ld_16x256b_x2(tmem + lane_addr + col, v[0][0]);
-                        tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + col, v[0][1]);
-                        if (two_blk) {
-                            tmem_ld_16x256b_x2(tmem + lane_addr + col + 16, v[1][0]);
-                            tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + col + 16, v[1][1]);
+                // 16-token blocks: block b's TMEM load is in flight while block b - 1 is
+                // converted and staged (one wait covers all loads issued, so two register
+                // buffers alternate).  A 32-token chunk (two blocks) is transposed through
+                // this warp's 2 KiB of shared memory and written with 16-byte global
+                // stores, which need no completion wait before the buffer is reused.
+                const int nblk = (ntok + 15) >> 4;
+                uint8_t *yb = y0 + q * YW_BYTES;
+                uint32_t va[2][8], vb[2][8];
+                auto ld = [&](int blk, uint32_t (&v)[2][8]) {
+                    const uint32_t col = uint32_t(blk * 16);
+                    tmem_ld_16x256b_x2(tmem + lane_addr + col, v[0]);
+                    tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + col, v[1]);
+                };
+                auto stage = [&](int blk, const uint32_t (&v)[2][8]) {
+                    const int tok = (blk & 1) * 16 + tok_in;  // token row of the 32-token chunk
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t x4[4];
+#pragma unroll
+                        for (int mm = 0; mm < 4; ++mm) {
+                            const float bb = bias[h][mm & 1];
+                            const float lo = __uint_as_float(v[h][2 * mm]) + bb;
+                            const float hi = __uint_as_float(v[h][2 * mm + 1]) + bb;
+                            x4[mm] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
                         }
+                        // registers {0,1}: columns +0, tokens +0..7; {2,3}: columns +8; {4,5}/{6,7}: tokens +8;
+                        // 16-byte chunk (kq & 1) + 2h of the token's 64-byte row, 64B swizzle
+                        const int cw = (kq & 1) + 2 * h;
+                        const uint8_t *dst = yb + tok * 64 + ((cw ^ ((tok >> 1) & 3)) << 4);
+                        stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
+                    }
+                };
+                auto flush = [&](int b0) {  // the staged chunk -> y (tokens from t0 + 16 b0)
+                    __syncwarp();
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const int piece = lane + 32 * r;  // 128 pieces of 16 bytes: 4 per token row
+                        const int tok = piece >> 2, cw = piece & 3;
+                        const uint4 v4 = *reinterpret_cast<const uint4 *>(yb + tok * 64 + ((cw ^ ((tok >> 1) & 3)) << 4));
+                        const int64_t t = t0 + b0 * 16 + tok, n = nw + cw * 8;
+                        if (t < p.T && n < p.M) *reinterpret_cast<uint4 *>(p.y + t * p.M + n) = v4;
+                    }
+                    __syncwarp();  // every lane has read the chunk before it is overwritten
+                };
+                ld(0, va);
+                tmem_ld_wait();
+                if (nblk == 1) release();  // the next tile may start
+#pragma unroll 1
+                for (int b0 = 0; b0 < nblk; b0 += 2) {
+                    const bool has1 = b0 + 1 < nblk, has2 = b0 + 2 < nblk;  // warp-uniform
+                    if (has1) ld(b0 + 1, vb);
+                    stage(b0, va);
+                    if (has1) {
                         tmem_ld_wait();
-                        if (c == nchunks - 1 && cb + 2 >= nblk) release();  // the next tile may start
-#pragma unroll
-                        for (int b = 0; b < 2; ++b) {
-                            if (b == 1 && !two_blk) break;
-                            const int tok = (cb + b) * 16 + tok_in;
-#pragma unroll
-                            for (int h = 0; h < 2; ++h) {
-                                uint32_t x4[4];
-#pragma unroll
-                                for (int mm = 0; mm < 4; ++mm) {
-                                    const float bb = bias[h][mm & 1];
-                                    const float lo = __uint_as_float(v[b][h][2 * mm]) + bb;
-                                    const float hi = __uint_as_float(v[b][h][2 * mm + 1]) + bb;
-                                    x4[mm] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
-                                }
-                                // registers {0,1}: columns +0, tokens +0..7; {2,3}: columns +8; {4,5}/{6,7}: tokens +8;
-                                // 16-byte chunk (kq & 1) + 2h of the token's 64-byte row, 64B swizzle
-                                const int cw = (kq & 1) + 2 * h;
-                                const uint8_t *dst = yb + tok * 64 + ((cw ^ ((tok >> 1) & 3)) << 4);
-                                stmatrix_x4_trans(smem_u32(dst), x4[0], x4[1], x4[2], x4[3]);
-                            }
-                        }
+                        if (b0 + 2 >= nblk) release();
                     }
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (nw < p.M) tma_store_2d(&tm_y, int32_t(nw), int32_t(t0 + c * CH), yb);
-                        bulk_commit();  // one group per chunk (possibly empty), so the waits count chunks
+                    if (has2) ld(b0 + 2, va);
+                    if (has1) stage(b0 + 1, vb);
+                    flush(b0);
+                    if (has2) {
+                        tmem_ld_wait();
+                        if (b0 + 3 >= nblk) release();
                     }
-                    buf ^= 1;
                 }
             } else {
                 // generic path (columns % 8 != 0 or unaligned output): element stores
@@ -1338,7 +1361,6 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 }
             }
         }
-        if (lane == 0) bulk_wait0();  // this warp's stores complete before the CTA exits
     }
 
     tc_fence_before();
@@ -1638,12 +1660,7 @@ int dx_run(const void *dy, int dtype, int64_t T, int64_t N, const stratum_nf4_we
         } else {
             mdyb = mdy;
         }
-        mdx = mdy;
-        if (q.tma_store) {
-            rc = make_map_2d(&mdx, xdt, dx_out, uint64_t(K), uint64_t(T), uint64_t(K) * 2, 32, pair::CH,
-                             CU_TENSOR_MAP_SWIZZLE_64B, what);
-            if (rc) return rc;
-        }
+        mdx = mdy;  // dx is written with 16-byte stores (q.tma_store: 16-byte aligned)
 #define STRATUM_DX2(B, D)                                                                  \
     (pair ? launch_pair<B, D, true, true>(mdy, mw, mw2, mdyb, mdx, q, st, what)           \
           : launch_pair<B, D, true, false>(mdy, mw, mw2, mdyb, mdx, q, st, what))
@@ -1780,12 +1797,7 @@ int stratum_nf4_gemm_fwd(const void *x, int x_dtype, int64_t T, int64_t K, const
         } else {
             mxa = mx;
         }
-        CUtensorMap my = mx;
-        if (q.tma_store) {
-            rc = gemm::make_map_2d(&my, xdt, y, uint64_t(N), uint64_t(T), uint64_t(N) * 2, 32, pr::CH,
-                                   CU_TENSOR_MAP_SWIZZLE_64B, "nf4_gemm_fwd y");
-            if (rc) return rc;
-        }
+        const CUtensorMap &my = mx;  // y is written with 16-byte stores (q.tma_store: aligned, N % 8 == 0)
         if (bf16)
             return dq ? gemm::launch_pair<true, true, false, false>(mx, mw, mw, mxa, my, q, st, "nf4_gemm_fwd")
                       : gemm::launch_pair<true, false, false, false>(mx, mw, mw, mxa, my, q, st, "nf4_gemm_fwd");
