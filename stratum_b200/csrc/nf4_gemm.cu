@@ -879,6 +879,9 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
 #ifndef PAIR_DQG
 #define PAIR_DQG 3
 #endif
+#ifndef PAIR_EPI
+#define PAIR_EPI 4
+#endif
 namespace pair {
 
 constexpr int BM = 128;                        // output columns per CTA; the pair's MMA M is 256
@@ -895,10 +898,12 @@ constexpr int A_ATOM = BK * 128;               // dX: one 64-column MN atom (64 
 constexpr int W_BYTES = BM * BK / 2;           // 4 KiB
 constexpr int CH = 32;                         // tokens per epilogue chunk
 constexpr int YW_BYTES = CH * 32 * 2;          // one epilogue warp's chunk: [32 tokens][32 columns], 64B swizzle
-constexpr int Y_BUF_BYTES = 4 * YW_BYTES;      // the four warps' chunks
+constexpr int EPI_WARPS = PAIR_EPI;            // epilogue warps: 4 (one per TMEM lane quarter) or 8 (two)
+constexpr int PART_TOK = BN / (EPI_WARPS / 4); // tokens of a tile drained by one warp
+constexpr int Y_BUF_BYTES = EPI_WARPS * YW_BYTES;  // the epilogue warps' chunks
 constexpr int DQG = PAIR_DQG;                  // decode groups (four warps each) taking turns by K step
 constexpr int EPI_WARP0 = 16;
-constexpr int NUM_THREADS = (EPI_WARP0 + 4) * 32;
+constexpr int NUM_THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES =
     1024 + XS * (X_BYTES + A_BYTES) + Y_BUF_BYTES + WS * W_BYTES + BAR_BYTES + (16 + 256) * 4;
@@ -989,7 +994,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
             mbar_init(&wempty[i], 4);  // the owning group's four warps
         }
         mbar_init(accfull, 1);
-        mbar_init(accempty, 2 * 4);  // both CTAs' epilogue warps
+        mbar_init(accempty, 2 * EPI_WARPS);  // both CTAs' epilogue warps
         mbar_init(drain, 1);
         fence_barrier_init();
     }
@@ -1120,9 +1125,6 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
         // forward: weight row tid of the CTA's 128; dX: weight row rl of the step over
         // the 64 columns of block kb of the CTA's 128
         const int rl = tid & 63, kb = tid >> 6;
-        float lv[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
         // A position in this group's walk over (tile turn tl, step ks): advanced
         // by DQG steps at a time with no division in the loop (one per tile change)
         struct Pos {
@@ -1201,7 +1203,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                     p1 = src[sw ^ 1];
                 }
                 const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-                const Nf4Tables t = nf4_build_tables<BF16>(lv, am);
+                const Nf4Tables t = nf4_build_tables<BF16>(lv_s, am);  // levels read from shared memory
                 nf4_decode_block(t, w, vals);
                 // release the packed tile once every lane has read it; order these
                 // generic-proxy reads before the TMA refill of the slot
@@ -1247,11 +1249,12 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
     } else if (warp >= EPI_WARP0) {
         // -------------------------------------------------- epilogue (both CTAs)
         const int q = warp & 3;
+        const int ew = warp - EPI_WARP0;
+        const int tok_lo = (ew >> 2) * PART_TOK;  // this warp's tokens of a tile: [tok_lo, tok_lo + PART_TOK)
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
         // this thread's stmatrix row: matrix k = lane/8, row j = lane%8
         const int kq = lane >> 3, jr = lane & 7;
         const int tok_in = jr + 8 * (kq >> 1);  // token offset within a 16-column block
-        const int nrow = q * 32 + 8 * (kq & 1);  // + 16h: first output column of the 8x8 matrix
         auto release = [&]() {                   // this warp's accumulator reads are done
             tc_fence_before();
             __syncwarp();
@@ -1283,11 +1286,12 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 // buffers alternate).  A 32-token chunk (two blocks) is transposed through
                 // this warp's 2 KiB of shared memory and written with 16-byte global
                 // stores, which need no completion wait before the buffer is reused.
-                const int nblk = (ntok + 15) >> 4;
-                uint8_t *yb = y0 + q * YW_BYTES;
+                const int ptok = ntok - tok_lo < PART_TOK ? ntok - tok_lo : PART_TOK;  // may be <= 0
+                const int nblk = ptok > 0 ? (ptok + 15) >> 4 : 0;
+                uint8_t *yb = y0 + ew * YW_BYTES;
                 uint32_t va[2][8], vb[2][8];
                 auto ld = [&](int blk, uint32_t (&v)[2][8]) {
-                    const uint32_t col = uint32_t(blk * 16);
+                    const uint32_t col = uint32_t(tok_lo + blk * 16);
                     tmem_ld_16x256b_x2(tmem + lane_addr + col, v[0]);
                     tmem_ld_16x256b_x2(tmem + lane_addr + (16u << 16) + col, v[1]);
                 };
@@ -1317,11 +1321,15 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                         const int piece = lane + 32 * r;  // 128 pieces of 16 bytes: 4 per token row
                         const int tok = piece >> 2, cw = piece & 3;
                         const uint4 v4 = *reinterpret_cast<const uint4 *>(yb + tok * 64 + ((cw ^ ((tok >> 1) & 3)) << 4));
-                        const int64_t t = t0 + b0 * 16 + tok, n = nw + cw * 8;
+                        const int64_t t = t0 + tok_lo + b0 * 16 + tok, n = nw + cw * 8;
                         if (t < p.T && n < p.M) *reinterpret_cast<uint4 *>(p.y + t * p.M + n) = v4;
                     }
                     __syncwarp();  // every lane has read the chunk before it is overwritten
                 };
+                if (nblk == 0) {
+                    release();
+                    continue;
+                }
                 ld(0, va);
                 tmem_ld_wait();
                 if (nblk == 1) release();  // the next tile may start
@@ -1346,15 +1354,17 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 // generic path (columns % 8 != 0 or unaligned output): element stores
                 const int64_t n = n0 + q * 32 + lane;
                 const float bias = (n < p.M && p.bias) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
-                const int nblk = (ntok + 31) >> 5;
+                const int ptok = ntok - tok_lo < PART_TOK ? ntok - tok_lo : PART_TOK;  // may be <= 0
+                const int nblk = ptok > 0 ? (ptok + 31) >> 5 : 0;
+                if (nblk == 0) release();
 #pragma unroll 1
                 for (int c = 0; c < nblk; ++c) {
                     uint32_t v[32];
-                    tmem_ld_32x32b_x32(tmem + lane_addr + c * 32, v);
+                    tmem_ld_32x32b_x32(tmem + lane_addr + tok_lo + c * 32, v);
                     tmem_ld_wait();
                     if (c == nblk - 1) release();
                     if (n < p.M) {
-                        const int64_t tcb = t0 + c * 32;
+                        const int64_t tcb = t0 + tok_lo + c * 32;
                         for (int i = 0; i < 32 && tcb + i < p.T; ++i)
                             p.y[(tcb + i) * p.M + n] = to16<BF16>(__uint_as_float(v[i]) + bias);
                     }
