@@ -316,20 +316,35 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             const int m = (int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles;
             return SWIGLU ? int64_t(m) * 64 + (row & 63) : int64_t(m) * BM + row;
         };
-        auto absmax_of = [&](uint32_t it) -> float {
-            const int tl = int(it / nk), ks = int(it % nk);
-            if (tl >= my_tiles || ks >= nkw) return 0.f;
-            const int64_t n = row_of(tl);
-            if (n >= p.N) return 0.f;
-            return block_scale<DQ>(ws, c2, n * kb + ks);
+        // (tile turn, step) of a position in the group's walk, advanced DQG steps at a
+        // time with no division (the row is recomputed only when the tile changes)
+        struct Pos {
+            int tl, ks;
+            int64_t n;
+        };
+        auto norm = [&](Pos &q) {
+            if (q.ks < nk) return;
+            while (q.ks >= nk) {
+                q.ks -= nk;
+                ++q.tl;
+            }
+            if (q.tl < my_tiles) q.n = row_of(q.tl);
+        };
+        auto absmax_at = [&](const Pos &q) -> float {
+            if (q.tl >= my_tiles || q.ks >= nkw || q.n >= p.N) return 0.f;
+            return block_scale<DQ>(ws, c2, q.n * kb + q.ks);
         };
         const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
-        float am_next = absmax_of(uint32_t(grp));
-        for (uint32_t it = uint32_t(grp); it < total; it += DQG) {
+        Pos cur{0, grp, row_of(0)};
+        norm(cur);
+        Pos nxt{cur.tl, cur.ks + DQG, cur.n};
+        norm(nxt);
+        float am_next = absmax_at(cur);
+        for (uint32_t it = uint32_t(grp); it < total; it += DQG, cur = nxt, nxt.ks += DQG, norm(nxt)) {
             const float am = am_next;
-            am_next = absmax_of(it + DQG);  // one owned step ahead
-            const int tl = int(it / nk), ks = int(it % nk);
-            const int64_t n = row_of(tl);
+            am_next = absmax_at(nxt);  // one owned step ahead
+            const int tl = cur.tl, ks = cur.ks;
+            const int64_t n = cur.n;
             uint32_t vals[32];
             if (ks < nkw) {
                 const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
@@ -696,17 +711,30 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
 #pragma unroll
         for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
         const int64_t kbl = p.K / 64;  // NF4 blocks per weight row
-        auto block_of = [&](uint32_t it, int64_t &wrow, int64_t &kblk) {
-            const int tl = int(it / nk), ks = int(it % nk);
-            const int tile = int(blockIdx.x) + tl * int(gridDim.x);
-            wrow = int64_t(ks) * BK + rl;
-            kblk = int64_t(tile % p.k_tiles) * 2 + kb;
-            return ks;
+        // (tile turn, step) of a position in the group's walk, advanced DQG steps at a
+        // time with no division (the column block is recomputed only when the tile changes)
+        struct Pos {
+            int tl, ks;
+            int64_t kb0;  // first NF4 column block of the tile
         };
-        auto absmax_of = [&](uint32_t it) -> float {
-            if (it / nk >= uint32_t(my_tiles)) return 0.f;
+        auto kb0_of = [&](int tl) { return int64_t((int(blockIdx.x) + tl * int(gridDim.x)) % p.k_tiles) * 2; };
+        auto norm = [&](Pos &q) {
+            if (q.ks < nk) return;
+            while (q.ks >= nk) {
+                q.ks -= nk;
+                ++q.tl;
+            }
+            if (q.tl < my_tiles) q.kb0 = kb0_of(q.tl);
+        };
+        auto block_at = [&](const Pos &q, int64_t &wrow, int64_t &kblk) {
+            wrow = int64_t(q.ks) * BK + rl;
+            kblk = q.kb0 + kb;
+            return q.ks;
+        };
+        auto absmax_at = [&](const Pos &q) -> float {
+            if (q.tl >= my_tiles) return 0.f;
             int64_t wrow, kblk;
-            const int ks = block_of(it, wrow, kblk);
+            const int ks = block_at(q, wrow, kblk);
             if (ks >= nkw || wrow >= p.N || kblk >= kbl) return 0.f;
             if (PAIR && ks >= p.nkw0)  // a row of the second weight (step-uniform choice); its code2
                 // table is read from global memory (shared memory has room for one table only)
@@ -714,13 +742,17 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
             return block_scale<DQ>(p.w, c2, wrow * kbl + kblk);
         };
         const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
-        float am_next = absmax_of(uint32_t(grp));
-        for (uint32_t it = uint32_t(grp); it < total; it += DQG) {
+        Pos cur{0, grp, kb0_of(0)};
+        norm(cur);
+        Pos nxt{cur.tl, cur.ks + DQG, cur.kb0};
+        norm(nxt);
+        float am_next = absmax_at(cur);
+        for (uint32_t it = uint32_t(grp); it < total; it += DQG, cur = nxt, nxt.ks += DQG, norm(nxt)) {
             const float am = am_next;
-            am_next = absmax_of(it + DQG);
+            am_next = absmax_at(nxt);  // one owned step ahead
             int64_t wrow, kblk;
-            const int ks = block_of(it, wrow, kblk);
-            const int tl = int(it / nk);
+            const int ks = block_at(cur, wrow, kblk);
+            const int tl = cur.tl;
             uint32_t vals[32];
             if (ks < nkw) {
                 const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);

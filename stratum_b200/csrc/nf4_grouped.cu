@@ -346,8 +346,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
 #pragma unroll
         for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
         const int64_t kb = p.K / BK;
-        auto absmax_of = [&](uint32_t it) -> float {
-            const int tl = int(it / nk), ks = int(it % nk);
+        auto absmax_at = [&](int tl, int ks) -> float {
             if (tl >= my_tiles) return 0.f;
             const Tile t = tile_at(tl);
             const int64_t grow = row < 64 ? row_lo(t) + row : row_hi(t) + (row - 64);
@@ -359,10 +358,23 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
             }
         };
         const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
-        float am_next = absmax_of(uint32_t(grp));
+        // (tile, step) of the group's next owned step, advanced without division
+        int ntl = 0, nks = grp;
+        auto step = [&]() {
+            while (nks >= nk) {
+                nks -= nk;
+                ++ntl;
+            }
+        };
+        step();
+        float am_next = absmax_at(ntl, nks);
+        nks += DQG;
+        step();
         for (uint32_t it = uint32_t(grp); it < total; it += DQG) {
             const float am = am_next;
-            am_next = absmax_of(it + DQG);
+            am_next = absmax_at(ntl, nks);  // one owned step ahead
+            nks += DQG;
+            step();
             const uint32_t wt = it;  // one weight tile per step (no LoRA chunks here)
             const int s = wt % F_WS;
             if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / F_WS) & 1, p.status, kErrTimeoutDequant))) break;
@@ -629,8 +641,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
 #pragma unroll
         for (int i = 0; i < 16; ++i) lv[i] = lv_s[i];
         const int64_t kbl = p.K / 64;
-        auto absmax_of = [&](uint32_t it) -> float {
-            const int tl = int(it / nk), ks = int(it % nk);
+        auto absmax_at = [&](int tl, int ks) -> float {
             if (tl >= my_tiles) return 0.f;
             const Tile t = tile_at(tl);
             const int64_t kblk = int64_t(t.m) * 2 + kb;
@@ -643,10 +654,23 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
             }
         };
         const uint32_t total = uint32_t(my_tiles) * uint32_t(nk);
-        float am_next = absmax_of(uint32_t(grp));
+        // (tile, step) of the group's next owned step, advanced without division
+        int ntl = 0, nks = grp;
+        auto step = [&]() {
+            while (nks >= nk) {
+                nks -= nk;
+                ++ntl;
+            }
+        };
+        step();
+        float am_next = absmax_at(ntl, nks);
+        nks += DQG;
+        step();
         for (uint32_t it = uint32_t(grp); it < total; it += DQG) {
             const float am = am_next;
-            am_next = absmax_of(it + DQG);
+            am_next = absmax_at(ntl, nks);  // one owned step ahead
+            nks += DQG;
+            step();
             const int s = it % D_WS;
             if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (it / D_WS) & 1, p.status, kErrTimeoutDequant))) break;
             const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * D_W_BYTES + rl * 64);
