@@ -152,6 +152,13 @@ int stratum_nf4_dequantize_many(const stratum_nf4_tensor *tensors, int count, co
  * when `reset` is nonzero. */
 int stratum_device_status(int *out, int reset, void *stream);
 
+/* Diagnostic record beside the status word (8 ints, host): [0] the status, and
+ * for a wait that gave up [1] block, [2] thread, [3] the parity it waited for,
+ * [4] the barrier's shared-memory offset, [5..6] the barrier's 64-bit state.
+ * Read it before stratum_device_status with reset, which clears it.  No
+ * counterpart in the reference. */
+int stratum_device_status_detail(int *out8, void *stream);
+
 /* GEMM kernel used by stratum_nf4_gemm_fwd and the input-gradient entry points
  * (stratum_nf4_gemm_dx, stratum_nf4_gemm_dx_pair): STRATUM_GEMM_AUTO picks by
  * estimated makespan; PAIR forces the CTA-pair kernels (512-token x 256-column

@@ -35,6 +35,7 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_abi_version": (_int, []),
     "stratum_last_error": (ctypes.c_char_p, []),
     "stratum_launch_count": (ctypes.c_uint64, []),
+    "stratum_device_status_detail": (_int, [_vp, _vp]),
     "stratum_nf4_gemm_set_kernel": (_int, [_int]),
     "stratum_set_device": (_int, [_int]),
     "stratum_nf4_quantize": (_int, [_vp, _int, _i64, _int, _vp, _vp, _vp, _vp]),
@@ -168,10 +169,23 @@ def check_device_status(what: str, device=None) -> None:
     """Raise :class:`StratumError` if a GEMM kernel on ``device`` gave up a bounded wait
     (or rejected its tile table) since the last read.  The read clears the word, so
     after the error the caller may retry; the results of the failed step are invalid."""
-    st = device_status(device)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    detail = (ctypes.c_int * 8)()
+    with torch.cuda.device(dev):
+        check(lib().stratum_device_status_detail(ctypes.cast(detail, ctypes.c_void_p), stream_of(dev)),
+              "device_status_detail")
+    st = device_status(dev)
     if st != 0:
-        raise StratumError(f"{what}: a device-side wait timed out or a tile table was rejected (status 0x{st:x}); "
-                           "the kernel unwound and its outputs are invalid (the status word is now cleared)")
+        d = list(detail)
+        where = ""
+        if d[0] == st and (st & 0xf00) == 0x100:
+            where = (f"; first wait to give up: block {d[1]}, thread {d[2]}, parity {d[3]}, barrier at shared "
+                     f"offset 0x{d[4] & 0xffffffff:x}, state 0x{d[6] & 0xffffffff:08x}{d[5] & 0xffffffff:08x}")
+        elif d[0] == st and st == 0x202 and d[6] != 0:
+            where = (f"; bad tile record: block {d[1]}, tile {d[2]}: expert {d[3]}, column tile {d[4]}, "
+                     f"tokens [{d[5]}, {d[6]})")
+        raise StratumError(f"{what}: a device-side wait timed out or a tile table was rejected (status 0x{st:x})"
+                           f"{where}; the kernel unwound and its outputs are invalid (the status word is now cleared)")
 
 
 def launch_count() -> int:

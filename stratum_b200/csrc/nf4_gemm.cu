@@ -40,7 +40,8 @@
 namespace stratum {
 
 // Status word of the GEMM kernels (0 = ok), one per device.
-__device__ int g_gemm_status;
+// [0] the code, [1..6] where the first wait that gave up was (see record_timeout).
+__device__ int g_gemm_status[8];
 
 namespace gemm {
 
@@ -215,7 +216,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const bool second = p.T - t0 > BNH && p.tile_tokens > BNH;  // the tile has a second half
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % XS;
-                    if (!mbar_wait(&sm.empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                    if (!mbar_wait(&sm.empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrFwdOffset)) {
                         ok = false;
                         break;
                     }
@@ -228,7 +229,13 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 }
             }
             for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)  // every copy lands before exit
-                mbar_wait_issued(&sm.full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&sm.full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown + kErrFwdOffset);
+            // the MMAs' last completion signals (commits into this CTA's shared memory)
+            // land before the CTA exits: an arrival still in flight would hit the
+            // shared memory of whichever CTA runs on this SM next
+            if (ok)
+                for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
+                    mbar_wait(&sm.empty[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown + kErrFwdOffset);
         }
     } else if (warp == 2) {
         // ---------------------------------- producer: packed weight tiles
@@ -241,7 +248,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const int m = (int(blockIdx.x) + tl * int(gridDim.x)) % p.n_tiles;
                 for (int ks = 0; ks < nkw; ++ks, ++wt) {
                     const int s = wt % WS;
-                    if (!mbar_wait(&sm.wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                    if (!mbar_wait(&sm.wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrFwdOffset)) {
                         ok = false;
                         break;
                     }
@@ -255,7 +262,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 }
             }
             for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
-                mbar_wait_issued(&sm.wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&sm.wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown + kErrFwdOffset);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
@@ -270,13 +277,13 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const int nb = ntok > BNH ? ((ntok - BNH + 15) & ~15) : 0;
                 const uint32_t ida = idesc_f16(BF16, BM, na);
                 const uint32_t idb = idesc_f16(BF16, BM, nb > 0 ? nb : 16);
-                if (!mbar_wait(sm.accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                if (!mbar_wait(sm.accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma + kErrFwdOffset)) { ok = false; break; }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     // one wait and one commit per stage: each costs the issuing thread
                     // ~100 cycles that the tensor pipe spends idle
                     const int s = it % XS;
-                    if (!mbar_wait(&sm.full[s], (it / XS) & 1, p.status, kErrTimeoutMma)) {
+                    if (!mbar_wait(&sm.full[s], (it / XS) & 1, p.status, kErrTimeoutMma + kErrFwdOffset)) {
                         ok = false;
                         break;
                     }
@@ -295,7 +302,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 if (ok) mma_commit(sm.accfull);
             }
             mma_commit(sm.drain);  // all issued MMAs complete before TMEM is released
-            mbar_wait_issued(sm.drain, 0, p.status, kErrTimeoutTeardown);
+            mbar_wait_issued(sm.drain, 0, p.status, kErrTimeoutTeardown + kErrFwdOffset);
         }
     } else if (warp >= 4 && warp < EPI_WARP0) {
         // ---------------------------------------------------- dequant warps
@@ -350,7 +357,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
                 const int s = wt % WS;
                 // warp-uniform outcome: the tcgen05.st below is a warp collective
-                if (!__all_sync(0xffffffffu, mbar_wait(&sm.wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant)))
+                if (!__all_sync(0xffffffffu, mbar_wait(&sm.wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant + kErrFwdOffset)))
                     break;
                 // 32-byte swizzled tile: row r's 16-byte halves are swapped when bit 2 of r is set
                 const uint4 *src = reinterpret_cast<const uint4 *>(sm.w0 + s * W_BYTES + row * 32);
@@ -387,7 +394,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 }
             }
             const int sa = it % AS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&sm.empty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.empty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant + kErrFwdOffset)))
                 break;
             tc_fence_after();
             tmem_st_32x32b_x32(tmem + lane_addr + A_COL0 + sa * 32, vals);
@@ -401,7 +408,7 @@ k_nf4_gemm_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
         const bool leader = warp == EPI_WARP0 && lane == 0;
         for (int tl = 0; tl < my_tiles; ++tl) {
-            if (!__all_sync(0xffffffffu, mbar_wait(sm.accfull, tl & 1, p.status, kErrTimeoutEpilogue))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(sm.accfull, tl & 1, p.status, kErrTimeoutEpilogue + kErrFwdOffset))) break;
             tc_fence_after();
             const int tile = int(blockIdx.x) + tl * int(gridDim.x);
             const int64_t n0 = int64_t(tile % p.n_tiles) * BM;
@@ -645,14 +652,20 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 const int t0 = ((int(blockIdx.x) + tl * int(gridDim.x)) / p.k_tiles) * BN;
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % XS;
-                    if (!mbar_wait(&empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    if (!mbar_wait(&empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrDxOffset)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full[s], X_BYTES);
                     if (ks < nkw) tma_load_2d(x0 + s * X_BYTES, &tm_dy, ks * BK, t0, &full[s]);
                     else tma_load_2d(x0 + s * X_BYTES, &tm_dyb, (ks - nkw) * BK, t0, &full[s]);
                 }
             }
             for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
-                mbar_wait_issued(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown + kErrDxOffset);
+            // the MMAs' last completion signals (commits into this CTA's shared memory)
+            // land before the CTA exits: an arrival still in flight would hit the
+            // shared memory of whichever CTA runs on this SM next
+            if (ok)
+                for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
+                    mbar_wait(&empty[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown + kErrDxOffset);
         }
     } else if (warp == 2) {
         // ------------------------------- producer: packed weight tiles (64 x 128)
@@ -665,14 +678,14 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 const int k0 = ((int(blockIdx.x) + tl * int(gridDim.x)) % p.k_tiles) * BM;
                 for (int ks = 0; ks < nkw; ++ks, ++wt) {
                     const int s = wt % WS;
-                    if (!mbar_wait(&wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    if (!mbar_wait(&wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrDxOffset)) { ok = false; break; }
                     mbar_arrive_expect_tx(&wfull[s], W_BYTES);
                     if (PAIR && ks >= p.nkw0) tma_load_2d(w0 + s * W_BYTES, &tm_w2, k0 / 2, (ks - p.nkw0) * BK, &wfull[s]);
                     else tma_load_2d(w0 + s * W_BYTES, &tm_w, k0 / 2, ks * BK, &wfull[s]);
                 }
             }
             for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
-                mbar_wait_issued(&wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown + kErrDxOffset);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
@@ -682,12 +695,12 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
             bool ok = true;
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
                 const int ab = tl & 1;
-                if (!mbar_wait(&accempty[ab], ((tl >> 1) & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                if (!mbar_wait(&accempty[ab], ((tl >> 1) & 1) ^ 1, p.status, kErrTimeoutMma + kErrDxOffset)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t acc = tmem + uint32_t(ab * 256);
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % XS, sa = s;
-                    if (!mbar_wait(&full[s], (it / XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                    if (!mbar_wait(&full[s], (it / XS) & 1, p.status, kErrTimeoutMma + kErrDxOffset)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t bdesc = smem_desc_k_sw128(x0 + s * X_BYTES);
                     const uint64_t adesc = smem_desc_mn_sw128(a0 + sa * A_BYTES, A_ATOM, 1024);
@@ -699,7 +712,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 if (ok) mma_commit(&accfull[ab]);
             }
             mma_commit(drain);
-            mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown);
+            mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown + kErrDxOffset);
         }
     } else if (warp >= 4 && warp < EPI_WARP0) {
         // ---------------------------------------------------- dequant warps
@@ -757,7 +770,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
             if (ks < nkw) {
                 const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
                 const int s = wt % WS;
-                if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant))) break;
+                if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant + kErrDxOffset))) break;
                 // 64-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3)
                 const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * W_BYTES + rl * 64);
                 const int sw = (rl >> 1) & 3;
@@ -781,7 +794,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
                 }
             }
             const int sa = it % AS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / AS) & 1) ^ 1, p.status, kErrTimeoutDequant + kErrDxOffset))) break;
             // MN-major atom kb, K-row rl: 8 chunks of 16 B, XOR-swizzled by rl % 8
             uint8_t *dst = a0 + sa * A_BYTES + kb * A_ATOM + (rl >> 3) * 1024 + (rl & 7) * 128;
 #pragma unroll
@@ -801,7 +814,7 @@ k_nf4_gemm_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__
         const int nrow = q * 32 + 8 * (kq & 1);
         for (int tl = 0; tl < my_tiles; ++tl) {
             const int ab = tl & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&accfull[ab], (tl >> 1) & 1, p.status, kErrTimeoutEpilogue))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(&accfull[ab], (tl >> 1) & 1, p.status, kErrTimeoutEpilogue + kErrDxOffset))) break;
             tc_fence_after();
             const int tile = int(blockIdx.x) + tl * int(gridDim.x);
             const int64_t k0 = int64_t(tile % p.k_tiles) * BM;
@@ -1059,7 +1072,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 const int ta = int(t0) + int(rank) * CT, tb = ta + NH;
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % XS;
-                    if (!mbar_wait(&empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                    if (!mbar_wait(&empty[s], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrPairOffset)) {
                         ok = false;
                         break;
                     }
@@ -1073,7 +1086,13 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
             }
             if (first)  // the pair's copies land before either CTA exits
                 for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
-                    mbar_wait_issued(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown);
+                    mbar_wait_issued(&full[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown + kErrPairOffset);
+            // the MMAs' last completion signals (multicast commits into both CTAs' shared memory)
+            // land before the CTA exits: an arrival still in flight would hit the
+            // shared memory of whichever CTA runs on this SM next
+            if (ok)
+                for (uint32_t j = (it > XS ? it - XS : 0); j < it; ++j)
+                    mbar_wait(&empty[j % XS], (j / XS) & 1, p.status, kErrTimeoutTeardown + kErrPairOffset);
         }
     } else if (warp == 2) {
         // ------------------------------ producer: this CTA's packed weight tiles
@@ -1089,7 +1108,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 const int c0 = m * (2 * BM) + int(rank) * BM;  // this CTA's first output column
                 for (int ks = 0; ks < nkw; ++ks, ++wt) {
                     const int s = wt % WS;
-                    if (!mbar_wait(&wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+                    if (!mbar_wait(&wempty[s], ((wt / WS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrPairOffset)) {
                         ok = false;
                         break;
                     }
@@ -1105,7 +1124,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 }
             }
             for (uint32_t j = (wt > WS ? wt - WS : 0); j < wt; ++j)
-                mbar_wait_issued(&wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&wfull[j % WS], (j / WS) & 1, p.status, kErrTimeoutTeardown + kErrPairOffset);
         }
     } else if (warp == 1) {
         // ------------------------------------ MMA issuer (first CTA of the pair)
@@ -1118,14 +1137,14 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 int64_t t0;
                 tile_of(tl, m, t0, ntok);
                 const bool two = ntok > NH;
-                if (!mbar_wait(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) {
+                if (!mbar_wait(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma + kErrPairOffset)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % XS;
-                    if (!mbar_wait(&full[s], (it / XS) & 1, p.status, kErrTimeoutMma)) {
+                    if (!mbar_wait(&full[s], (it / XS) & 1, p.status, kErrTimeoutMma + kErrPairOffset)) {
                         ok = false;
                         break;
                     }
@@ -1218,7 +1237,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
             if (ks < nkw) {
                 const uint32_t wt = uint32_t(tl) * uint32_t(nkw) + uint32_t(ks);
                 const int s = wt % WS;
-                if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant)))
+                if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / WS) & 1, p.status, kErrTimeoutDequant + kErrPairOffset)))
                     break;
                 uint4 p0, p1;
                 if constexpr (DX) {
@@ -1267,7 +1286,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
                 }
             }
             const int sa = it % XS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / XS) & 1) ^ 1, p.status, kErrTimeoutDequant + kErrPairOffset)))
                 break;
             uint8_t *dst = a0 + sa * A_BYTES + arow;
 #pragma unroll
@@ -1293,7 +1312,7 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
             if (lane == 0) mbar_arrive_remote(accempty_c);
         };
         for (int tl = 0; tl < my_tiles; ++tl) {
-            if (!__all_sync(0xffffffffu, mbar_wait(accfull, tl & 1, p.status, kErrTimeoutEpilogue))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(accfull, tl & 1, p.status, kErrTimeoutEpilogue + kErrPairOffset))) break;
             tc_fence_after();
             int m, ntok;
             int64_t t0;
@@ -1407,14 +1426,22 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1 && lane == 0)  // the pair's MMAs into this CTA's TMEM are complete
-        mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown);
+    if (warp == 1 && lane == 0) {  // the pair's MMAs into this CTA's TMEM are complete
+        mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown + kErrPairOffset);
+        // the second CTA's epilogue releases of the last accumulator (remote arrivals
+        // on this CTA's barrier) have landed before this CTA's shared memory is reused
+        if (first && my_tiles > 0)
+            mbar_wait(accempty, (my_tiles & 1) ^ 1, p.status, kErrTimeoutTeardown + kErrPairOffset);
+    }
     __syncwarp();
     cluster_sync();  // neither CTA leaves while the peer may still signal its barriers
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc_pair(tmem, 512);
     }
+    // the pair's TMEM is released on both SMs before either CTA exits and its SM
+    // takes the next CTA (the 2-SM deallocation spans both)
+    cluster_sync();
 }
 
 }  // namespace pair
@@ -1734,9 +1761,21 @@ int stratum_device_status(int *out, int reset, void *stream) {
         cudaStreamSynchronize(st) != cudaSuccess)
         return fail(STRATUM_ERR_CUDA, "device_status: copy failed: %s", cudaGetErrorString(cudaGetLastError()));
     if (reset && *out != 0) {
-        if (cudaMemsetAsync(dp, 0, sizeof(int), st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+        if (cudaMemsetAsync(dp, 0, 8 * sizeof(int), st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
             return fail(STRATUM_ERR_CUDA, "device_status: reset failed");
     }
+    return STRATUM_OK;
+}
+
+int stratum_device_status_detail(int *out8, void *stream) {
+    STRATUM_REQUIRE(out8 != nullptr, "device_status_detail: null out");
+    STRATUM_BIND_STREAM(stream);
+    int *dp = gemm::status_ptr();
+    if (!dp) return fail(STRATUM_ERR_CUDA, "device_status_detail: cannot resolve the status word");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(out8, dp, 8 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(STRATUM_ERR_CUDA, "device_status_detail: copy failed: %s", cudaGetErrorString(cudaGetLastError()));
     return STRATUM_OK;
 }
 

@@ -219,8 +219,40 @@ struct FwdParams {
     int64_t Ttot;
     int N_e;               // weight rows per expert (2I for gate_up)
     int K;                 // contraction (H)
+    int E, m_tiles, cap;   // bounds a tile record must respect (checked before any tile runs)
     int *status;
 };
+
+// Warp 3 (idle otherwise) checks this CTA's tile records before any role uses
+// them: a record outside the bounds (a table overwritten after it was built, or
+// built from bad offsets) would make an MMA that never completes.  On a bad
+// record the status word gets kErrTileTable with the record beside it (block,
+// tile index, e, m, t0, t_end) and the CTA runs no tile.  Returns through *bad
+// (shared memory) after the caller's __syncthreads.
+__device__ __forceinline__ void check_tiles(const Tile *tiles, int first, int stride, int n, int E, int m_tiles,
+                                            int cap, int64_t Ttot, int *status, int *bad) {
+    const int lane = threadIdx.x & 31;
+    bool ok = true;
+    for (int i = lane; i < n; i += 32) {
+        const Tile t = tiles[first + i * stride];
+        if (t.e < 0 || t.e >= E || t.m < 0 || t.m >= m_tiles || t.t0 < 0 || t.t_end <= t.t0 ||
+            int64_t(t.t_end) > Ttot || t.t_end - t.t0 > cap) {
+            ok = false;
+            if (atomicCAS(status, 0, kErrTileTable) == 0) {
+                volatile int *d = status;
+                d[1] = first;
+                d[2] = i;
+                d[3] = t.e;
+                d[4] = t.m;
+                d[5] = t.t0;
+                d[6] = t.t_end;
+                __threadfence();
+            }
+        }
+    }
+    const bool all_ok = __all_sync(0xffffffffu, ok);
+    if (lane == 0) *bad = all_ok ? 0 : 1;
+}
 
 template <bool BF16, bool DQ, bool SWIGLU>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -243,8 +275,11 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = p.K / BK;
     const int ntiles = *p.ntiles;
-    const int my_tiles = ntiles > int(blockIdx.x) ? (ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
+    const int my_tiles0 = ntiles > int(blockIdx.x) ? (ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
     const int half_rows = p.N_e / 2;  // SWIGLU: I
+    int *bad = reinterpret_cast<int *>(tmem_slot + 1);
+    if (warp == 3) check_tiles(p.tiles, int(blockIdx.x), int(gridDim.x), my_tiles0, p.E, p.m_tiles, p.cap, p.Ttot,
+                               p.status, bad);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < F_XS; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
@@ -261,6 +296,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const int my_tiles = *bad ? 0 : my_tiles0;  // a bad tile record: run no tile (the status word says why)
     TileCursor cursor(p.tiles, int(blockIdx.x), int(gridDim.x), my_tiles);
     auto tile_at = [&](int tl) { return cursor.at(tl); };
     // first global weight row of the tile's rows r < 64 (and, in SWIGLU mode, r >= 64)
@@ -277,7 +313,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 const int nbox = (tile_mma_n(t) + F_XBOX - 1) / F_XBOX;  // 64-token boxes the MMAs read
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % F_XS;
-                    if (!mbar_wait(&empty[s], ((it / F_XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    if (!mbar_wait(&empty[s], ((it / F_XS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrGroupedFwdOffset)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full[s], uint32_t(nbox * F_XBOX_BYTES));
                     for (int bx = 0; bx < nbox; ++bx)
                         tma_load_2d(x0 + s * F_X_BYTES + bx * F_XBOX_BYTES, &tm_x, ks * BK, t.t0 + bx * F_XBOX,
@@ -285,7 +321,13 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 }
             }
             for (uint32_t j = (it > F_XS ? it - F_XS : 0); j < it; ++j)
-                mbar_wait_issued(&full[j % F_XS], (j / F_XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&full[j % F_XS], (j / F_XS) & 1, p.status, kErrTimeoutTeardown + kErrGroupedFwdOffset);
+            // the MMAs' last completion signals (commits into this CTA's shared memory)
+            // land before the CTA exits: an arrival still in flight would hit the
+            // shared memory of whichever CTA runs on this SM next
+            if (ok)
+                for (uint32_t j = (it > F_XS ? it - F_XS : 0); j < it; ++j)
+                    mbar_wait(&empty[j % F_XS], (j / F_XS) & 1, p.status, kErrTimeoutTeardown + kErrGroupedFwdOffset);
         }
     } else if (warp == 2) {
         if (lane == 0) {
@@ -296,7 +338,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 const Tile t = tile_at(tl);
                 for (int ks = 0; ks < nk; ++ks, ++wt) {
                     const int s = wt % F_WS;
-                    if (!mbar_wait(&wempty[s], ((wt / F_WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    if (!mbar_wait(&wempty[s], ((wt / F_WS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrGroupedFwdOffset)) { ok = false; break; }
                     mbar_arrive_expect_tx(&wfull[s], F_W_BYTES);
                     // two 64-row boxes: rows [0, 64) and [64, 128) of the stage
                     tma_load_2d(w0 + s * F_W_BYTES, &tm_w, ks * (BK / 2), row_lo(t), &wfull[s]);
@@ -304,7 +346,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 }
             }
             for (uint32_t j = (wt > F_WS ? wt - F_WS : 0); j < wt; ++j)
-                mbar_wait_issued(&wfull[j % F_WS], (j / F_WS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&wfull[j % F_WS], (j / F_WS) & 1, p.status, kErrTimeoutTeardown + kErrGroupedFwdOffset);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -316,11 +358,11 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 const int n0 = ntot < BN ? ntot : BN, n1 = ntot - n0;
                 const uint32_t idesc0 = idesc_f16(BF16, BM, n0);
                 const uint32_t idesc1 = n1 ? idesc_f16(BF16, BM, n1) : 0u;
-                if (!mbar_wait(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                if (!mbar_wait(accempty, (tl & 1) ^ 1, p.status, kErrTimeoutMma + kErrGroupedFwdOffset)) { ok = false; break; }
                 tc_fence_after();
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % F_XS, sa = s;
-                    if (!mbar_wait(&full[s], (it / F_XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                    if (!mbar_wait(&full[s], (it / F_XS) & 1, p.status, kErrTimeoutMma + kErrGroupedFwdOffset)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t bdesc0 = smem_desc_k_sw128(x0 + s * F_X_BYTES);
                     const uint64_t bdesc1 = smem_desc_k_sw128(x0 + s * F_X_BYTES + BN * BK * 2);
@@ -335,7 +377,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
                 if (ok) mma_commit(accfull);
             }
             mma_commit(drain);
-            mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown);
+            mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown + kErrGroupedFwdOffset);
         }
     } else if (warp >= 4 && warp < EPI_WARP0) {
         const int grp = (warp - 4) >> 2;
@@ -377,7 +419,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
             step();
             const uint32_t wt = it;  // one weight tile per step (no LoRA chunks here)
             const int s = wt % F_WS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / F_WS) & 1, p.status, kErrTimeoutDequant))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (wt / F_WS) & 1, p.status, kErrTimeoutDequant + kErrGroupedFwdOffset))) break;
             const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * F_W_BYTES + row * 32);
             const int sw = (row >> 2) & 1;  // 32-byte swizzle
             const uint4 p0 = src[sw], p1 = src[sw ^ 1];
@@ -388,7 +430,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
             fence_proxy_async_smem();  // generic reads before the stage's TMA refill
             mbar_arrive(&wempty[s]);
             const int sa = it % F_AS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / F_AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / F_AS) & 1) ^ 1, p.status, kErrTimeoutDequant + kErrGroupedFwdOffset)))
                 break;
             tc_fence_after();
             tmem_st_32x32b_x32(tmem + lane_addr + F_TMAX + sa * 32, vals);
@@ -402,7 +444,7 @@ k_grouped_fwd(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
         const int etid = threadIdx.x - EPI_WARP0 * 32;  // 0..127
         for (int tl = 0; tl < my_tiles; ++tl) {
-            if (!__all_sync(0xffffffffu, mbar_wait(accfull, tl & 1, p.status, kErrTimeoutEpilogue))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(accfull, tl & 1, p.status, kErrTimeoutEpilogue + kErrGroupedFwdOffset))) break;
             tc_fence_after();
             const Tile t = tile_at(tl);
             const int ncols = tile_cols(t);          // tokens of this expert in the tile
@@ -529,6 +571,8 @@ struct DxParams {
     uint16_t *dx;     // [Ttot, K]
     int N_e;          // contraction: weight rows per expert
     int K;            // weight columns (output width)
+    int64_t Ttot;
+    int E, m_tiles, cap;  // bounds a tile record must respect (checked before any tile runs)
     int *status;
 };
 
@@ -554,7 +598,10 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = p.N_e / BK;
     const int ntiles = *p.ntiles;
-    const int my_tiles = ntiles > int(blockIdx.x) ? (ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
+    const int my_tiles0 = ntiles > int(blockIdx.x) ? (ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
+    int *bad = reinterpret_cast<int *>(tmem_slot + 1);
+    if (warp == 3) check_tiles(p.tiles, int(blockIdx.x), int(gridDim.x), my_tiles0, p.E, p.m_tiles, p.cap, p.Ttot,
+                               p.status, bad);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < D_XS; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
@@ -570,6 +617,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const int my_tiles = *bad ? 0 : my_tiles0;  // a bad tile record: run no tile (the status word says why)
     TileCursor cursor(p.tiles, int(blockIdx.x), int(gridDim.x), my_tiles);
     auto tile_at = [&](int tl) { return cursor.at(tl); };
 
@@ -582,13 +630,19 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                 const Tile t = tile_at(tl);
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % D_XS;
-                    if (!mbar_wait(&empty[s], ((it / D_XS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    if (!mbar_wait(&empty[s], ((it / D_XS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrGroupedDxOffset)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full[s], X_BYTES);
                     tma_load_2d(x0 + s * X_BYTES, &tm_dy, ks * BK, t.t0, &full[s]);
                 }
             }
             for (uint32_t j = (it > D_XS ? it - D_XS : 0); j < it; ++j)
-                mbar_wait_issued(&full[j % D_XS], (j / D_XS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&full[j % D_XS], (j / D_XS) & 1, p.status, kErrTimeoutTeardown + kErrGroupedDxOffset);
+            // the MMAs' last completion signals (commits into this CTA's shared memory)
+            // land before the CTA exits: an arrival still in flight would hit the
+            // shared memory of whichever CTA runs on this SM next
+            if (ok)
+                for (uint32_t j = (it > D_XS ? it - D_XS : 0); j < it; ++j)
+                    mbar_wait(&empty[j % D_XS], (j / D_XS) & 1, p.status, kErrTimeoutTeardown + kErrGroupedDxOffset);
         }
     } else if (warp == 2) {
         if (lane == 0) {
@@ -599,13 +653,13 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                 const Tile t = tile_at(tl);
                 for (int ks = 0; ks < nk; ++ks, ++wt) {
                     const int s = wt % D_WS;
-                    if (!mbar_wait(&wempty[s], ((wt / D_WS) & 1) ^ 1, p.status, kErrTimeoutProducer)) { ok = false; break; }
+                    if (!mbar_wait(&wempty[s], ((wt / D_WS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrGroupedDxOffset)) { ok = false; break; }
                     mbar_arrive_expect_tx(&wfull[s], D_W_BYTES);
                     tma_load_2d(w0 + s * D_W_BYTES, &tm_w, t.m * (BM / 2), t.e * p.N_e + ks * BK, &wfull[s]);
                 }
             }
             for (uint32_t j = (wt > D_WS ? wt - D_WS : 0); j < wt; ++j)
-                mbar_wait_issued(&wfull[j % D_WS], (j / D_WS) & 1, p.status, kErrTimeoutTeardown);
+                mbar_wait_issued(&wfull[j % D_WS], (j / D_WS) & 1, p.status, kErrTimeoutTeardown + kErrGroupedDxOffset);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -614,12 +668,12 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
             for (int tl = 0; ok && tl < my_tiles; ++tl) {
                 const uint32_t idesc = idesc_f16_amn(BF16, BM, tile_mma_n(tile_at(tl)));
                 const int ab = tl & 1;
-                if (!mbar_wait(&accempty[ab], ((tl >> 1) & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                if (!mbar_wait(&accempty[ab], ((tl >> 1) & 1) ^ 1, p.status, kErrTimeoutMma + kErrGroupedDxOffset)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t acc = tmem + uint32_t(ab * 256);
                 for (int ks = 0; ks < nk; ++ks, ++it) {
                     const int s = it % D_XS, sa = s;
-                    if (!mbar_wait(&full[s], (it / D_XS) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+                    if (!mbar_wait(&full[s], (it / D_XS) & 1, p.status, kErrTimeoutMma + kErrGroupedDxOffset)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t bdesc = smem_desc_k_sw128(x0 + s * X_BYTES);
                     const uint64_t adesc = smem_desc_mn_sw128(a0 + sa * D_A_BYTES, D_A_ATOM, 1024);
@@ -631,7 +685,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                 if (ok) mma_commit(&accfull[ab]);
             }
             mma_commit(drain);
-            mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown);
+            mbar_wait_issued(drain, 0, p.status, kErrTimeoutTeardown + kErrGroupedDxOffset);
         }
     } else if (warp >= 4 && warp < EPI_WARP0) {
         const int grp = (warp - 4) >> 2;
@@ -672,7 +726,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
             nks += DQG;
             step();
             const int s = it % D_WS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (it / D_WS) & 1, p.status, kErrTimeoutDequant))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (it / D_WS) & 1, p.status, kErrTimeoutDequant + kErrGroupedDxOffset))) break;
             const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * D_W_BYTES + rl * 64);
             const int sw = (rl >> 1) & 3;  // 64-byte swizzle
             const uint4 p0 = src[(2 * kb) ^ sw], p1 = src[(2 * kb + 1) ^ sw];
@@ -683,7 +737,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
             fence_proxy_async_smem();
             mbar_arrive(&wempty[s]);
             const int sa = it % D_AS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / D_AS) & 1) ^ 1, p.status, kErrTimeoutDequant)))
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[sa], ((it / D_AS) & 1) ^ 1, p.status, kErrTimeoutDequant + kErrGroupedDxOffset)))
                 break;
             uint8_t *dst = a0 + sa * D_A_BYTES + kb * D_A_ATOM + (rl >> 3) * 1024 + (rl & 7) * 128;
 #pragma unroll
@@ -702,7 +756,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
         const int nrow = q * 32 + 8 * (kq & 1);
         for (int tl = 0; tl < my_tiles; ++tl) {
             const int ab = tl & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&accfull[ab], (tl >> 1) & 1, p.status, kErrTimeoutEpilogue))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(&accfull[ab], (tl >> 1) & 1, p.status, kErrTimeoutEpilogue + kErrGroupedDxOffset))) break;
             tc_fence_after();
             const Tile t = tile_at(tl);
             const int ncols = tile_cols(t);
@@ -893,6 +947,7 @@ int stratum_nf4_grouped_fwd(const void *x_sorted, int dtype, int64_t Ttot, int K
                            uint64_t(K / 2), 32, 64, CU_TENSOR_MAP_SWIZZLE_32B, "nf4_grouped_fwd packed");
     if (rc) return rc;
     grouped::FwdParams p{};
+    p.E = E; p.m_tiles = m_tiles; p.cap = grouped::F_TMAX;
     p.tiles = tiles; p.ntiles = ntiles; p.absmax = absmax; p.absmax_q = absmax_q; p.absmax2 = absmax2;
     p.code2 = code2; p.offset = offset; p.code16 = code16; p.rw = rw; p.y = static_cast<uint16_t *>(y);
     p.gu = static_cast<uint16_t *>(gate_up);
@@ -940,6 +995,7 @@ int stratum_nf4_grouped_dx(const void *dy_sorted, int dtype, int64_t Ttot, int N
                            uint64_t(K / 2), 64, 64, CU_TENSOR_MAP_SWIZZLE_64B, "nf4_grouped_dx packed");
     if (rc) return rc;
     grouped::DxParams p{};
+    p.Ttot = Ttot; p.E = E; p.m_tiles = m_tiles; p.cap = grouped::BN;
     p.tiles = tiles; p.ntiles = ntiles; p.absmax = absmax; p.absmax_q = absmax_q; p.absmax2 = absmax2;
     p.code2 = code2; p.offset = offset; p.code16 = code16; p.dx = static_cast<uint16_t *>(dx);
     p.N_e = N_e; p.K = K; p.status = status;

@@ -20,6 +20,12 @@ enum DeviceError : int {
     kErrTimeoutDequant = 0x103,
     kErrTimeoutEpilogue = 0x104,
     kErrTimeoutTeardown = 0x105,
+    // added to the five codes above, so the status word names the kernel family
+    kErrPairOffset = 0x10,     // CTA-pair GEMMs
+    kErrFwdOffset = 0x20,      // one-SM forward GEMM
+    kErrDxOffset = 0x30,       // one-SM input-gradient GEMM
+    kErrGroupedFwdOffset = 0x40,  // grouped expert forward
+    kErrGroupedDxOffset = 0x50,   // grouped expert input gradient
     kErrBadOffsets = 0x201,  // grouped GEMM: expert offsets outside [0, total tokens]
     kErrTileTable = 0x202,   // grouped GEMM: tile table smaller than the offsets need
 };
@@ -83,6 +89,24 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
     return ok != 0;
 }
 
+// Record a wait that gave up: the first such thread of the grid writes `code` to
+// err[0] and, beside it, where it was -- block, thread, the parity it waited for,
+// the barrier's shared-memory offset and the barrier's 64-bit state -- so the
+// host can report which wait of which kernel gave up (err points to 8 ints).
+__device__ __forceinline__ void record_timeout(int *err, int code, uint64_t *bar, uint32_t parity) {
+    if (atomicCAS(err, 0, code) != 0) return;
+    uint64_t state;
+    asm volatile("ld.shared.b64 %0, [%1];" : "=l"(state) : "r"(smem_u32(bar)));
+    volatile int *d = err;
+    d[1] = int(blockIdx.x);
+    d[2] = int(threadIdx.x);
+    d[3] = int(parity);
+    d[4] = int(smem_u32(bar));
+    d[5] = int(uint32_t(state));
+    d[6] = int(uint32_t(state >> 32));
+    __threadfence();
+}
+
 // Bounded wait for the phase with the given parity.  Returns false (after
 // recording `code` in *err) on timeout, or when another thread of the grid
 // already recorded an error, so every role unwinds instead of spinning.
@@ -93,7 +117,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
         if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
         if (*reinterpret_cast<volatile int *>(err) != 0) return false;
         if (globaltimer() - t0 > kWaitTimeoutNs) {
-            atomicCAS(err, 0, code);
+            record_timeout(err, code, bar, parity);
             return false;
         }
     }
@@ -108,7 +132,7 @@ __device__ __forceinline__ bool mbar_wait_issued(uint64_t *bar, uint32_t parity,
     while (true) {
         if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
         if (globaltimer() - t0 > kWaitTimeoutNs) {
-            atomicCAS(err, 0, code);
+            record_timeout(err, code, bar, parity);
             return false;
         }
     }
@@ -351,7 +375,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
         if (mbar_try_wait_cluster(bar, parity, kSuspendHintNs)) return true;
         if (*reinterpret_cast<volatile int *>(err) != 0) return false;
         if (globaltimer() - t0 > kWaitTimeoutNs) {
-            atomicCAS(err, 0, code);
+            record_timeout(err, code, bar, parity);
             return false;
         }
     }
@@ -364,7 +388,7 @@ __device__ __forceinline__ bool mbar_wait_cluster_issued(uint64_t *bar, uint32_t
     while (true) {
         if (mbar_try_wait_cluster(bar, parity, kSuspendHintNs)) return true;
         if (globaltimer() - t0 > kWaitTimeoutNs) {
-            atomicCAS(err, 0, code);
+            record_timeout(err, code, bar, parity);
             return false;
         }
     }

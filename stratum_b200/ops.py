@@ -8,6 +8,7 @@ accumulator.  Shapes follow F.linear: x [..., K], weight [N, K], y [..., N].
 
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -47,13 +48,30 @@ def lora_down(x2: torch.Tensor, lora_A: torch.Tensor, scaling: float) -> torch.T
 _GEMM_KERNELS = {"auto": 0, "pair": 1, "single": 2}
 
 
+_gemm_kernel_chosen = False  # set_gemm_kernel was called by the user
+
+
 def set_gemm_kernel(which: str) -> None:
     """Kernel for every later NF4 forward and input-gradient GEMM in this process:
     ``"auto"`` (by estimated makespan), ``"pair"`` (512-token x 256-column tiles on
     CTA pairs sharing 2-SM MMAs) or ``"single"`` (the one-SM kernels)."""
+    global _gemm_kernel_chosen
     if which not in _GEMM_KERNELS:
         raise ValueError(f"set_gemm_kernel: expected one of {sorted(_GEMM_KERNELS)}, got {which!r}")
     _lib.check(_lib.lib().stratum_nf4_gemm_set_kernel(_GEMM_KERNELS[which]), "set_gemm_kernel")
+    _gemm_kernel_chosen = True
+
+
+def multirank_gemm_default() -> None:
+    """One-SM GEMM kernels for a process that runs beside NCCL traffic (one rank of a
+    multi-rank pipeline), unless the kernel was chosen explicitly (``set_gemm_kernel``
+    or ``STRATUM_NF4_GEMM``).  In 2-GPU pipeline runs of the MoE config with the
+    CTA-pair kernels, the grouped expert input-gradient kernel's first tile in a
+    late-starting CTA sometimes never completed (its bounded wait gave up; cause not
+    yet found); the one-SM kernels ran those configurations clean."""
+    if _gemm_kernel_chosen or os.environ.get("STRATUM_NF4_GEMM"):
+        return
+    _lib.check(_lib.lib().stratum_nf4_gemm_set_kernel(_GEMM_KERNELS["single"]), "multirank_gemm_default")
 
 
 def nf4_gemm_fwd(

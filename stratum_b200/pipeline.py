@@ -605,6 +605,10 @@ class RankPipeline(nn.Module):
         self.schedule, self.recompute = schedule, recompute
         self.stage, self.prefix, self.postfix = stage, prefix, postfix
         self.rank, self.world, self.group = rank, world, group
+        if world > 1 and torch.cuda.is_available():
+            from . import ops
+
+            ops.multirank_gemm_default()  # one-SM GEMM kernels beside NCCL traffic
         self.device = _dev(stage.device_id)
         self.hidden_size, self.hidden_dtype = hidden_size, hidden_dtype
         self.offload = offload_stage_inputs
