@@ -159,6 +159,26 @@ int stratum_device_status(int *out, int reset, void *stream);
  * counterpart in the reference. */
 int stratum_device_status_detail(int *out8, void *stream);
 
+/* The whole diagnostic record (up to 72 ints; words beyond it are returned as 0):
+ * the 8 of stratum_device_status_detail, then [7] the SM, [8..9] nanoseconds
+ * (low word first) and [10] SM clock cycles the wait lasted, and from [12] 27
+ * 64-bit shared-memory words around the barrier waited on (17 below, the
+ * barrier, 9 above): the CTA's other stage barriers and, in the grouped
+ * kernels, the progress words of each role.  No counterpart in the reference. */
+int stratum_device_status_record(int *out, int n, void *stream);
+
+/* Limit of every bounded device-side wait of the GEMM kernels on the stream's
+ * device, in nanoseconds: 0 restores the default (2 s), otherwise 1 ms .. 60 s.
+ * Synchronises `stream`.  No counterpart in the reference. */
+int stratum_set_wait_limit_ns(uint64_t ns, void *stream);
+
+/* Launches one warp that waits, through the GEMMs' bounded wait, on a barrier
+ * nothing completes: after the limit in force the wait gives up and writes
+ * status 0x1f0 with its record (read with stratum_device_status_record /
+ * stratum_device_status), and the kernel returns -- a check of the failure path
+ * that faults nothing.  No counterpart in the reference. */
+int stratum_wait_selftest(void *stream);
+
 /* GEMM kernel used by stratum_nf4_gemm_fwd and the input-gradient entry points
  * (stratum_nf4_gemm_dx, stratum_nf4_gemm_dx_pair): STRATUM_GEMM_AUTO picks by
  * estimated makespan; PAIR forces the CTA-pair kernels (512-token x 256-column

@@ -36,6 +36,9 @@ SIGNATURES: dict[str, tuple] = {
     "stratum_last_error": (ctypes.c_char_p, []),
     "stratum_launch_count": (ctypes.c_uint64, []),
     "stratum_device_status_detail": (_int, [_vp, _vp]),
+    "stratum_device_status_record": (_int, [_vp, _int, _vp]),
+    "stratum_set_wait_limit_ns": (_int, [ctypes.c_uint64, _vp]),
+    "stratum_wait_selftest": (_int, [_vp]),
     "stratum_nf4_gemm_set_kernel": (_int, [_int]),
     "stratum_set_device": (_int, [_int]),
     "stratum_nf4_quantize": (_int, [_vp, _int, _i64, _int, _vp, _vp, _vp, _vp]),
@@ -165,27 +168,70 @@ def device_status(device=None, reset: bool = True) -> int:
     return out.value
 
 
+STATUS_WORDS = 72  # ints in the status record (include/stratum_nf4.h)
+BAR_BELOW, BAR_ABOVE = 17, 9  # shared-memory words snapshotted around the barrier waited on
+
+
+def device_status_record(device=None) -> list:
+    """The GEMM kernels' whole diagnostic record on ``device`` (see
+    ``stratum_device_status_record``), without clearing it."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    rec = (ctypes.c_int * STATUS_WORDS)()
+    with torch.cuda.device(dev):
+        check(lib().stratum_device_status_record(ctypes.cast(rec, ctypes.c_void_p), STATUS_WORDS, stream_of(dev)),
+              "device_status_record")
+    return list(rec)
+
+
+def set_wait_limit_ns(ns: int, device=None) -> None:
+    """Limit of the GEMM kernels' bounded device-side waits on ``device`` (0 = the 2 s default)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        check(lib().stratum_set_wait_limit_ns(int(ns), stream_of(dev)), "set_wait_limit_ns")
+
+
+def wait_selftest(device=None) -> None:
+    """Enqueue one bounded wait that gives up (status 0x1f0 after the limit in force)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        check(lib().stratum_wait_selftest(stream_of(dev)), "wait_selftest")
+
+
+def _u64(lo: int, hi: int) -> int:
+    return (lo & 0xffffffff) | ((hi & 0xffffffff) << 32)
+
+
+def describe_status_record(d: list) -> str:
+    """Readable form of a record from :func:`device_status_record` (empty when it
+    holds no wait that gave up or rejected tile record)."""
+    st = d[0]
+    if st != 0 and (st & 0xf00) == 0x100:
+        text = (f"first wait to give up: block {d[1]}, thread {d[2]}, SM {d[7]}, parity {d[3]}, barrier at shared "
+                f"offset 0x{d[4] & 0xffffffff:x}, state 0x{_u64(d[5], d[6]):016x}; the wait lasted "
+                f"{_u64(d[8], d[9]) / 1e9:.3f} s by %globaltimer and {d[10] & 0xffffffff} SM cycles")
+        n = BAR_BELOW + 1 + BAR_ABOVE
+        if len(d) >= 12 + 2 * n:
+            snap = [_u64(d[12 + 2 * i], d[13 + 2 * i]) for i in range(n)]
+            text += (f"; shared-memory words from {BAR_BELOW} below it to {BAR_ABOVE} above: "
+                     + " ".join(f"{v:016x}" for v in snap))
+        return text
+    if st == 0x202 and d[6] != 0:
+        return f"bad tile record: block {d[1]}, tile {d[2]}: expert {d[3]}, column tile {d[4]}, tokens [{d[5]}, {d[6]})"
+    return ""
+
+
 def check_device_status(what: str, device=None) -> None:
     """Raise :class:`StratumError` if a GEMM kernel on ``device`` gave up a bounded wait
     (or rejected its tile table) since the last read.  The read clears the word, so
     after the error the caller may retry; the results of the failed step are invalid."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    detail = (ctypes.c_int * 8)()
-    with torch.cuda.device(dev):
-        check(lib().stratum_device_status_detail(ctypes.cast(detail, ctypes.c_void_p), stream_of(dev)),
-              "device_status_detail")
+    rec = device_status_record(dev)
     st = device_status(dev)
     if st != 0:
-        d = list(detail)
-        where = ""
-        if d[0] == st and (st & 0xf00) == 0x100:
-            where = (f"; first wait to give up: block {d[1]}, thread {d[2]}, parity {d[3]}, barrier at shared "
-                     f"offset 0x{d[4] & 0xffffffff:x}, state 0x{d[6] & 0xffffffff:08x}{d[5] & 0xffffffff:08x}")
-        elif d[0] == st and st == 0x202 and d[6] != 0:
-            where = (f"; bad tile record: block {d[1]}, tile {d[2]}: expert {d[3]}, column tile {d[4]}, "
-                     f"tokens [{d[5]}, {d[6]})")
+        where = describe_status_record(rec) if rec[0] == st else ""
         raise StratumError(f"{what}: a device-side wait timed out or a tile table was rejected (status 0x{st:x})"
-                           f"{where}; the kernel unwound and its outputs are invalid (the status word is now cleared)")
+                           f"{'; ' + where if where else ''}; the kernel unwound and its outputs are invalid "
+                           f"(the status word is now cleared)")
 
 
 def launch_count() -> int:

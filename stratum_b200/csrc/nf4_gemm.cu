@@ -39,9 +39,11 @@
 
 namespace stratum {
 
-// Status word of the GEMM kernels (0 = ok), one per device.
-// [0] the code, [1..6] where the first wait that gave up was (see record_timeout).
-__device__ int g_gemm_status[8];
+// Status word of the GEMM kernels (0 = ok), one per device: [0] the code, then
+// the record of the first wait that gave up (sm100::record_timeout) or of a
+// rejected tile record (grouped::check_tiles); after the record, the wait limit
+// (sm100::kLimitWord).
+__device__ int g_gemm_status[sm100::kStatusAlloc];
 
 namespace gemm {
 
@@ -1447,6 +1449,25 @@ k_nf4_gemm_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant_
 }  // namespace pair
 
 
+// ------------------------------------------------------- wait self-test --
+
+// One warp: lane 0 waits on an mbarrier that nothing arrives on, through the same
+// bounded wait as the GEMMs, so the wait gives up after the limit in force and
+// writes kErrWaitSelfTest and its record to the status word; the kernel then
+// returns.  The barrier sits inside zeroed words, as the record's snapshot
+// expects shared memory on both sides of a waited barrier.
+__global__ void __launch_bounds__(32) k_wait_selftest(int *status) {
+    __shared__ __align__(8) uint64_t bars[sm100::kBarSnap];
+    if (threadIdx.x < sm100::kBarSnap) bars[threadIdx.x] = 0;
+    __syncwarp();
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&bars[sm100::kBarBelow], 1);
+        sm100::fence_barrier_init();
+        sm100::mbar_wait(&bars[sm100::kBarBelow], 0, status, sm100::kErrWaitSelfTest);
+    }
+    __syncwarp();
+}
+
 // ------------------------------------------------------------------- host --
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1761,7 +1782,8 @@ int stratum_device_status(int *out, int reset, void *stream) {
         cudaStreamSynchronize(st) != cudaSuccess)
         return fail(STRATUM_ERR_CUDA, "device_status: copy failed: %s", cudaGetErrorString(cudaGetLastError()));
     if (reset && *out != 0) {
-        if (cudaMemsetAsync(dp, 0, 8 * sizeof(int), st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+        if (cudaMemsetAsync(dp, 0, sm100::kStatusWords * sizeof(int), st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
             return fail(STRATUM_ERR_CUDA, "device_status: reset failed");
     }
     return STRATUM_OK;
@@ -1777,6 +1799,43 @@ int stratum_device_status_detail(int *out8, void *stream) {
         cudaStreamSynchronize(st) != cudaSuccess)
         return fail(STRATUM_ERR_CUDA, "device_status_detail: copy failed: %s", cudaGetErrorString(cudaGetLastError()));
     return STRATUM_OK;
+}
+
+int stratum_device_status_record(int *out, int n, void *stream) {
+    STRATUM_REQUIRE(out != nullptr && n > 0, "device_status_record: null out or n <= 0");
+    STRATUM_BIND_STREAM(stream);
+    int *dp = gemm::status_ptr();
+    if (!dp) return fail(STRATUM_ERR_CUDA, "device_status_record: cannot resolve the status word");
+    const int m = n < sm100::kStatusWords ? n : sm100::kStatusWords;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(out, dp, size_t(m) * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(STRATUM_ERR_CUDA, "device_status_record: copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+    for (int i = m; i < n; ++i) out[i] = 0;
+    return STRATUM_OK;
+}
+
+int stratum_set_wait_limit_ns(uint64_t ns, void *stream) {
+    STRATUM_REQUIRE(ns == 0 || (ns >= 1000000ull && ns <= 60000000000ull),
+                    "set_wait_limit_ns: %llu ns outside [1 ms, 60 s] (0 restores the default)",
+                    (unsigned long long)ns);
+    STRATUM_BIND_STREAM(stream);
+    int *dp = gemm::status_ptr();
+    if (!dp) return fail(STRATUM_ERR_CUDA, "set_wait_limit_ns: cannot resolve the status word");
+    const uint32_t words[2] = {uint32_t(ns), uint32_t(ns >> 32)};
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(dp + sm100::kLimitWord, words, sizeof(words), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(STRATUM_ERR_CUDA, "set_wait_limit_ns: copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return STRATUM_OK;
+}
+
+int stratum_wait_selftest(void *stream) {
+    STRATUM_BIND_STREAM(stream);
+    int *dp = gemm::status_ptr();
+    if (!dp) return fail(STRATUM_ERR_CUDA, "wait_selftest: cannot resolve the status word");
+    gemm::k_wait_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(dp);
+    return check_launch("wait_selftest");
 }
 
 int stratum_nf4_gemm_set_kernel(int which) {

@@ -592,6 +592,10 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
     uint64_t *accfull = wempty + D_WS, *accempty = accfull + 2;
     uint64_t *drain = accempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    // progress words beside the barriers (snapshotted by a timeout record): [0] dY steps
+    // issued, [1] W steps issued, [2] steps the MMA consumed, [3..5] each decode
+    // group's step + 1, [6] the epilogue's tile | its tile count << 16, [7] ntiles as read
+    volatile int *prog = reinterpret_cast<volatile int *>(tmem_slot + 2);
     float *lv_s = reinterpret_cast<float *>(bars + 64);
     float *c2 = lv_s + 16;
 
@@ -609,6 +613,8 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
         for (int i = 0; i < 2; ++i) { mbar_init(&accfull[i], 1); mbar_init(&accempty[i], 128); }
         mbar_init(drain, 1);
         fence_barrier_init();
+        for (int i = 0; i < 7; ++i) prog[i] = 0;
+        prog[7] = ntiles;
     }
     if (threadIdx.x < 16) lv_s[threadIdx.x] = p.code16[threadIdx.x];
     if (DQ) for (int i = threadIdx.x; i < 256; i += NUM_THREADS) c2[i] = p.code2[i];
@@ -633,6 +639,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                     if (!mbar_wait(&empty[s], ((it / D_XS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrGroupedDxOffset)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full[s], X_BYTES);
                     tma_load_2d(x0 + s * X_BYTES, &tm_dy, ks * BK, t.t0, &full[s]);
+                    prog[0] = int(it) + 1;
                 }
             }
             for (uint32_t j = (it > D_XS ? it - D_XS : 0); j < it; ++j)
@@ -656,6 +663,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                     if (!mbar_wait(&wempty[s], ((wt / D_WS) & 1) ^ 1, p.status, kErrTimeoutProducer + kErrGroupedDxOffset)) { ok = false; break; }
                     mbar_arrive_expect_tx(&wfull[s], D_W_BYTES);
                     tma_load_2d(w0 + s * D_W_BYTES, &tm_w, t.m * (BM / 2), t.e * p.N_e + ks * BK, &wfull[s]);
+                    prog[1] = int(wt) + 1;
                 }
             }
             for (uint32_t j = (wt > D_WS ? wt - D_WS : 0); j < wt; ++j)
@@ -681,6 +689,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
                     for (int j = 0; j < BK / 16; ++j)
                         mma_ss_f16(acc, adesc + uint64_t(j * (2048 >> 4)), bdesc + uint64_t(j * 2), idesc, (ks | j) != 0);
                     mma_commit(&empty[s]);
+                    prog[2] = int(it) + 1;
                 }
                 if (ok) mma_commit(&accfull[ab]);
             }
@@ -726,6 +735,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
             nks += DQG;
             step();
             const int s = it % D_WS;
+            if (tid == 0) prog[3 + grp] = int(it) + 1;
             if (!__all_sync(0xffffffffu, mbar_wait(&wfull[s], (it / D_WS) & 1, p.status, kErrTimeoutDequant + kErrGroupedDxOffset))) break;
             const uint4 *src = reinterpret_cast<const uint4 *>(w0 + s * D_W_BYTES + rl * 64);
             const int sw = (rl >> 1) & 3;  // 64-byte swizzle
@@ -756,6 +766,7 @@ k_grouped_dx(const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ 
         const int nrow = q * 32 + 8 * (kq & 1);
         for (int tl = 0; tl < my_tiles; ++tl) {
             const int ab = tl & 1;
+            if (etid == 0) prog[6] = tl | (my_tiles << 16);
             if (!__all_sync(0xffffffffu, mbar_wait(&accfull[ab], (tl >> 1) & 1, p.status, kErrTimeoutEpilogue + kErrGroupedDxOffset))) break;
             tc_fence_after();
             const Tile t = tile_at(tl);

@@ -28,10 +28,12 @@ enum DeviceError : int {
     kErrGroupedDxOffset = 0x50,   // grouped expert input gradient
     kErrBadOffsets = 0x201,  // grouped GEMM: expert offsets outside [0, total tokens]
     kErrTileTable = 0x202,   // grouped GEMM: tile table smaller than the offsets need
+    kErrWaitSelfTest = 0x1f0,  // stratum_wait_selftest: its wait on a barrier nothing completes gave up
 };
 
 // A wait that takes longer than this is a hang, never a slow pipeline stage
 // (one stage is microseconds); the kernel then records an error and unwinds.
+// The default; stratum_set_wait_limit_ns changes it per device.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 // Suspend-time hint for a blocked mbarrier wait (the thread wakes when the phase completes).
 constexpr uint32_t kSuspendHintNs = 1000000u;
@@ -89,21 +91,73 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
     return ok != 0;
 }
 
+// Words of the status record (err): [0] code, [1] block, [2] thread, [3] parity,
+// [4] the barrier's shared-memory offset, [5..6] its 64-bit state, [7] the SM,
+// [8..9] nanoseconds and [10] SM clock cycles the wait lasted (%globaltimer and
+// clock64 each, so a clock that jumped shows as the two disagreeing), and from
+// [12] kBarSnap 64-bit shared-memory words (two ints each, low first): the
+// kBarBelow words below the barrier waited on, that barrier, and kBarAbove words
+// above it -- the CTA's other stage barriers and the progress words some
+// kernels keep beside them, which say which role stopped.  Every kernel keeps at
+// least 16 KiB of tiles below its barrier area and at least 1 KiB of tables
+// above it, so the snapshot stays inside the CTA's shared memory.
+constexpr int kBarBelow = 17, kBarAbove = 9;
+constexpr int kBarSnap = kBarBelow + 1 + kBarAbove;
+constexpr int kStatusWords = 72;
+static_assert(12 + 2 * kBarSnap <= kStatusWords, "status record");
+// Two more words after the record hold the wait limit in nanoseconds (0 =
+// kWaitTimeoutNs), set by stratum_set_wait_limit_ns; clearing the record keeps them.
+constexpr int kLimitWord = kStatusWords;
+constexpr int kStatusAlloc = kStatusWords + 2;
+
+// The wait limit in force (read from memory on every slow-path check, so the
+// loop holds no extra register for it).
+__device__ __forceinline__ uint64_t wait_limit_ns(const int *err) {
+    const volatile uint32_t *w = reinterpret_cast<const volatile uint32_t *>(err + kLimitWord);
+    const uint64_t v = uint64_t(w[0]) | (uint64_t(w[1]) << 32);
+    return v ? v : kWaitTimeoutNs;
+}
+
+__device__ __forceinline__ uint32_t sm_id() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint64_t ld_shared_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(smem_u32(p)));
+    return v;
+}
+
 // Record a wait that gave up: the first such thread of the grid writes `code` to
-// err[0] and, beside it, where it was -- block, thread, the parity it waited for,
-// the barrier's shared-memory offset and the barrier's 64-bit state -- so the
-// host can report which wait of which kernel gave up (err points to 8 ints).
-__device__ __forceinline__ void record_timeout(int *err, int code, uint64_t *bar, uint32_t parity) {
+// err[0] and the rest of the record above (err points to kStatusWords ints);
+// t0 is %globaltimer and c0 the low word of clock64 when the wait began (a wait
+// gives up after ~2 s, fewer than 2^32 cycles at B200 clocks, so the 32-bit
+// difference is exact).
+__device__ __forceinline__ void record_timeout(int *err, int code, uint64_t *bar, uint32_t parity, uint64_t t0,
+                                               uint32_t c0) {
     if (atomicCAS(err, 0, code) != 0) return;
-    uint64_t state;
-    asm volatile("ld.shared.b64 %0, [%1];" : "=l"(state) : "r"(smem_u32(bar)));
+    const uint64_t t1 = globaltimer();
+    const uint32_t dc = uint32_t(clock64()) - c0;
     volatile int *d = err;
+    const uint64_t state = ld_shared_u64(bar);
     d[1] = int(blockIdx.x);
     d[2] = int(threadIdx.x);
     d[3] = int(parity);
     d[4] = int(smem_u32(bar));
     d[5] = int(uint32_t(state));
     d[6] = int(uint32_t(state >> 32));
+    d[7] = int(sm_id());
+    d[8] = int(uint32_t(t1 - t0));
+    d[9] = int(uint32_t((t1 - t0) >> 32));
+    d[10] = int(dc);
+    d[11] = 0;
+    for (int i = 0; i < kBarSnap; ++i) {
+        const uint64_t v = ld_shared_u64(bar - kBarBelow + i);
+        d[12 + 2 * i] = int(uint32_t(v));
+        d[13 + 2 * i] = int(uint32_t(v >> 32));
+    }
     __threadfence();
 }
 
@@ -113,11 +167,12 @@ __device__ __forceinline__ void record_timeout(int *err, int code, uint64_t *bar
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
+    const uint32_t c0 = uint32_t(clock64());
     while (true) {
         if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
         if (*reinterpret_cast<volatile int *>(err) != 0) return false;
-        if (globaltimer() - t0 > kWaitTimeoutNs) {
-            record_timeout(err, code, bar, parity);
+        if (globaltimer() - t0 > wait_limit_ns(err)) {
+            record_timeout(err, code, bar, parity, t0, c0);
             return false;
         }
     }
@@ -129,10 +184,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
 // frees shared memory or TMEM.
 __device__ __forceinline__ bool mbar_wait_issued(uint64_t *bar, uint32_t parity, int *err, int code) {
     const uint64_t t0 = globaltimer();
+    const uint32_t c0 = uint32_t(clock64());
     while (true) {
         if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
-        if (globaltimer() - t0 > kWaitTimeoutNs) {
-            record_timeout(err, code, bar, parity);
+        if (globaltimer() - t0 > wait_limit_ns(err)) {
+            record_timeout(err, code, bar, parity, t0, c0);
             return false;
         }
     }
@@ -371,11 +427,12 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t pa
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int *err, int code) {
     if (mbar_try_wait_cluster(bar, parity, 0u)) return true;
     const uint64_t t0 = globaltimer();
+    const uint32_t c0 = uint32_t(clock64());
     while (true) {
         if (mbar_try_wait_cluster(bar, parity, kSuspendHintNs)) return true;
         if (*reinterpret_cast<volatile int *>(err) != 0) return false;
-        if (globaltimer() - t0 > kWaitTimeoutNs) {
-            record_timeout(err, code, bar, parity);
+        if (globaltimer() - t0 > wait_limit_ns(err)) {
+            record_timeout(err, code, bar, parity, t0, c0);
             return false;
         }
     }
@@ -385,10 +442,11 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
 // up on another thread's error, only on the time limit (as mbar_wait_issued).
 __device__ __forceinline__ bool mbar_wait_cluster_issued(uint64_t *bar, uint32_t parity, int *err, int code) {
     const uint64_t t0 = globaltimer();
+    const uint32_t c0 = uint32_t(clock64());
     while (true) {
         if (mbar_try_wait_cluster(bar, parity, kSuspendHintNs)) return true;
-        if (globaltimer() - t0 > kWaitTimeoutNs) {
-            record_timeout(err, code, bar, parity);
+        if (globaltimer() - t0 > wait_limit_ns(err)) {
+            record_timeout(err, code, bar, parity, t0, c0);
             return false;
         }
     }

@@ -63,12 +63,12 @@ def set_gemm_kernel(which: str) -> None:
 
 
 def multirank_gemm_default() -> None:
-    """One-SM GEMM kernels for a process that runs beside NCCL traffic (one rank of a
-    multi-rank pipeline), unless the kernel was chosen explicitly (``set_gemm_kernel``
-    or ``STRATUM_NF4_GEMM``).  In 2-GPU pipeline runs of the MoE config with the
-    CTA-pair kernels, the grouped expert input-gradient kernel's first tile in a
-    late-starting CTA sometimes never completed (its bounded wait gave up; cause not
-    yet found); the one-SM kernels ran those configurations clean."""
+    """One-SM GEMM kernels for one rank of a multi-rank pipeline, unless the kernel
+    was chosen explicitly (``set_gemm_kernel`` or ``STRATUM_NF4_GEMM``).  In MoE
+    pipeline runs the grouped expert input-gradient kernel sometimes finds foreign
+    data in its barrier words and its bounded wait gives up. On two GPUs that
+    happened in 9 of 39 steps beside the CTA-pair kernels (one run also ended in a
+    launch failure) and in 1 of 14 beside the one-SM kernels."""
     if _gemm_kernel_chosen or os.environ.get("STRATUM_NF4_GEMM"):
         return
     _lib.check(_lib.lib().stratum_nf4_gemm_set_kernel(_GEMM_KERNELS["single"]), "multirank_gemm_default")
