@@ -919,8 +919,9 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
 
     timed_own_ms = []
     # a step whose kernels report that a bounded device-side wait gave up (the status word
-    # read at the end of train_step) has invalid results and a ~2 s stall in its time: the
-    # attempt is discarded and timed again (at most twice), and the line says how many were
+    # read at the end of train_step) is run again by train_step (or raises once its retries
+    # are spent) and carries a ~2 s stall in its time: the attempt is discarded and timed
+    # again (at most twice), and the line says how many were
     status_errors = {"discarded_attempts": 0, "errors_in_reported": 0, "warmup_errors": 0, "last": ""}
 
     def guarded(mb, host=False):
@@ -940,7 +941,7 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
             torch.cuda.synchronize()
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
-            n0, g0 = _lib.launch_count(), pipe.graph_launches
+            n0, g0, r0 = _lib.launch_count(), pipe.graph_launches, pipe.status_retries
             e0.record()
             bad = 0
             for _ in range(n):
@@ -948,6 +949,7 @@ def run_pipeline_metrics(args, world, rank, local, model=None, microbatches=None
             e1.record()
             torch.cuda.synchronize()
             launches = _lib.launch_count() - n0 + pipe.graph_launches - g0
+            bad += pipe.status_retries - r0  # steps train_step itself ran again
             barrier(world)
             bad = int(max_over_ranks(float(bad), world))
             if bad == 0 or attempt == 2:

@@ -589,12 +589,20 @@ class RankPipeline(nn.Module):
     in-place updates (as torch optimizers make) keep the graph.
     ``graph_launches`` counts the library kernels the replays ran (they bypass
     the host-side launch counter).
+
+    ``step_retries`` (default 1): a step whose kernels report that a bounded
+    device-side wait gave up (the status word read at the end of every step) has
+    invalid gradients; every rank learns of it through one all-reduce of a flag,
+    the trainable parameters' ``.grad`` are put back as they were before the step,
+    and the step runs again, at most ``step_retries`` times before
+    ``StratumError`` is raised.  ``status_retries`` counts the retried steps.
     """
 
     def __init__(self, stage: DeviceStage, *, prefix: nn.Module, postfix: Optional[nn.Module], rank: int,
                  world: int, group=None, hidden_size: int, offload_stage_inputs: bool = False, router_sink=None,
                  router_aux_coef: float = 0.0, n_experts: int = 0, hidden_dtype=torch.bfloat16,
-                 schedule: str = "gpipe", recompute: bool = True, cuda_graph: bool = False):
+                 schedule: str = "gpipe", recompute: bool = True, cuda_graph: bool = False,
+                 step_retries: int = 1):
         super().__init__()
         if (postfix is None) != (rank + 1 < world):
             raise ValueError("RankPipeline: the postfix lives on the last rank only")
@@ -629,6 +637,8 @@ class RankPipeline(nn.Module):
                 raise ValueError("RankPipeline: cuda_graph does not cover the router aux loss")
         self._graphs: dict = {}
         self.graph_launches = 0
+        self.step_retries = max(0, int(step_retries))
+        self.status_retries = 0
 
     def _aux_reduce(self, states: list[_AuxState]) -> None:
         E = self.n_experts
@@ -841,6 +851,23 @@ class RankPipeline(nn.Module):
         _check_status([self.device], "RankPipeline.train_step")
         return loss_acc / M
 
+    def _grads_before(self) -> list:
+        return [(p, None if p.grad is None else p.grad.detach().clone()) for p in self.parameters()
+                if p.requires_grad]
+
+    @staticmethod
+    def _grads_restore(saved: list) -> None:
+        for p, g in saved:
+            p.grad = None if g is None else g.clone()  # a copy: the next attempt accumulates into it
+
+    def _failed_anywhere(self, failed: bool) -> bool:
+        """Whether this rank or any other saw its step fail (one all-reduce when world > 1)."""
+        if self.world == 1 or not dist.is_initialized():
+            return failed
+        flag = torch.tensor([1.0 if failed else 0.0], dtype=torch.float32, device=self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
+        return bool(flag.item() > 0)
+
     def train_step(self, input_ids: Optional[torch.Tensor] = None, labels: Optional[torch.Tensor] = None, *,
                    microbatches: int = 1, seq_len: Optional[int] = None):
         M = int(microbatches)
@@ -850,6 +877,26 @@ class RankPipeline(nn.Module):
                 ids = input_ids.reshape(M, 1, -1).to(dev, non_blocking=True)
                 labs = labels.reshape(M, 1, -1).to(dev, non_blocking=True)
                 return self._graph_train(ids, labs, M)
+        if self.step_retries == 0:
+            return self._train_step_once(input_ids, labels, M, seq_len)
+        from ._lib import StratumError
+
+        saved = self._grads_before()
+        for attempt in range(self.step_retries + 1):
+            err, out = None, None
+            try:
+                out = self._train_step_once(input_ids, labels, M, seq_len)
+            except StratumError as exc:
+                err = exc
+            if not self._failed_anywhere(err is not None):
+                return out
+            if attempt == self.step_retries:
+                raise err if err is not None else StratumError(
+                    "RankPipeline.train_step: a device-side wait gave up on another rank in every attempt")
+            self.status_retries += 1
+            self._grads_restore(saved)
+
+    def _train_step_once(self, input_ids, labels, M: int, seq_len: Optional[int]):
         first, last = self.rank == 0, self.rank + 1 == self.world
         dev = self.device
         if first:

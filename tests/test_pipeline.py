@@ -311,3 +311,81 @@ def test_p2p_channel_send_only_groups_do_not_block_and_flush_retires_them():
     assert r0["after_flush"] == 0 and r1["after_flush"] == 0
     assert [float(t[0]) for t in r1["got"]] == [0.0, 1.0, 2.0]
     assert torch.equal(r0["got"][0], torch.full((5,), 7.0))
+
+
+def _retry_main(rank, world, port, out_dir, fail_rank, fail_times, retries):
+    """RankPipeline.train_step with the status check of ``fail_rank`` raising, on the host,
+    for its first ``fail_times`` calls (no GPU: the failure is injected, nothing faults)."""
+    import torch.distributed as dist
+
+    from stratum_b200 import _lib
+    from stratum_b200 import pipeline as P
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from stratum_b200.assign import assign_layers_to_devices, strata
+
+        calls = {"n": 0}
+
+        def fake_check(devices, what):
+            calls["n"] += 1
+            if rank == fail_rank and calls["n"] <= fail_times:
+                raise _lib.StratumError(f"{what}: injected device-side wait timeout")
+
+        P._check_status = fake_check
+        M, n_layers = 3, 4
+        layers = _model(n_layers, False)
+        parts = strata(assign_layers_to_devices(n_layers, n_devices=world))
+        mine = parts[rank][1]
+        stage = DeviceStage([layers[i] for i in mine], "cpu")
+        pipe = RankPipeline(stage, prefix=ToyPrefix(), postfix=ToyPostfix() if rank == world - 1 else None,
+                            rank=rank, world=world, hidden_size=H, hidden_dtype=torch.float32,
+                            schedule="1f1b", recompute=False, step_retries=retries)
+        ids, labels = _data(M)
+        # gradients already present before the step must survive a retried step unchanged
+        for i in mine:
+            for p in layers[i].parameters():
+                if p.requires_grad:
+                    p.grad = torch.full_like(p, 0.5)
+        result = {}
+        try:
+            loss = pipe.train_step(ids if rank == 0 else None, labels if rank == world - 1 else None,
+                                   microbatches=M, seq_len=S)
+            result["loss"] = None if loss is None else float(loss)
+        except _lib.StratumError as exc:
+            result["error"] = str(exc)
+        result["retries"] = pipe.status_retries
+        result["grads"] = {f"{i}.{n}": p.grad for i in mine for n, p in layers[i].named_parameters()
+                           if p.requires_grad}
+        torch.save(result, os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_retry(fail_rank, fail_times, retries):
+    world = 2
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_retry_main, args=(world, _free_port(), d, fail_rank, fail_times, retries),
+                           nprocs=world, start_method="spawn", join=True)
+        return [torch.load(os.path.join(d, f"rank{r}.pt")) for r in range(world)]
+
+
+def test_rank_pipeline_retries_a_step_whose_kernels_gave_up():
+    """A status error on one rank makes every rank run the step again, from the gradients
+    held before it: the result equals a clean step's."""
+    clean = _run_retry(fail_rank=-1, fail_times=0, retries=1)
+    retried = _run_retry(fail_rank=1, fail_times=1, retries=1)
+    assert [o["retries"] for o in clean] == [0, 0]
+    assert [o["retries"] for o in retried] == [1, 1]
+    assert retried[-1]["loss"] == pytest.approx(clean[-1]["loss"], rel=1e-6)
+    for a, b in zip(clean, retried):
+        for k in a["grads"]:
+            torch.testing.assert_close(b["grads"][k], a["grads"][k], rtol=0, atol=0, msg=k)
+
+
+def test_rank_pipeline_raises_once_retries_are_spent():
+    outs = _run_retry(fail_rank=0, fail_times=5, retries=1)
+    assert "injected" in outs[0]["error"]
+    assert "another rank" in outs[1]["error"]
+    assert [o["retries"] for o in outs] == [1, 1]
