@@ -590,7 +590,7 @@ class RankPipeline(nn.Module):
     ``graph_launches`` counts the library kernels the replays ran (they bypass
     the host-side launch counter).
 
-    ``step_retries`` (default 1): a step whose kernels report that a bounded
+    ``step_retries`` (default 2): a step whose kernels report that a bounded
     device-side wait gave up (the status word read at the end of every step) has
     invalid gradients; every rank learns of it through one all-reduce of a flag,
     the trainable parameters' ``.grad`` are put back as they were before the step,
@@ -602,7 +602,7 @@ class RankPipeline(nn.Module):
                  world: int, group=None, hidden_size: int, offload_stage_inputs: bool = False, router_sink=None,
                  router_aux_coef: float = 0.0, n_experts: int = 0, hidden_dtype=torch.bfloat16,
                  schedule: str = "gpipe", recompute: bool = True, cuda_graph: bool = False,
-                 step_retries: int = 1):
+                 step_retries: int = 2):
         super().__init__()
         if (postfix is None) != (rank + 1 < world):
             raise ValueError("RankPipeline: the postfix lives on the last rank only")
