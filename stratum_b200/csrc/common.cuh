@@ -109,6 +109,38 @@ __device__ __forceinline__ float load_as_f32(const float *p, int64_t i) { return
 __device__ __forceinline__ float load_as_f32(const __half *p, int64_t i) { return __half2float(p[i]); }
 __device__ __forceinline__ float load_as_f32(const __nv_bfloat16 *p, int64_t i) { return __bfloat162float(p[i]); }
 
+// Global accesses that allocate no L1 line, for the small kernels that run right
+// before the grouped NF4 GEMMs.  Those GEMMs' CTAs take the whole of the SM's
+// shared memory (the SRAM that L1 shares), and 128-byte lines the preceding kernel
+// had touched (bf16 rows of dy_sorted, routing weights) were found in a grouped
+// GEMM's barrier words.  The loads are for data no thread of the kernel writes
+// (the non-coherent path), so they carry no ordering and the compiler may move them.
+__device__ __forceinline__ uint4 ld_na(const uint4 *p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ int ld_na(const int *p) {
+    int v;
+    asm("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float ld_na(const float *p) {
+    float v;
+    asm("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st_na(uint4 *p, uint4 v) {
+    asm volatile("st.global.L1::no_allocate.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void st_na(float *p, float v) {
+    asm volatile("st.global.L1::no_allocate.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
 // Index of the level for a scaled value: number of thresholds strictly below x.
 // thr[0..14] sorted, thr[15] = +inf padding; NaN fails every test -> 0.
 __device__ __forceinline__ uint32_t nf4_code(float x, const float *thr, float t7) {

@@ -112,9 +112,9 @@ __global__ void k_gather_rows(const uint4 *__restrict__ src, const int *__restri
     const int lane = threadIdx.x & 31;
     const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
     for (int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-        const uint4 *s = src + int64_t(idx[r]) * vec_per_row;
+        const uint4 *s = src + int64_t(ld_na(idx + r)) * vec_per_row;
         uint4 *d = dst + r * vec_per_row;
-        for (int c = lane; c < vec_per_row; c += 32) d[c] = s[c];
+        for (int c = lane; c < vec_per_row; c += 32) st_na(d + c, ld_na(s + c));
     }
 }
 
@@ -157,22 +157,22 @@ __global__ void k_combine(const uint4 *__restrict__ rows, const int *__restrict_
                           const int *__restrict__ offsets, int E, int64_t T, int k, int vec_per_row,
                           uint4 *__restrict__ out) {
     const int lane = threadIdx.x & 31;
-    const int routed = offsets[E];
+    const int routed = ld_na(offsets + E);
     const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
     for (int64_t t = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
         for (int c = lane; c < vec_per_row; c += 32) {
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             for (int s = 0; s < k; ++s) {
                 const int64_t j = t * k + s;
-                const int p = inv[j];
+                const int p = ld_na(inv + j);
                 if (p >= routed) continue;
-                const float ws = w ? w[j] : 1.f;
+                const float ws = w ? ld_na(w + j) : 1.f;
                 float f[8];
-                unpack8<BF16>(rows[int64_t(p) * vec_per_row + c], f);
+                unpack8<BF16>(ld_na(rows + int64_t(p) * vec_per_row + c), f);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(ws, f[i]));
             }
-            out[t * vec_per_row + c] = pack8<BF16>(acc);
+            st_na(out + t * vec_per_row + c, pack8<BF16>(acc));
         }
     }
 }
@@ -188,30 +188,30 @@ __global__ void k_combine_grad(const uint4 *__restrict__ dout, const int *__rest
                                int64_t n_rows, int vec_per_row, uint4 *__restrict__ dy_sorted,
                                float *__restrict__ dw) {
     const int lane = threadIdx.x & 31;
-    const int routed = offsets[E];
+    const int routed = ld_na(offsets + E);
     const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
     for (int64_t p = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); p < n_rows; p += warps) {
-        const int j = order[p];
-        const int64_t t = token_of[p];
+        const int j = ld_na(order + p);
+        const int64_t t = ld_na(token_of + p);
         const bool live = p < routed;
-        const float ws = live ? (w ? w[j] : 1.f) : 0.f;
+        const float ws = live ? (w ? ld_na(w + j) : 1.f) : 0.f;
         float dot = 0.f;
         for (int c = lane; c < vec_per_row; c += 32) {
             float g[8], r[8], o[8];
-            unpack8<BF16>(dout[t * vec_per_row + c], g);
+            unpack8<BF16>(ld_na(dout + t * vec_per_row + c), g);
             if (rows && live) {
-                unpack8<BF16>(rows[p * vec_per_row + c], r);
+                unpack8<BF16>(ld_na(rows + p * vec_per_row + c), r);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) dot = fmaf(g[i], r[i], dot);
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) o[i] = ws * g[i];
-            dy_sorted[p * vec_per_row + c] = pack8<BF16>(o);
+            st_na(dy_sorted + p * vec_per_row + c, pack8<BF16>(o));
         }
         if (dw) {
 #pragma unroll
             for (int d = 16; d > 0; d >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, d);
-            if (lane == 0) dw[j] = dot;
+            if (lane == 0) st_na(dw + j, dot);
         }
     }
 }
@@ -226,17 +226,17 @@ __global__ void k_swiglu_grad(const uint4 *__restrict__ gu, const uint4 *__restr
         const int64_t r = v / vec_i;
         const int c = int(v - r * vec_i);
         float g[8], u[8], d[8], dg[8], du[8];
-        unpack8<BF16>(gu[r * 2 * vec_i + c], g);
-        unpack8<BF16>(gu[r * 2 * vec_i + vec_i + c], u);
-        unpack8<BF16>(dh[v], d);
+        unpack8<BF16>(ld_na(gu + r * 2 * vec_i + c), g);
+        unpack8<BF16>(ld_na(gu + r * 2 * vec_i + vec_i + c), u);
+        unpack8<BF16>(ld_na(dh + v), d);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float s = 1.f / (1.f + __expf(-g[i]));
             du[i] = d[i] * g[i] * s;
             dg[i] = d[i] * u[i] * s * (1.f + g[i] * (1.f - s));
         }
-        dgu[r * 2 * vec_i + c] = pack8<BF16>(dg);
-        dgu[r * 2 * vec_i + vec_i + c] = pack8<BF16>(du);
+        st_na(dgu + r * 2 * vec_i + c, pack8<BF16>(dg));
+        st_na(dgu + r * 2 * vec_i + vec_i + c, pack8<BF16>(du));
     }
 }
 

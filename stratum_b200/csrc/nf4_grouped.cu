@@ -95,7 +95,7 @@ k_build_tiles(const int *__restrict__ offsets, int E, int m_tiles, int cap, int6
     if (threadIdx.x == 0) base_s = 0;
     int bad = 0;
     for (int e = threadIdx.x; e < E; e += kTileThreads) {
-        const int a = offsets[e], b = offsets[e + 1];
+        const int a = ld_na(offsets + e), b = ld_na(offsets + e + 1);
         bad |= a < 0 || b < a || int64_t(b) > Ttot;
     }
     if (__syncthreads_or(bad)) {
@@ -109,8 +109,8 @@ k_build_tiles(const int *__restrict__ offsets, int E, int m_tiles, int cap, int6
         const int e = e0 + threadIdx.x;
         int a = 0, b = 0, cnt = 0, sz = cap;
         if (e < E) {
-            a = offsets[e];
-            b = offsets[e + 1];
+            a = ld_na(offsets + e);
+            b = ld_na(offsets + e + 1);
             if (b > a) {
                 const int n = b - a, parts = (n + cap - 1) / cap;
                 sz = ((n + parts - 1) / parts + 15) & ~15;  // <= cap (a multiple of 16)
@@ -139,7 +139,9 @@ k_build_tiles(const int *__restrict__ offsets, int E, int m_tiles, int cap, int6
         int n = start;
         for (int t0 = a; t0 < b; t0 += sz)
             for (int m = 0; m < m_tiles; ++m, ++n)
-                if (n < max_tiles) tiles[n] = Tile{e, m, t0, t0 + sz < b ? t0 + sz : b};
+                if (n < max_tiles)
+                    st_na(reinterpret_cast<uint4 *>(tiles + n),
+                          make_uint4(uint32_t(e), uint32_t(m), uint32_t(t0), uint32_t(t0 + sz < b ? t0 + sz : b)));
         __syncthreads();
         if (threadIdx.x == kTileThreads - 1) base_s = start + cnt;
         __syncthreads();
